@@ -1,0 +1,468 @@
+"""Benchmark of the MoE-FFN hot path on B200.
+
+Workload (default, --workload ep_decode): gpt-oss-120b-shaped MoE FFN stack,
+36 layers, 128 experts per layer with gate_up [5760 x 2880] and down
+[2880 x 2880] in MXFP4 (quantized on the device from N(0, 0.02)), top-4
+softmax routing over N(0, 1) logits (uniform expert popularity), a 64-token
+decode batch with bf16 activations. All experts are resident: with N GPUs
+each GPU holds 128/N experts of every layer and 64/N of the tokens, and the
+(token, expert) rows are dispatched to the experts' GPUs and the results
+combined back with NCCL all-to-all (expert parallelism; total work fixed, so
+scaling is strong). One step = the 36 layers for one batch:
+remap + grouping -> fused gate/up mul_mat_id + SwiGLU -> down mul_mat_id ->
+router-weighted combine (plus dispatch / combine exchanges when N > 1).
+
+The 60.9 GB of expert weights are far larger than L2 (126 MB), so no step
+finds its weights in cache.
+
+`value` is tokens/s with inputs resident in HBM; `e2e` is the same step
+through the public API with host buffers: the step's activations and routing
+copied from pinned host memory and every layer's output read back, inside
+the timed region. `--impl reference` times the CPU restatement of the same
+path (the oracle) on the host cores on a bounded sample of the workload.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE-FFN tokens/s + mul_mat_id HBM GB/s & FP4 TC util at 1/2/4/8 B200"
+
+SHAPE = dict(n_layer=36, n_expert=128, hidden=2880, n_ff=2880, top_k=4, tokens=64)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="msb", choices=["msb", "reference"])
+    ap.add_argument("--tokens", type=int, default=SHAPE["tokens"])
+    ap.add_argument("--layers", type=int, default=SHAPE["n_layer"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.f = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = sorted(float(r[1]) for r in rows)
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][2]),
+                "reasons": sorted(reasons), "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows)}
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif args.impl == "msb":
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# Workload
+# ---------------------------------------------------------------------------
+def make_routing(g, n_steps, n_layer, tokens, n_expert, top_k):
+    """Per (step, layer): top-k ids of N(0,1) logits and softmax weights over the
+    selected logits."""
+    import torch
+    logits = torch.randn(n_steps, n_layer, tokens, n_expert, generator=g, device="cuda")
+    sel, ids = torch.topk(logits, top_k, dim=-1)
+    w = torch.softmax(sel, dim=-1).float().contiguous()
+    return ids.to(torch.int32).contiguous(), w
+
+
+def build_layers(n_layer, e_lo, e_hi, K, n_ff, seed):
+    """Pools of this rank's experts [e_lo, e_hi) for every layer, quantized on
+    the device from N(0, 0.02). Slot j holds expert e_lo + j."""
+    import torch
+
+    from moestream_b200 import ops
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    n_loc = e_hi - e_lo
+    layers = []
+    for layer in range(n_layer):
+        gu = ops.SlotPool("mxfp4", K, 2 * n_ff, n_loc, max_fill_batch=8)
+        dn = ops.SlotPool("mxfp4", n_ff, K, n_loc, max_fill_batch=8)
+        for pool, rows, cols in ((gu, 2 * n_ff, K), (dn, K, n_ff)):
+            for j0 in range(0, n_loc, 8):
+                j1 = min(n_loc, j0 + 8)
+                wts = torch.randn((j1 - j0) * rows, cols, generator=g, device="cuda") * 0.02
+                q = ops.quantize_rows("mxfp4", wts).view(j1 - j0, -1)
+                pool.fill(list(range(j0, j1)), [q[i] for i in range(j1 - j0)])
+                del wts
+        layers.append((gu, dn))
+    torch.cuda.synchronize()
+    return layers
+
+
+class EPState:
+    """Buffers for one rank's expert-parallel layer."""
+
+    def __init__(self, world, rank, tokens, top_k, K, n_loc):
+        import torch
+        self.world, self.rank = world, rank
+        self.t_loc = tokens // world
+        self.pairs = self.t_loc * top_k
+        self.cap = self.pairs  # rows any single destination can receive from this rank
+        R = world * self.cap
+        self.send_x = torch.empty(R, K, dtype=torch.bfloat16, device="cuda")
+        self.recv_x = torch.empty_like(self.send_x)
+        self.send_e = torch.empty(R, 1, dtype=torch.int32, device="cuda")
+        self.recv_e = torch.empty_like(self.send_e)
+        self.y_loc = torch.empty(R, K, dtype=torch.float32, device="cuda")
+        self.y_back = torch.empty_like(self.y_loc)
+        self.pos = torch.empty(self.pairs, dtype=torch.int32, device="cuda")
+        self.ones = torch.ones(R, 1, dtype=torch.float32, device="cuda")
+        self.n_loc = n_loc
+
+
+def run_layer(ctx, layer, x, ids, w, y, timed_events=None):
+    """One MoE FFN layer on this rank. x: [t_loc, K] bf16, ids/w: [t_loc, top_k]."""
+    from moestream_b200 import ops
+    top_k = ids.shape[1]
+    gu, dn = ctx["layers"][layer]
+    lib = ops.lib()
+    if timed_events is not None:
+        lib.msb_time_next_gate_up(ops.c_vp(timed_events[0].cuda_event),
+                                  ops.c_vp(timed_events[1].cuda_event))
+    if ctx["world"] == 1:
+        r = ops.remap_group(ids, gu.n_slot, route=ctx["route"])
+        ops.moe_ffn(gu, gu, dn, x, r, w, top_k, up_row0=dn.K, ws=ctx["ws"], out=y)
+        return
+    import torch.distributed as dist
+    ep = ctx["ep"]
+    ops.ep_dispatch(ids, x, ep.n_loc, ep.world, ep.cap, ep.send_x, ep.send_e, ep.pos)
+    dist.all_to_all_single(ep.recv_x, ep.send_x)
+    dist.all_to_all_single(ep.recv_e, ep.send_e)
+    r = ops.remap_group(ep.recv_e, gu.n_slot, route=ctx["route"])
+    ops.moe_ffn(gu, gu, dn, ep.recv_x, r, ep.ones, 1, up_row0=dn.K, ws=ctx["ws"], out=ep.y_loc)
+    dist.all_to_all_single(ep.y_back, ep.y_loc)
+    ops.ep_combine(ep.y_back, ep.pos, w, y)
+
+
+def cpu_sample(layer0, tokens, top_k, K, n_ff, n_expert, ids0, w0, x0, threads):
+    """Times the oracle (CPU restatement, q8 arithmetic) on one layer of the
+    step; returns seconds per layer (best of 2)."""
+    import numpy as np
+
+    from oracle import oracle as O
+    gu, dn = layer0
+    gu_h = np.stack([gu.read_slot(s).cpu().numpy() for s in range(n_expert)] +
+                    [np.zeros(gu.expert_bytes, np.uint8)])
+    dn_h = np.stack([dn.read_slot(s).cpu().numpy() for s in range(n_expert)] +
+                    [np.zeros(dn.expert_bytes, np.uint8)])
+    best = None
+    for _ in range(2):
+        t0 = time.perf_counter()
+        O.moe_ffn("mxfp4", gu_h, gu_h, dn_h, K, n_ff, x0, ids0, w0, mode="q8", up_row0=n_ff,
+                  up_rows=2 * n_ff, nthreads=threads)
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    return best
+
+
+# ---------------------------------------------------------------------------
+# Reference arm: the CPU restatement on the host cores
+# ---------------------------------------------------------------------------
+def reference_arm(args, world, rank):
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    from oracle import oracle as O
+    K, n_ff, E, top_k = SHAPE["hidden"], SHAPE["n_ff"], SHAPE["n_expert"], SHAPE["top_k"]
+    T, L = args.tokens, args.layers
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    # One layer's weights per step sample: N(0, 0.02) experts quantized by the
+    # oracle's quantizer would take minutes on the host, so the sample uses
+    # MXFP4 blocks with uniform nibbles and scale exponents 118-120 (the range
+    # N(0, 0.02) weights quantize to). Timing does not depend on the values.
+    def slab(rows, cols):
+        nb = cols // 32
+        a = rng.integers(0, 256, size=(E + 1, rows * nb, 17), dtype=np.uint8)
+        a[:, :, 0] = rng.integers(118, 121, size=(E + 1, rows * nb), dtype=np.uint8)
+        a[E] = 0
+        return a.reshape(E + 1, -1)
+    gu, dn = slab(2 * n_ff, K), slab(K, n_ff)
+    times = []
+    for step in range(args.warmup + args.steps):
+        logits = rng.normal(0, 1, size=(T, E))
+        ids = np.argsort(-logits, axis=1)[:, :top_k].astype(np.int32)
+        sel = np.take_along_axis(logits, ids, 1)
+        w = np.exp(sel - sel.max(1, keepdims=True))
+        w = (w / w.sum(1, keepdims=True)).astype(np.float32)
+        x = rng.normal(0, 1, size=(T, K)).astype(np.float32)
+        t0 = time.perf_counter()
+        O.moe_ffn("mxfp4", gu, gu, dn, K, n_ff, x, ids, w, mode="q8", up_row0=n_ff,
+                  up_rows=2 * n_ff, nthreads=threads)
+        dt = time.perf_counter() - t0
+        if step >= args.warmup:
+            times.append(dt * L)  # one layer sampled, the step has L layers
+    step_s = sum(times) / len(times)
+    v = T / step_s
+    line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "mxfp4xq8->f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "gpt-oss-120b-shaped MoE FFN decode, all experts resident",
+                       "n_layer": L, "n_expert": E, "hidden": K, "n_ff": n_ff,
+                       "top_k": top_k, "tokens": T},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": f"1 of {L} layers per step ({T} tokens), scaled x{L}; "
+                                       "CPU restatement of ggml's q8_0 vec_dot (ggml is not "
+                                       "available offline)"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# Main arm
+# ---------------------------------------------------------------------------
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        rc = reference_arm(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return rc
+    import numpy as np
+    import torch
+
+    from moestream_b200 import ops
+    K, n_ff, E, top_k = SHAPE["hidden"], SHAPE["n_ff"], SHAPE["n_expert"], SHAPE["top_k"]
+    T, L = args.tokens, args.layers
+    assert T % world == 0 and E % world == 0
+    n_loc = E // world
+    t_loc = T // world
+    t_setup = time.time()
+    layers = build_layers(L, rank * n_loc, (rank + 1) * n_loc, K, n_ff, seed=1234 + rank)
+    S = args.warmup + args.steps
+    g = torch.Generator(device="cuda")
+    g.manual_seed(99)  # same routing on every rank; each takes its token slice
+    ids_all, w_all = make_routing(g, S, L, T, E, top_k)
+    xs = (torch.randn(S, T, K, generator=g, device="cuda")).to(torch.bfloat16)
+    ids_loc = ids_all[:, :, rank * t_loc:(rank + 1) * t_loc].contiguous()
+    w_loc = w_all[:, :, rank * t_loc:(rank + 1) * t_loc].contiguous()
+    x_loc = xs[:, rank * t_loc:(rank + 1) * t_loc].contiguous()
+    rows_max = T * top_k if world == 1 else world * t_loc * top_k
+    ctx = {"layers": layers, "world": world,
+           "route": ops.RouteBuffers(rows_max, n_loc),
+           "ws": ops.workspace(K, rows_max if world > 1 else T, 1 if world > 1 else top_k, n_loc),
+           "ep": EPState(world, rank, T, top_k, K, n_loc) if world > 1 else None}
+    y = torch.empty(L, t_loc, K, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    t_setup = time.time() - t_setup
+
+    def step(s, events=None):
+        for layer in range(L):
+            ev = events[layer] if events is not None else None
+            run_layer(ctx, layer, x_loc[s], ids_loc[s, layer], w_loc[s, layer], y[layer], ev)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    barrier(world)
+    # Dominant kernel timing: events around every fused gate/up launch.
+    gate_ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(L)] for _ in range(args.steps)]
+    clocks = Clocks(local)
+    clocks.start()
+    launches0 = int(ops.lib().msb_kernel_launches())
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0.record()
+    for i in range(args.steps):
+        step(args.warmup + i, gate_ev[i])
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    launches = int(ops.lib().msb_kernel_launches()) - launches0
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    ms = max_over_ranks(ms, world)
+    ms_step = ms / args.steps
+    value = T * args.steps / (ms / 1e3)
+
+    # Roofline of the fused gate/up mul_mat_id (this rank's launches).
+    ids_np = ids_all.cpu().numpy()
+    ebytes_gu = ops.expert_bytes("mxfp4", K, 2 * n_ff)
+    tot_bytes, tot_ms = 0.0, 0.0
+    for i in range(args.steps):
+        s = args.warmup + i
+        for layer in range(L):
+            e = np.unique(ids_np[s, layer].reshape(-1))
+            distinct = int(((e >= rank * n_loc) & (e < (rank + 1) * n_loc)).sum())
+            rows_in = T * top_k if world > 1 else T  # activation rows read (q8: 36 B / block)
+            act = rows_in * (K // 32) * 36 + T * top_k * (n_ff // 32) * 36
+            tot_bytes += distinct * ebytes_gu + act
+            tot_ms += gate_ev[i][layer][0].elapsed_time(gate_ev[i][layer][1])
+    gate_gbs = tot_bytes / (tot_ms / 1e3) / 1e9
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+
+    # End to end through the public API with host buffers.
+    e2e = None
+    if not args.no_e2e:
+        x_h = x_loc.cpu().pin_memory()
+        ids_h = ids_loc.cpu().pin_memory()
+        w_h = w_loc.cpu().pin_memory()
+        y_h = torch.empty(L, t_loc, K, dtype=torch.float32).pin_memory()
+        x_d = torch.empty_like(x_loc[0])
+        ids_d = torch.empty_like(ids_loc[0])
+        w_d = torch.empty_like(w_loc[0])
+        h2d = x_h[0].numel() * 2 + ids_h[0].numel() * 4 + w_h[0].numel() * 4
+        d2h = y_h.numel() * 4
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(args.steps):
+            s = args.warmup + i
+            x_d.copy_(x_h[s], non_blocking=True)
+            ids_d.copy_(ids_h[s], non_blocking=True)
+            w_d.copy_(w_h[s], non_blocking=True)
+            for layer in range(L):
+                run_layer(ctx, layer, x_d, ids_d[layer], w_d[layer], y[layer])
+            y_h.copy_(y, non_blocking=True)
+            torch.cuda.current_stream().synchronize()  # the step's result is on the host
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+        e2e = {"value": T * args.steps / (e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        s = args.warmup
+        ids0 = ids_np[s, 0]
+        w0 = w_all[s, 0].cpu().numpy()
+        x0 = xs[s].float().cpu().numpy()
+        t_layer = cpu_sample(layers[0], T, top_k, K, n_ff, E, ids0, w0, x0, threads)
+        cpu = {"value": T / (t_layer * L), "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"layer 0 of step {s} ({T} tokens), best of 2, scaled x{L} layers; CPU "
+                         "restatement of ggml's q8_0 vec_dot (ggml is not available offline)"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "mxfp4xq8->f32", "data": "synthetic",
+                "config": {"workload": "gpt-oss-120b-shaped MoE FFN decode, all experts resident"
+                                       + (", expert-parallel" if world > 1 else ""),
+                           "n_layer": L, "n_expert": E, "hidden": K, "n_ff": n_ff,
+                           "top_k": top_k, "tokens": T, "experts_per_gpu": n_loc,
+                           "weights": "MXFP4 from N(0,0.02), quantized on device",
+                           "routing": "top-4 softmax over N(0,1) logits",
+                           "activations": "bf16 N(0,1)",
+                           "l2": "inputs larger than L2 (60.9 GB of expert weights)",
+                           "parallelism": f"ep{world}"},
+                "roofline": {"bound": "hbm", "achieved": gate_gbs, "peak": hbm, "unit": "GB/s",
+                             "frac": gate_gbs / hbm, "traffic": None,
+                             "kernel": "gemv_kernel<MXFP4, SwiGLU> (fused gate/up mul_mat_id)",
+                             "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
+                "setup_s": round(t_setup, 1)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        barrier(world)
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

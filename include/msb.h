@@ -1,0 +1,352 @@
+/*
+ * msb.h -- C ABI of the B200-native expert-indexed matmul over a GPU slot pool.
+ *
+ * This library replaces the hot path of MoEStream (monowalker/moestream):
+ *   router expert ids -> ExpertCache remap to slot ids -> per-slot grouping
+ *   -> ggml's GGML_OP_MUL_MAT_ID over a slab of quantized expert weights
+ *   -> SwiGLU -> down projection -> router-weighted combine,
+ * plus the slot fills that bring missing experts into the slab.
+ *
+ * Conventions (all entry points):
+ *   - plain C types, opaque handles, `int` status return (MSB_OK == 0);
+ *     msb_last_error() returns a thread-local message for the last failure;
+ *   - no C++ exceptions cross this boundary;
+ *   - every device pointer argument is memory on the device the handle lives on;
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy default
+ *     stream. Kernels are stream-ordered; nothing here synchronizes the host
+ *     unless the comment says so.
+ *
+ * Tensor layout vocabulary follows ggml: ne[0] is the fastest dimension.
+ *   as  : expert weights [K (in), N (out), n_slot + 1]; slot n_slot is the
+ *         zero slot (every weight 0, so any row routed there yields exactly 0);
+ *   b   : activations [K, b_ne1, n_tok], b_ne1 is 1 (one vector per token,
+ *         shared by its top_k rows) or top_k (one vector per (token, k));
+ *   ids : int32 [top_k, n_tok], read with byte strides nb0 / nb1;
+ *   res : float32 [N, top_k, n_tok], contiguous.
+ */
+#ifndef MSB_H
+#define MSB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define MSB_OK               0
+#define MSB_ERR_INVALID      1   /* bad argument (shape, pointer, type)        */
+#define MSB_ERR_CUDA         2   /* a CUDA runtime call failed                 */
+#define MSB_ERR_NOMEM        3   /* device or pinned host allocation failed    */
+#define MSB_ERR_UNSUPPORTED  4   /* valid request this build does not handle   */
+#define MSB_ERR_TIMEOUT      5   /* a bounded device wait gave up              */
+
+/* ---- element types (values are ggml's enum ggml_type) ------------------ */
+#define MSB_TYPE_F32     0
+#define MSB_TYPE_F16     1
+#define MSB_TYPE_IQ4_NL 20   /* 32 elements: fp16 d + 16 B nibbles (18 B)    */
+#define MSB_TYPE_BF16   30
+#define MSB_TYPE_MXFP4  39   /* 32 elements: e8m0 e + 16 B nibbles (17 B)    */
+
+/* ---- expert roles of one MoE layer (reference: role 0 gate, 1 up, 2 down;
+ *      src/llama-moestream.cpp:434-445 parse_name) ------------------------- */
+#define MSB_ROLE_GATE 0
+#define MSB_ROLE_UP   1
+#define MSB_ROLE_DOWN 2
+
+/* Null expert / unassigned slot marker (reference ExpertCache NO_SLOT,
+ * src/expert_cache.hpp:109). */
+#define MSB_NO_SLOT 0xFFFFFFFFu
+
+/* ======================================================================== */
+/* Library                                                                   */
+/* ======================================================================== */
+
+/* Version as 10000*major + 100*minor + patch. */
+int msb_version(void);
+
+/* Message for the last failure on the calling thread ("" if none). */
+const char *msb_last_error(void);
+
+/* Bytes of one expert in ggml's block layout (N rows of K elements), or -1
+ * when K is not a multiple of 32 or the type is not a block type.
+ * Replaces the per-(layer, role) `expert_bytes` the reference records in
+ * register_slab (src/llama-moestream.cpp:1211-1225, SlabInfo :68-75). */
+int64_t msb_expert_bytes(int wtype, int64_t K, int64_t N);
+
+/* Slot count for a slab the way the reference sizes it:
+ *   s = round(frac * n_expert), raised so that one micro-batch's expected
+ *   union of experts fits with a 1.15 margin plus top_k, clamped to
+ *   [8, n_expert]. The allocation is s + 1 (the zero slot).
+ * Replaces moestream::slab_slots (src/llama-moestream.cpp:1017-1086) for the
+ * plain-fraction mode; returns s (not s + 1), or 0 when n_expert <= 1. */
+uint32_t msb_slab_slots(int64_t n_expert, double frac, int top_k, int max_ubatch);
+
+/* Largest token count the slot pool can serve without exhausting it:
+ * max n with n_expert*(1-(1-top_k/n_expert)^(n+1))*1.15 + top_k <= n_slot.
+ * Batches above it take the full-arena path. Replaces the threshold in
+ * finalize (src/llama-moestream.cpp:1530-1543). */
+int msb_arena_threshold(int64_t n_expert, int top_k, uint32_t n_slot);
+
+/* ======================================================================== */
+/* Slot pool (device slab)                                                    */
+/* ======================================================================== */
+
+typedef struct msb_pool_s *msb_pool_t;
+
+typedef struct {
+  int      wtype;          /* MSB_TYPE_IQ4_NL or MSB_TYPE_MXFP4              */
+  int64_t  K;              /* input features (row length), multiple of 32    */
+  int64_t  N;              /* output features (rows)                         */
+  int32_t  n_slot;         /* usable slots; slot n_slot is the zero slot     */
+  int32_t  device;         /* CUDA device ordinal                            */
+  int64_t  expert_bytes;   /* ggml bytes of one expert                       */
+  int64_t  slot_stride;    /* device bytes between consecutive slots         */
+  void    *data;           /* device base of slot 0                          */
+} msb_pool_info_t;
+
+/* Allocate a device slab of n_slot + 1 slots for experts of shape [K, N] and
+ * zero-fill the zero slot. `max_fill_batch` experts can be staged per fill
+ * call (0 picks 4). Replaces the slab allocation the patched loader makes
+ * from slab_slots (src/apply.py:47-83) and ensure_zero_slot
+ * (src/llama-moestream.cpp:1749-1792). Synchronous. */
+int msb_pool_create(int wtype, int64_t K, int64_t N, int32_t n_slot,
+                    int32_t max_fill_batch, msb_pool_t *out);
+int msb_pool_destroy(msb_pool_t pool);
+int msb_pool_get_info(msb_pool_t pool, msb_pool_info_t *out);
+
+/* Copy n experts given in ggml block layout (host memory; pinned memory makes
+ * the copies asynchronous) into `slots` of the pool, stream-ordered on
+ * `stream`, converting them to the pool's device layout on the way.
+ * Each src[i] points at expert_bytes bytes. Slot indices must be < n_slot.
+ * Replaces the read loop of ms_remap_fn (src/llama-moestream.cpp:1954-2028):
+ * do_read / run_reads_parallel (:1230-1263) plus ggml_backend_tensor_set. */
+int msb_fill_slots_async(msb_pool_t pool, int32_t n, const int32_t *slots,
+                         const void *const *src_host, void *stream);
+
+/* Same, with the ggml-layout source already in device memory (no staging). */
+int msb_fill_slots_from_device_async(msb_pool_t pool, int32_t n,
+                                     const int32_t *slots,
+                                     const void *const *src_dev, void *stream);
+
+/* Copy slot `slot` back out in ggml block layout into device memory `dst`
+ * (expert_bytes bytes). Used to check fills. */
+int msb_read_slot_async(msb_pool_t pool, int32_t slot, void *dst_dev,
+                        void *stream);
+
+/* ======================================================================== */
+/* Routing: remap + per-slot grouping (device)                               */
+/* ======================================================================== */
+
+/* Grouped routing of one mul_mat_id call, all device arrays, caller-owned.
+ * n_pairs = n_tok * top_k; pair index i = t * top_k + k.               */
+typedef struct {
+  int32_t *slot_ids;  /* [n_pairs]     slot of pair i                     */
+  int32_t *counts;    /* [n_slot + 1]  pairs per slot                     */
+  int32_t *offsets;   /* [n_slot + 2]  exclusive scan of counts           */
+  int32_t *rows;      /* [n_pairs]     pair indices grouped by slot, each
+                                       group in increasing pair order     */
+  int32_t *active;    /* [n_slot + 2]  active[0] = #slots with pairs,
+                                       active[1..] = those slots ascending */
+} msb_route_t;
+
+/* Remap router ids to slot ids and group the (token, k) pairs per slot.
+ *   ids_dev   : int32 expert ids, element (k, t) at byte k*nb0 + t*nb1
+ *               (the reference reads ids with strides, :1900-1952, :2481);
+ *   table_dev : int32 [n_expert] expert -> slot (negative or >= n_slot means
+ *               not resident). NULL means ids already hold slot ids.
+ *   Out-of-range ids and non-resident experts map to the zero slot n_slot,
+ *   as the reference does for exhaustion and invalid ids (:1904-1928).
+ * Bit-exact and deterministic. Replaces the ms_remap_fn output loop
+ * (src/llama-moestream.cpp:1900-1952) and ggml's internal row grouping. */
+int msb_remap_group(const int32_t *ids_dev, int64_t nb0, int64_t nb1,
+                    int32_t top_k, int32_t n_tok,
+                    const int32_t *table_dev, int32_t n_expert, int32_t n_slot,
+                    const msb_route_t *route, void *stream);
+
+/* ======================================================================== */
+/* mul_mat_id                                                                 */
+/* ======================================================================== */
+
+/* Workspace bytes for msb_mul_mat_id / msb_moe_ffn with these shapes. */
+int64_t msb_workspace_bytes(int64_t K_max, int32_t n_tok, int32_t top_k,
+                            int32_t n_slot);
+
+/* res[n, k, t] = sum_i dequant(as[:, n, slot(k,t)])[i] * b[i, k % b_ne1, t]
+ * for a grouped route. b is f32 or bf16 with element (i, j, t) at
+ * b + t*b_nb2 + j*b_nb1 + i*elem (byte strides). res is f32, contiguous.
+ * The activations are quantized per 32-element block to int8 with an fp16
+ * scale (ggml's q8_0 vec_dot form); products accumulate in int32 per block
+ * and in f32 across blocks. Operator contract: ggml_mul_mat_id(ctx, as, b,
+ * ids), call sites research/spikes/s0_slot_slab/main.c:148,
+ * research/spikes/s6_arena_mulmatid/main.c:134. */
+int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type,
+                   int64_t b_ne1, int64_t b_nb1, int64_t b_nb2,
+                   const msb_route_t *route, int32_t top_k, int32_t n_tok,
+                   float *res_dev, void *workspace, int64_t workspace_bytes,
+                   void *stream);
+
+/* ======================================================================== */
+/* MoE FFN layer                                                              */
+/* ======================================================================== */
+
+/* One MoE FFN layer over grouped routing:
+ *   g = mul_mat_id(gate, x), u = mul_mat_id(up, x), a = silu(g) * u,
+ *   r = mul_mat_id(down, a), y[:, t] = sum_k w[k, t] * r[:, k, t].
+ * gate and up may be the same pool with up_row0 = N_ff (a fused gate_up
+ * tensor whose first N_ff rows are the gate); otherwise up_row0 = 0.
+ * x: f32 or bf16 [K, 1, n_tok] (byte stride x_nb1 between tokens);
+ * w: f32 [top_k, n_tok] router weights (contiguous); y: f32 [K, n_tok].
+ * act_dev (optional, may be NULL): f32 [N_ff, top_k, n_tok] receives a.
+ * Composition restated from research/spikes/s1_real_expert_stream/main.c:
+ * 186-209 and research/spikes/s4_sweep_math/main.c:89-92. */
+int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0,
+                msb_pool_t down, const void *x_dev, int x_type, int64_t x_nb1,
+                const msb_route_t *route, const float *w_dev, int32_t top_k,
+                int32_t n_tok, float *y_dev, float *act_dev, void *workspace,
+                int64_t workspace_bytes, void *stream);
+
+/* ======================================================================== */
+/* Expert parallelism (packing around the all-to-all exchanges)               */
+/* ======================================================================== */
+
+/* The reference is single-process and single-GPU; these have no counterpart
+ * there. Experts are split evenly over n_rank GPUs (expert e lives on rank
+ * e / n_local as local slot e % n_local).
+ *
+ * Packs this rank's (token, k) rows for an equal-split all-to-all: row of
+ * pair p = t*top_k + k goes to block dest = ids[p] / n_local of send_x
+ * (bf16 [n_rank * cap, K]) at dest*cap + (its rank among earlier pairs with
+ * that destination); send_e (int32 [n_rank * cap]) gets the local expert id,
+ * -1 for unused rows; pos (int32 [n_tok * top_k]) records each pair's row,
+ * -1 for invalid ids or rows beyond cap. x is f32 or bf16 [n_tok, K] with
+ * byte stride x_nb1 between tokens. */
+int msb_ep_dispatch(const int32_t *ids_dev, const void *x_dev, int x_type,
+                    int64_t x_nb1, int32_t top_k, int32_t n_tok, int64_t K,
+                    int32_t n_local, int32_t n_rank, int32_t cap,
+                    void *send_x_dev, int32_t *send_e_dev, int32_t *pos_dev,
+                    void *stream);
+
+/* y[t, :] = sum_k w[t, k] * back[pos[t*top_k + k], :] (k ascending), where
+ * back (f32 [n_rank * cap, K]) holds the expert outputs returned by the
+ * reverse all-to-all. */
+int msb_ep_combine(const float *back_dev, const int32_t *pos_dev,
+                   const float *w_dev, int32_t top_k, int32_t n_tok, int64_t K,
+                   float *y_dev, void *stream);
+
+/* ======================================================================== */
+/* Measurement hooks                                                          */
+/* ======================================================================== */
+
+/* Kernels this library has launched in this process (all threads). */
+uint64_t msb_kernel_launches(void);
+
+/* Arms a one-shot timing of the next fused gate/up matmul that msb_moe_ffn
+ * launches on the calling thread: `start` (a cudaEvent_t) is recorded on the
+ * launch stream just before that kernel and `stop` just after it. */
+void msb_time_next_gate_up(void *start, void *stop);
+
+/* ======================================================================== */
+/* Device quantizers (ggml block layout out)                                  */
+/* ======================================================================== */
+
+/* Quantize n_rows rows of K f32 values (row stride K) to ggml blocks.
+ * MXFP4 follows ggml/gguf's quantizer (e = floor(log2(amax)) - 2 + 127,
+ * nearest doubled-e2m1 value, first index on ties); IQ4_NL uses this
+ * library's deterministic scale search (see oracle). */
+int msb_quantize_rows(int wtype, const float *src_dev, int64_t n_rows,
+                      int64_t K, void *dst_dev, void *stream);
+
+/* ======================================================================== */
+/* Host expert cache (S3-FIFO) -- the reference's ExpertCache                 */
+/* ======================================================================== */
+
+typedef struct msb_cache_s *msb_cache_t;
+
+/* Field-for-field the reference ExpertCache::Config
+ * (src/expert_cache.hpp:63-75). */
+typedef struct {
+  uint32_t n_layer;
+  uint32_t n_expert;
+  uint32_t n_slot;        /* 0 derives it from cache_frac                  */
+  double   cache_frac;
+  double   pin_ratio;
+  double   small_ratio;
+  uint32_t ghost_mult;
+  int32_t  layer_quota_adapt;
+  uint32_t quota_period;
+  double   quota_eta;
+  uint32_t quota_min;
+} msb_cache_config_t;
+
+/* Reference CacheStats (src/expert_cache.hpp:38-55), in declaration order. */
+typedef struct {
+  uint64_t hit, miss, hit_pinned, hit_small, hit_main, ghost_hit, admit,
+      evict, bypass, promote, bytes_fetched;
+} msb_cache_stats_t;
+
+/* Origins (reference enum class Origin, src/expert_cache.hpp:29-34). */
+#define MSB_ORIGIN_DEMAND        0
+#define MSB_ORIGIN_PREFETCH_HIGH 1
+#define MSB_ORIGIN_PREFETCH_LOW  2
+#define MSB_ORIGIN_SWEEP         3
+
+/* Fill `cfg` with the reference defaults (src/expert_cache.hpp:63-75). */
+void msb_cache_config_default(msb_cache_config_t *cfg);
+int  msb_cache_create(const msb_cache_config_t *cfg, msb_cache_t *out);
+void msb_cache_destroy(msb_cache_t c);
+/* ExpertCache::acquire (src/expert_cache.cpp:62-153): returns 1 on a hit,
+ * 0 on a miss; *slot gets the slot or MSB_NO_SLOT. */
+int  msb_cache_acquire(msb_cache_t c, uint32_t layer, uint32_t expert,
+                       int origin, uint32_t *slot);
+/* ExpertCache::mark_resident / release / end_step
+ * (src/expert_cache.cpp:155-167, :228-231). */
+void msb_cache_mark_resident(msb_cache_t c, uint32_t layer, uint32_t expert,
+                             uint64_t nbytes);
+void msb_cache_release(msb_cache_t c, uint32_t layer, uint32_t expert);
+void msb_cache_end_step(msb_cache_t c);
+/* ExpertCache::build_pinned (src/expert_cache.cpp:32-60); freq has
+ * n_layer * n_expert entries. Ties in frequency pin the lower expert id. */
+void msb_cache_build_pinned(msb_cache_t c, const uint32_t *freq, size_t n);
+void msb_cache_get_stats(msb_cache_t c, msb_cache_stats_t *out);
+uint32_t msb_cache_n_slot(msb_cache_t c);
+uint32_t msb_cache_slot_of(msb_cache_t c, uint32_t layer, uint32_t expert);
+/* Per-layer quotas (reference layer_quota()), n_layer entries. */
+void msb_cache_layer_quota(msb_cache_t c, uint32_t *out);
+
+/* ======================================================================== */
+/* Slot streamer: ms_remap_fn's host half                                    */
+/* ======================================================================== */
+
+typedef struct msb_streamer_s *msb_streamer_t;
+
+/* One ExpertCache per layer with n_layer = 1, pin_ratio 0 and quota
+ * adaptation off, exactly as finalize builds them
+ * (src/llama-moestream.cpp:1438-1447). Zero slot = n_slot. */
+int  msb_streamer_create(uint32_t n_layer, uint32_t n_expert, uint32_t n_slot,
+                         uint64_t expert_bytes_total, msb_streamer_t *out);
+void msb_streamer_destroy(msb_streamer_t s);
+
+/* The decode remap of one layer (ms_remap_fn, src/llama-moestream.cpp:
+ * 1799-2105, core loop :1900-1952): releases the references this layer took
+ * on its previous call (:1839-1852), then for each (t, k) in order acquires
+ * the expert (Origin::Demand), writes its slot to out_slots[t*top_k + k]
+ * (zero slot on exhaustion or out-of-range id), and appends each miss as
+ * (expert, slot) in first-seen order. Host memory throughout.
+ * miss_experts / miss_slots must hold n_tok*top_k entries.
+ * table_out (optional, n_expert entries) receives expert -> slot after the
+ * call, -1 for experts without a slot. */
+int msb_streamer_remap(msb_streamer_t s, uint32_t layer, const int32_t *ids,
+                       int64_t nb0, int64_t nb1, int32_t top_k, int32_t n_tok,
+                       int32_t *out_slots, int32_t *n_miss,
+                       int32_t *miss_experts, int32_t *miss_slots,
+                       int32_t *table_out);
+/* Summed stats over the layers plus the exhaustion count. */
+int msb_streamer_stats(msb_streamer_t s, msb_cache_stats_t *out,
+                       uint64_t *n_exhausted);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MSB_H */

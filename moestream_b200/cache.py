@@ -1,0 +1,115 @@
+"""Host expert cache and slot streamer over the C ABI.
+
+ExpertCache mirrors the reference class moestream::ExpertCache
+(src/expert_cache.hpp:61-147): same constructor config, same acquire /
+mark_resident / release / end_step / build_pinned methods and the same
+decisions. SlotStreamer is the host half of the reference's ms_remap_fn
+(src/llama-moestream.cpp:1799-2105): per-layer caches, reference release on
+the next call, misses in first-seen order, zero slot on exhaustion.
+"""
+import ctypes
+
+import numpy as np
+
+from ._lib import (CacheConfig, CacheStats, NO_SLOT, ORIGIN_DEMAND, c_i32p, c_u32p, c_vp,
+                   check, lib)
+
+
+class ExpertCache:
+    def __init__(self, n_layer=40, n_expert=256, n_slot=0, **kw):
+        cfg = CacheConfig()
+        lib().msb_cache_config_default(ctypes.byref(cfg))
+        cfg.n_layer, cfg.n_expert, cfg.n_slot = n_layer, n_expert, n_slot
+        for k, v in kw.items():
+            setattr(cfg, k, int(v) if k == "layer_quota_adapt" else v)
+        h = c_vp()
+        check(lib().msb_cache_create(ctypes.byref(cfg), ctypes.byref(h)))
+        self.h = h
+        self.n_layer = n_layer
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().msb_cache_destroy(self.h)
+            self.h = None
+
+    def acquire(self, layer, expert, origin=ORIGIN_DEMAND):
+        """Returns (hit, slot); slot is NO_SLOT when none was reserved."""
+        s = ctypes.c_uint32(0)
+        hit = lib().msb_cache_acquire(self.h, layer, expert, origin, ctypes.byref(s))
+        return bool(hit), int(s.value)
+
+    def mark_resident(self, layer, expert, nbytes):
+        lib().msb_cache_mark_resident(self.h, layer, expert, nbytes)
+
+    def release(self, layer, expert):
+        lib().msb_cache_release(self.h, layer, expert)
+
+    def end_step(self):
+        lib().msb_cache_end_step(self.h)
+
+    def build_pinned(self, freq):
+        a = np.ascontiguousarray(freq, dtype=np.uint32)
+        lib().msb_cache_build_pinned(self.h, a.ctypes.data_as(c_u32p), a.size)
+
+    def stats(self):
+        st = CacheStats()
+        lib().msb_cache_get_stats(self.h, ctypes.byref(st))
+        return st.as_dict()
+
+    @property
+    def n_slot(self):
+        return int(lib().msb_cache_n_slot(self.h))
+
+    def slot_of(self, layer, expert):
+        return int(lib().msb_cache_slot_of(self.h, layer, expert))
+
+    def layer_quota(self):
+        out = np.zeros(self.n_layer, dtype=np.uint32)
+        lib().msb_cache_layer_quota(self.h, out.ctypes.data_as(c_u32p))
+        return out
+
+
+class SlotStreamer:
+    def __init__(self, n_layer, n_expert, n_slot, expert_bytes_total=0):
+        h = c_vp()
+        check(lib().msb_streamer_create(n_layer, n_expert, n_slot, expert_bytes_total,
+                                        ctypes.byref(h)))
+        self.h = h
+        self.n_expert, self.n_slot = n_expert, n_slot
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().msb_streamer_destroy(self.h)
+            self.h = None
+
+    def remap(self, layer, ids, want_table=False):
+        """ids: int32 array [n_tok, top_k] (any strides). Returns
+        (slots [n_tok, top_k], misses [(expert, slot)], table or None)."""
+        ids = np.asarray(ids)
+        assert ids.dtype == np.int32 and ids.ndim == 2
+        n_tok, top_k = ids.shape
+        nb0, nb1 = ids.strides[1], ids.strides[0]
+        out = np.empty((n_tok, top_k), dtype=np.int32)
+        me = np.empty(max(n_tok * top_k, 1), dtype=np.int32)
+        ms = np.empty_like(me)
+        nm = ctypes.c_int32(0)
+        table = np.empty(self.n_expert, dtype=np.int32) if want_table else None
+        base = ids.__array_interface__["data"][0]
+        check(lib().msb_streamer_remap(
+            self.h, layer, ctypes.cast(base, c_i32p), nb0, nb1, top_k, n_tok,
+            out.ctypes.data_as(c_i32p), ctypes.byref(nm), me.ctypes.data_as(c_i32p),
+            ms.ctypes.data_as(c_i32p),
+            table.ctypes.data_as(c_i32p) if table is not None else None))
+        misses = list(zip(me[:nm.value].tolist(), ms[:nm.value].tolist()))
+        return out, misses, table
+
+    def stats(self):
+        st = CacheStats()
+        ex = ctypes.c_uint64(0)
+        check(lib().msb_streamer_stats(self.h, ctypes.byref(st), ctypes.byref(ex)))
+        d = st.as_dict()
+        d["exhausted"] = int(ex.value)
+        return d
+
+
+__all__ = ["ExpertCache", "SlotStreamer", "NO_SLOT"]

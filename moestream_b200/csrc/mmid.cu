@@ -1,0 +1,490 @@
+// mul_mat_id over the slot pool, the fused SwiGLU variant, the router-weighted
+// combine, and the MoE FFN layer built from them.
+//
+// Operator contract (ggml_mul_mat_id; call sites research/spikes/
+// s0_slot_slab/main.c:117-148, s6_arena_mulmatid/main.c:82-134):
+//   res[n, k, t] = sum_i dequant(as[:, n, slot(k, t)])[i] * b[i, k % b_ne1, t]
+//
+// Arithmetic (the form of ggml's CPU vec_dot for IQ4_NL and MXFP4 with q8_0
+// activations): each 32-element activation block is quantized to int8 with
+// d = amax / 127 (codes from the unrounded d, d stored as fp16); per weight
+// block the int8 codes are dotted in int32 (dp4a), scaled by
+// d_weight * d_act and accumulated in f32.
+//
+// Kernel shape (decode GEMV): one CTA per (active slot, 32-row tile); lane =
+// output row, the 8 warps split the K blocks. Weights stream from HBM as
+// coalesced 128-bit loads of the block-major pool layout; the activations of
+// the slot's pairs sit in shared memory and are read as warp-wide broadcasts.
+// Pairs beyond kMaxPairs per slot are processed in further passes over the
+// same weights.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include "msb_internal.h"
+#include "pool.cuh"
+#include "quant.cuh"
+
+namespace msb {
+
+static constexpr int kThreads = 256;
+static constexpr int kWarps = kThreads / 32;
+static constexpr int kMaxPairs = 8;  // activation rows held per pass
+static constexpr int kPrefetch = 4;  // weight blocks in flight per lane and view
+
+// Activations quantized per block, interleaved order (quant.cuh):
+// codes at q + (row*nb + b)*32, scale at d[row*nb + b].
+struct ActQ8 {
+  int8_t *q;
+  float *d;
+  int64_t nb;
+};
+
+__device__ __forceinline__ float round_half_away(float x) { return roundf(x); }
+
+// ---------------------------------------------------------------------------
+// Activation quantization: one warp per (row, block); lane j owns element j.
+// Row r = t * ne1 + j1 covers b[:, j1, t].
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float load_act(const char *p) {
+  if constexpr (sizeof(T) == 4) return *reinterpret_cast<const float *>(p);
+  else return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(p));
+}
+
+__device__ __forceinline__ void store_q8_block(ActQ8 out, int64_t row, int64_t b, float v,
+                                               int lane) {
+  float amax = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float d = amax / 127.f;
+  const float id = d != 0.f ? 1.f / d : 0.f;
+  const int q = int(round_half_away(__fmul_rn(v, id)));
+  out.q[(row * out.nb + b) * 32 + interleaved_pos(lane)] = int8_t(q);
+  if (lane == 0) out.d[row * out.nb + b] = __half2float(__float2half_rn(d));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) quantize_act_kernel(
+    const char *b, int64_t nb1, int64_t nb2, int64_t ne1, int64_t n_rows, ActQ8 out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t item = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  if (item >= n_rows * out.nb) return;
+  const int64_t row = item / out.nb, blk = item % out.nb;
+  const int64_t t = row / ne1, j1 = row % ne1;
+  const char *p = b + t * nb2 + j1 * nb1 + (blk * 32 + lane) * int64_t(sizeof(T));
+  store_q8_block(out, row, blk, load_act<T>(p), lane);
+}
+
+// ---------------------------------------------------------------------------
+// Grouped GEMV
+// ---------------------------------------------------------------------------
+struct GemvArgs {
+  PoolView w;        // weights (the gate when SWIGLU)
+  PoolView w2;       // up weights (SWIGLU only)
+  int64_t n_out;     // output rows per view
+  int tiles;         // ceil(n_out / 32)
+  const int32_t *counts, *offsets, *rows, *active;
+  int32_t zero_slot;
+  int32_t top_k, b_ne1;
+  ActQ8 in;          // activations, nb = w.nb
+  float *res;        // plain: res[pair * n_out + n]
+  ActQ8 out;         // SWIGLU: quantized silu(g) * u, nb = n_out / 32
+  float *act;        // SWIGLU, optional: f32 silu(g) * u [pair * n_out + n]
+};
+
+template <int WT>
+__device__ __forceinline__ Codebook codebook() {
+  if constexpr (WT == MSB_TYPE_MXFP4) return codebook_mxfp4();
+  else return codebook_iq4nl();
+}
+
+// Dot of one weight block (8 code words) with one activation block.
+__device__ __forceinline__ int dot_block(const uint32_t (&wq)[8], const int4 *a) {
+  const int4 a0 = a[0], a1 = a[1];
+  int s = __dp4a(int(wq[0]), a0.x, 0);
+  s = __dp4a(int(wq[1]), a0.y, s);
+  s = __dp4a(int(wq[2]), a0.z, s);
+  s = __dp4a(int(wq[3]), a0.w, s);
+  s = __dp4a(int(wq[4]), a1.x, s);
+  s = __dp4a(int(wq[5]), a1.y, s);
+  s = __dp4a(int(wq[6]), a1.z, s);
+  s = __dp4a(int(wq[7]), a1.w, s);
+  return s;
+}
+
+// Raw weight block of one lane: 16 bytes of nibbles and the scale bits.
+struct RawBlock {
+  uint4 q;
+  uint32_t s;
+};
+
+template <int WT>
+__device__ __forceinline__ RawBlock load_block(const PoolView &v, int slot, int64_t b, int64_t n,
+                                               bool valid) {
+  RawBlock r{make_uint4(0, 0, 0, 0), 0u};
+  if (valid) {
+    const uint8_t *sb = v.base + int64_t(slot) * v.slot_stride;
+    const int64_t off = b * v.N + v.row0 + n;
+    r.q = __ldg(reinterpret_cast<const uint4 *>(sb + off * 16));
+    if constexpr (WT == MSB_TYPE_MXFP4) r.s = __ldg(sb + v.nb * v.N * 16 + off);
+    else r.s = __ldg(reinterpret_cast<const unsigned short *>(sb + v.nb * v.N * 16) + off);
+  }
+  return r;
+}
+
+template <int WT>
+__device__ __forceinline__ float scale_of(uint32_t s) {
+  if constexpr (WT == MSB_TYPE_MXFP4) return e8m0_half(s);
+  else return __half2float(__ushort_as_half((unsigned short)s));
+}
+
+__device__ __forceinline__ void decode_block(const uint4 &q, const Codebook &cb,
+                                             uint32_t (&wq)[8]) {
+  decode_nibbles(q.x, cb, wq[0], wq[1]);
+  decode_nibbles(q.y, cb, wq[2], wq[3]);
+  decode_nibbles(q.z, cb, wq[4], wq[5]);
+  decode_nibbles(q.w, cb, wq[6], wq[7]);
+}
+
+template <int WT, bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
+  constexpr int NV = SWIGLU ? 2 : 1;  // weight views per lane
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int nb = int(a.w.nb);
+  int8_t *s_q = reinterpret_cast<int8_t *>(smem);                           // [kMaxPairs][nb][32]
+  float *s_d = reinterpret_cast<float *>(smem + size_t(kMaxPairs) * nb * 32);  // [kMaxPairs][nb]
+  float *s_red = s_d + size_t(kMaxPairs) * nb;                              // [kWarps][NV][kMaxPairs][32]
+
+  const int ai = blockIdx.x / a.tiles;
+  const int tile = blockIdx.x - ai * a.tiles;
+  if (ai >= a.active[0]) return;
+  const int slot = a.active[1 + ai];
+  const int c_total = a.counts[slot];
+  const int32_t *prs = a.rows + a.offsets[slot];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t n0 = int64_t(tile) * 32;
+  const int64_t n = n0 + lane;
+  const bool valid = n < a.n_out;
+
+  if (slot == a.zero_slot) {
+    // Every weight of the zero slot is 0: write the exact result directly.
+    for (int r = warp; r < c_total; r += kWarps) {
+      const int64_t pair = prs[r];
+      if constexpr (SWIGLU) {
+        a.out.q[(pair * a.out.nb + tile) * 32 + lane] = 0;
+        if (lane == 0) a.out.d[pair * a.out.nb + tile] = 0.f;
+        if (a.act && valid) a.act[pair * a.n_out + n] = 0.f;
+      } else if (valid) {
+        a.res[pair * a.n_out + n] = 0.f;
+      }
+    }
+    return;
+  }
+
+  const Codebook cb = codebook<WT>();
+  for (int c0 = 0; c0 < c_total; c0 += kMaxPairs) {
+    const int cc = min(kMaxPairs, c_total - c0);
+    __syncthreads();  // shared buffers of the previous pass are consumed
+    // Stage the activation blocks of this pass's pairs.
+    const int units = cc * nb * 2;  // 16-byte units
+    for (int u = threadIdx.x; u < units; u += kThreads) {
+      const int r = u / (nb * 2), rem = u - r * nb * 2;
+      const int64_t pair = prs[c0 + r];
+      const int64_t t = pair / a.top_k, k = pair - t * a.top_k;
+      const int64_t arow = t * a.b_ne1 + (k % a.b_ne1);
+      reinterpret_cast<int4 *>(s_q)[int64_t(r) * nb * 2 + rem] =
+          reinterpret_cast<const int4 *>(a.in.q + arow * a.in.nb * 32)[rem];
+    }
+    for (int u = threadIdx.x; u < cc * nb; u += kThreads) {
+      const int r = u / nb, bb = u - r * nb;
+      const int64_t pair = prs[c0 + r];
+      const int64_t t = pair / a.top_k, k = pair - t * a.top_k;
+      const int64_t arow = t * a.b_ne1 + (k % a.b_ne1);
+      s_d[u] = a.in.d[arow * a.in.nb + bb];
+    }
+    __syncthreads();
+
+    float acc[NV][kMaxPairs];
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+#pragma unroll
+      for (int r = 0; r < kMaxPairs; ++r) acc[v][r] = 0.f;
+
+    // Rolling prefetch: kPrefetch block loads per view stay in flight; each
+    // consumed slot is refilled with the block kPrefetch iterations ahead.
+    const int n_iter = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0;
+    RawBlock buf[kPrefetch][NV];
+#pragma unroll
+    for (int p = 0; p < kPrefetch; ++p) {
+      const bool in = p < n_iter;
+      buf[p][0] = load_block<WT>(a.w, slot, warp + p * kWarps, n, valid && in);
+      if constexpr (SWIGLU) buf[p][NV - 1] = load_block<WT>(a.w2, slot, warp + p * kWarps, n, valid && in);
+    }
+    for (int base = 0; base < n_iter; base += kPrefetch) {
+#pragma unroll
+      for (int p = 0; p < kPrefetch; ++p) {
+        const int it = base + p;
+        if (it < n_iter) {
+          const int b = warp + it * kWarps;
+          uint32_t wq[NV][8];
+          float sw[NV];
+#pragma unroll
+          for (int v = 0; v < NV; ++v) {
+            decode_block(buf[p][v].q, cb, wq[v]);
+            sw[v] = scale_of<WT>(buf[p][v].s);
+          }
+          const int nxt = it + kPrefetch;
+          const bool in = nxt < n_iter;
+          buf[p][0] = load_block<WT>(a.w, slot, warp + nxt * kWarps, n, valid && in);
+          if constexpr (SWIGLU) buf[p][NV - 1] = load_block<WT>(a.w2, slot, warp + nxt * kWarps, n, valid && in);
+#pragma unroll
+          for (int r = 0; r < kMaxPairs; ++r) {
+            if (r < cc) {
+              const int4 *ap = reinterpret_cast<const int4 *>(s_q + (int64_t(r) * nb + b) * 32);
+              const float da = s_d[r * nb + b];
+#pragma unroll
+              for (int v = 0; v < NV; ++v)
+                acc[v][r] += __fmul_rn(sw[v], da) * float(dot_block(wq[v], ap));
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+#pragma unroll
+      for (int r = 0; r < kMaxPairs; ++r)
+        if (r < cc) s_red[((warp * NV + v) * kMaxPairs + r) * 32 + lane] = acc[v][r];
+    __syncthreads();
+
+    // Reduce over warps in fixed order; warp r finishes pair r of the pass.
+    for (int r = warp; r < cc; r += kWarps) {
+      float tot[NV];
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        float s = 0.f;
+        for (int w = 0; w < kWarps; ++w) s += s_red[((w * NV + v) * kMaxPairs + r) * 32 + lane];
+        tot[v] = s;
+      }
+      const int64_t pair = prs[c0 + r];
+      if constexpr (SWIGLU) {
+        const float g = tot[0], up = tot[1];
+        float h = valid ? g / (1.f + expf(-g)) * up : 0.f;
+        if (a.act && valid) a.act[pair * a.n_out + n] = h;
+        store_q8_block(a.out, pair, tile, h, lane);
+      } else if (valid) {
+        a.res[pair * a.n_out + n] = tot[0];
+      }
+    }
+  }
+}
+
+// y[t, n] = sum_k w[k, t] * r[n, k, t], k in increasing order.
+__global__ void combine_kernel(const float *r, const float *w, int32_t top_k, int64_t N,
+                               int64_t n_tok, float *y) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= N * n_tok) return;
+  const int64_t t = i / N, n = i - t * N;
+  float s = 0.f;
+  for (int k = 0; k < top_k; ++k) s = fmaf(w[t * top_k + k], r[(t * top_k + k) * N + n], s);
+  y[i] = s;
+}
+
+// ---------------------------------------------------------------------------
+// Host helpers
+// ---------------------------------------------------------------------------
+static int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+// Carves an ActQ8 for n_rows x nb out of the workspace at *off.
+static ActQ8 carve_act(uint8_t *ws, int64_t *off, int64_t n_rows, int64_t nb) {
+  ActQ8 q;
+  q.q = reinterpret_cast<int8_t *>(ws + *off);
+  *off = align_up(*off + n_rows * nb * 32, 256);
+  q.d = reinterpret_cast<float *>(ws + *off);
+  *off = align_up(*off + n_rows * nb * 4, 256);
+  q.nb = nb;
+  return q;
+}
+
+static int quantize_act(const void *b, int b_type, int64_t b_ne1, int64_t b_nb1, int64_t b_nb2,
+                        int64_t n_rows, ActQ8 out, cudaStream_t st) {
+  const int64_t items = n_rows * out.nb;
+  if (items == 0) return MSB_OK;
+  const int64_t grid = (items + kWarps - 1) / kWarps;
+  const char *p = static_cast<const char *>(b);
+  if (b_type == MSB_TYPE_F32)
+    quantize_act_kernel<float><<<unsigned(grid), kThreads, 0, st>>>(p, b_nb1, b_nb2, b_ne1, n_rows, out);
+  else if (b_type == MSB_TYPE_BF16)
+    quantize_act_kernel<__nv_bfloat16><<<unsigned(grid), kThreads, 0, st>>>(p, b_nb1, b_nb2, b_ne1, n_rows, out);
+  else
+    return fail(MSB_ERR_INVALID, "activation type %d is not F32 or BF16", b_type);
+  count_launch();
+  MSB_CUDA_TRY(cudaGetLastError());
+  return MSB_OK;
+}
+
+// One-shot timing request for the next fused gate/up launch on this thread.
+static thread_local cudaEvent_t g_gate_up_start = nullptr, g_gate_up_stop = nullptr;
+
+template <int WT, bool SWIGLU>
+static int launch_gemv_t(const GemvArgs &a, int max_active, cudaStream_t st) {
+  const int NV = SWIGLU ? 2 : 1;
+  const size_t smem = size_t(kMaxPairs) * a.w.nb * 36 + size_t(kWarps) * NV * kMaxPairs * 32 * 4;
+  if (smem > 48 * 1024)
+    MSB_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<WT, SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const int64_t grid = int64_t(max_active) * a.tiles;
+  if (grid == 0) return MSB_OK;
+  const bool timed = SWIGLU && g_gate_up_start && g_gate_up_stop;
+  if (timed) MSB_CUDA_TRY(cudaEventRecord(g_gate_up_start, st));
+  gemv_kernel<WT, SWIGLU><<<unsigned(grid), kThreads, smem, st>>>(a); count_launch();
+  if (timed) {
+    MSB_CUDA_TRY(cudaEventRecord(g_gate_up_stop, st));
+    g_gate_up_start = g_gate_up_stop = nullptr;
+  }
+  MSB_CUDA_TRY(cudaGetLastError());
+  return MSB_OK;
+}
+
+static int launch_gemv(int wtype, bool swiglu, const GemvArgs &a, int max_active, cudaStream_t st) {
+  if (a.w.nb * 36 * kMaxPairs > 160 * 1024)
+    return fail(MSB_ERR_UNSUPPORTED, "K = %lld too large for the staged activations", (long long)(a.w.nb * 32));
+  if (wtype == MSB_TYPE_MXFP4)
+    return swiglu ? launch_gemv_t<MSB_TYPE_MXFP4, true>(a, max_active, st)
+                  : launch_gemv_t<MSB_TYPE_MXFP4, false>(a, max_active, st);
+  if (wtype == MSB_TYPE_IQ4_NL)
+    return swiglu ? launch_gemv_t<MSB_TYPE_IQ4_NL, true>(a, max_active, st)
+                  : launch_gemv_t<MSB_TYPE_IQ4_NL, false>(a, max_active, st);
+  return fail(MSB_ERR_INVALID, "weight type %d", wtype);
+}
+
+static void set_route(GemvArgs &g, const msb_route_t *r) {
+  g.counts = r->counts;
+  g.offsets = r->offsets;
+  g.rows = r->rows;
+  g.active = r->active;
+}
+
+}  // namespace msb
+
+using namespace msb;
+
+extern "C" void msb_time_next_gate_up(void *start, void *stop) {
+  g_gate_up_start = static_cast<cudaEvent_t>(start);
+  g_gate_up_stop = static_cast<cudaEvent_t>(stop);
+}
+
+extern "C" int64_t msb_workspace_bytes(int64_t K_max, int32_t n_tok, int32_t top_k, int32_t n_slot) {
+  (void)n_slot;
+  if (K_max <= 0 || K_max % 32 || n_tok < 0 || top_k <= 0) return -1;
+  const int64_t nb = K_max / 32, pairs = int64_t(n_tok) * top_k;
+  int64_t off = 0;
+  off = align_up(off + pairs * nb * 32, 256);  // activations in (up to one row per pair)
+  off = align_up(off + pairs * nb * 4, 256);
+  off = align_up(off + pairs * nb * 32, 256);  // SwiGLU output
+  off = align_up(off + pairs * nb * 4, 256);
+  off = align_up(off + pairs * K_max * 4, 256);  // down projection result
+  return off + 256;
+}
+
+extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, int64_t b_ne1,
+                              int64_t b_nb1, int64_t b_nb2, const msb_route_t *route,
+                              int32_t top_k, int32_t n_tok, float *res_dev, void *workspace,
+                              int64_t workspace_bytes, void *stream) {
+  MSB_CHECK_ARG(pool && route && res_dev && workspace, "msb_mul_mat_id: null argument");
+  MSB_CHECK_ARG(b_dev || n_tok == 0, "msb_mul_mat_id: null b");
+  MSB_CHECK_ARG(top_k > 0 && n_tok >= 0, "msb_mul_mat_id: bad shape");
+  MSB_CHECK_ARG(b_ne1 == 1 || b_ne1 == top_k, "msb_mul_mat_id: b_ne1 must be 1 or top_k");
+  const int64_t need = msb_workspace_bytes(pool->K, n_tok, top_k, pool->n_slot);
+  MSB_CHECK_ARG(workspace_bytes >= need, "msb_mul_mat_id: workspace %lld < %lld bytes",
+                (long long)workspace_bytes, (long long)need);
+  if (n_tok == 0) return MSB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  int64_t off = 0;
+  const int64_t n_rows = int64_t(n_tok) * b_ne1;
+  ActQ8 in = carve_act(ws, &off, n_rows, pool->nb);
+  if (int rc = quantize_act(b_dev, b_type, b_ne1, b_nb1, b_nb2, n_rows, in, st)) return rc;
+  GemvArgs g{};
+  g.w = view_of(pool);
+  g.w2 = g.w;
+  g.n_out = pool->N;
+  g.tiles = int((pool->N + 31) / 32);
+  set_route(g, route);
+  g.zero_slot = pool->n_slot;
+  g.top_k = top_k;
+  g.b_ne1 = int32_t(b_ne1);
+  g.in = in;
+  g.res = res_dev;
+  const int64_t pairs = int64_t(n_tok) * top_k;
+  const int max_active = int(pairs < pool->n_slot + 1 ? pairs : pool->n_slot + 1);
+  return launch_gemv(pool->wtype, false, g, max_active, st);
+}
+
+extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
+                           const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
+                           const float *w_dev, int32_t top_k, int32_t n_tok, float *y_dev,
+                           float *act_dev, void *workspace, int64_t workspace_bytes, void *stream) {
+  MSB_CHECK_ARG(gate && up && down && route && w_dev && y_dev && workspace, "msb_moe_ffn: null argument");
+  MSB_CHECK_ARG(x_dev || n_tok == 0, "msb_moe_ffn: null x");
+  MSB_CHECK_ARG(top_k > 0 && n_tok >= 0, "msb_moe_ffn: bad shape");
+  const int64_t n_ff = down->K;
+  MSB_CHECK_ARG(gate->wtype == up->wtype && up->wtype == down->wtype,
+                "msb_moe_ffn: gate, up and down must share a weight type");
+  MSB_CHECK_ARG(gate->K == up->K && down->N == gate->K,
+                "msb_moe_ffn: gate/up input width must equal down output width");
+  MSB_CHECK_ARG(gate->n_slot == up->n_slot && up->n_slot == down->n_slot,
+                "msb_moe_ffn: pools must have the same slot count");
+  MSB_CHECK_ARG(up_row0 >= 0 && up_row0 + n_ff <= up->N && n_ff <= gate->N,
+                "msb_moe_ffn: gate/up rows do not cover the down input width %lld", (long long)n_ff);
+  MSB_CHECK_ARG(up != gate || up_row0 >= n_ff, "msb_moe_ffn: fused gate_up needs up_row0 >= N_ff");
+  const int64_t K = gate->K;
+  const int64_t kmax = K > n_ff ? K : n_ff;
+  const int64_t need = msb_workspace_bytes(kmax, n_tok, top_k, gate->n_slot);
+  MSB_CHECK_ARG(workspace_bytes >= need, "msb_moe_ffn: workspace %lld < %lld bytes",
+                (long long)workspace_bytes, (long long)need);
+  if (n_tok == 0) return MSB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  const int64_t pairs = int64_t(n_tok) * top_k;
+  int64_t off = 0;
+  ActQ8 xq = carve_act(ws, &off, n_tok, gate->nb);
+  ActQ8 hq = carve_act(ws, &off, pairs, n_ff / 32);
+  float *rdown = reinterpret_cast<float *>(ws + off);
+  const int elt = x_type == MSB_TYPE_BF16 ? 2 : 4;
+  if (int rc = quantize_act(x_dev, x_type, 1, x_nb1, x_nb1, n_tok, xq, st)) return rc;
+  (void)elt;
+  const int max_active = int(pairs < gate->n_slot + 1 ? pairs : gate->n_slot + 1);
+
+  GemvArgs g{};
+  g.w = view_of(gate, 0);
+  g.w2 = view_of(up, up_row0);
+  g.n_out = n_ff;
+  g.tiles = int((n_ff + 31) / 32);
+  set_route(g, route);
+  g.zero_slot = gate->n_slot;
+  g.top_k = top_k;
+  g.b_ne1 = 1;
+  g.in = xq;
+  g.out = hq;
+  g.act = act_dev;
+  if (int rc = launch_gemv(gate->wtype, true, g, max_active, st)) return rc;
+
+  GemvArgs d{};
+  d.w = view_of(down);
+  d.w2 = d.w;
+  d.n_out = down->N;
+  d.tiles = int((down->N + 31) / 32);
+  set_route(d, route);
+  d.zero_slot = down->n_slot;
+  d.top_k = top_k;
+  d.b_ne1 = top_k;
+  d.in = hq;
+  d.res = rdown;
+  if (int rc = launch_gemv(down->wtype, false, d, max_active, st)) return rc;
+
+  const int64_t total = down->N * n_tok;
+  combine_kernel<<<unsigned((total + 255) / 256), 256, 0, st>>>(rdown, w_dev, top_k, down->N, n_tok, y_dev); count_launch();
+  MSB_CUDA_TRY(cudaGetLastError());
+  return MSB_OK;
+}

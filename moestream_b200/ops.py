@@ -1,0 +1,170 @@
+"""Device operations over the C ABI, taking and returning torch CUDA tensors.
+
+torch provides device memory and streams here; every computation runs in
+libmsb.so's kernels.
+"""
+import ctypes
+
+import torch
+
+from ._lib import (TYPE_BF16, TYPE_F32, TYPE_IQ4_NL, TYPE_MXFP4, PoolInfo, Route, c_vp,
+                   check, lib)
+
+WEIGHT_TYPES = {"iq4_nl": TYPE_IQ4_NL, "mxfp4": TYPE_MXFP4}
+_ACT_TYPES = {torch.float32: TYPE_F32, torch.bfloat16: TYPE_BF16}
+
+
+def _stream(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return c_vp(s.cuda_stream)
+
+
+def _ptr(t):
+    return c_vp(t.data_ptr()) if t is not None else c_vp(0)
+
+
+def expert_bytes(wtype, K, N):
+    return int(lib().msb_expert_bytes(WEIGHT_TYPES.get(wtype, wtype), K, N))
+
+
+class SlotPool:
+    """Device slab of n_slot + 1 expert slots; slot n_slot is the zero slot."""
+
+    def __init__(self, wtype, K, N, n_slot, max_fill_batch=4):
+        self.wtype = WEIGHT_TYPES.get(wtype, wtype)
+        h = c_vp()
+        check(lib().msb_pool_create(self.wtype, K, N, n_slot, max_fill_batch, ctypes.byref(h)))
+        self.handle = h
+        info = PoolInfo()
+        check(lib().msb_pool_get_info(h, ctypes.byref(info)))
+        self.K, self.N, self.n_slot = info.K, info.N, info.n_slot
+        self.expert_bytes = info.expert_bytes
+        self.slot_stride = info.slot_stride
+        self.zero_slot = n_slot
+
+    def close(self):
+        if self.handle:
+            check(lib().msb_pool_destroy(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def fill(self, slots, srcs, stream=None):
+        """Fills slots from ggml-layout expert bytes: host uint8 tensors
+        (pinned for asynchrony) or device uint8 tensors."""
+        slots = [int(s) for s in slots]
+        n = len(slots)
+        if n == 0:
+            return
+        sl = (ctypes.c_int32 * n)(*slots)
+        ptrs = (c_vp * n)(*[s.data_ptr() for s in srcs])
+        for s in srcs:
+            assert s.dtype == torch.uint8 and s.numel() >= self.expert_bytes
+        if srcs[0].is_cuda:
+            check(lib().msb_fill_slots_from_device_async(self.handle, n, sl, ptrs, _stream(stream)))
+        else:
+            check(lib().msb_fill_slots_async(self.handle, n, sl, ptrs, _stream(stream)))
+
+    def read_slot(self, slot, stream=None):
+        out = torch.empty(self.expert_bytes, dtype=torch.uint8, device="cuda")
+        check(lib().msb_read_slot_async(self.handle, slot, _ptr(out), _stream(stream)))
+        return out
+
+
+class RouteBuffers:
+    """Device arrays of one grouped route (msb_route_t)."""
+
+    def __init__(self, n_pairs, n_slot, device="cuda"):
+        z = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=device)
+        self.slot_ids = z(n_pairs)
+        self.counts = z(n_slot + 1)
+        self.offsets = z(n_slot + 2)
+        self.rows = z(n_pairs)
+        self.active = z(n_slot + 2)
+        self.n_slot = n_slot
+        self.c = Route(self.slot_ids.data_ptr(), self.counts.data_ptr(), self.offsets.data_ptr(),
+                       self.rows.data_ptr(), self.active.data_ptr())
+
+
+def remap_group(ids, n_slot, table=None, n_expert=None, route=None, stream=None):
+    """ids: int32 [n_tok, top_k] device tensor (any strides). Returns RouteBuffers."""
+    assert ids.dtype == torch.int32 and ids.is_cuda and ids.dim() == 2
+    n_tok, top_k = ids.shape
+    if route is None:
+        route = RouteBuffers(n_tok * top_k, n_slot, ids.device)
+    nb0, nb1 = ids.stride(1) * 4, ids.stride(0) * 4
+    ne = int(n_expert if n_expert is not None else (table.numel() if table is not None else 0))
+    check(lib().msb_remap_group(_ptr(ids), nb0, nb1, top_k, n_tok, _ptr(table), ne, n_slot,
+                                ctypes.byref(route.c), _stream(stream)))
+    return route
+
+
+def workspace(K_max, n_tok, top_k, n_slot, device="cuda"):
+    nbytes = int(lib().msb_workspace_bytes(K_max, n_tok, top_k, n_slot))
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def mul_mat_id(pool, b, route, top_k, ws=None, out=None, stream=None):
+    """b: [n_tok, b_ne1, K] f32/bf16 (ggml b [K, b_ne1, n_tok]); returns res
+    [n_tok, top_k, N] f32 (ggml res [N, top_k, n_tok])."""
+    n_tok, b_ne1, K = b.shape
+    assert K == pool.K and b.stride(2) == 1
+    if ws is None:
+        ws = workspace(pool.K, n_tok, top_k, pool.n_slot, b.device)
+    if out is None:
+        out = torch.empty(n_tok, top_k, pool.N, dtype=torch.float32, device=b.device)
+    es = b.element_size()
+    check(lib().msb_mul_mat_id(pool.handle, _ptr(b), _ACT_TYPES[b.dtype], b_ne1, b.stride(1) * es,
+                               b.stride(0) * es, ctypes.byref(route.c), top_k, n_tok, _ptr(out),
+                               _ptr(ws), ws.numel(), _stream(stream)))
+    return out
+
+
+def moe_ffn(gate, up, down, x, route, w, top_k, up_row0=0, ws=None, out=None, act=None,
+            stream=None):
+    """x: [n_tok, K] f32/bf16; w: [n_tok, top_k] f32. Returns y [n_tok, K] f32."""
+    n_tok, K = x.shape
+    assert x.stride(1) == 1 and w.dtype == torch.float32 and w.is_contiguous()
+    kmax = max(K, down.K)
+    if ws is None:
+        ws = workspace(kmax, n_tok, top_k, gate.n_slot, x.device)
+    if out is None:
+        out = torch.empty(n_tok, K, dtype=torch.float32, device=x.device)
+    check(lib().msb_moe_ffn(gate.handle, up.handle, up_row0, down.handle, _ptr(x),
+                            _ACT_TYPES[x.dtype], x.stride(0) * x.element_size(),
+                            ctypes.byref(route.c), _ptr(w), top_k, n_tok, _ptr(out), _ptr(act),
+                            _ptr(ws), ws.numel(), _stream(stream)))
+    return out
+
+
+def quantize_rows(wtype, src, stream=None):
+    """src: f32 [n_rows, K] device tensor -> ggml block bytes (uint8)."""
+    wt = WEIGHT_TYPES.get(wtype, wtype)
+    n_rows, K = src.shape
+    nbytes = int(lib().msb_expert_bytes(wt, K, n_rows))
+    out = torch.empty(nbytes, dtype=torch.uint8, device=src.device)
+    check(lib().msb_quantize_rows(wt, _ptr(src.contiguous()), n_rows, K, _ptr(out),
+                                  _stream(stream)))
+    return out
+
+
+def ep_dispatch(ids, x, n_local, n_rank, cap, send_x, send_e, pos, stream=None):
+    """Packs this rank's (token, k) rows for an equal-split all-to-all."""
+    n_tok, top_k = ids.shape
+    assert ids.is_contiguous() and x.stride(1) == 1 and send_x.dtype == torch.bfloat16
+    check(lib().msb_ep_dispatch(_ptr(ids), _ptr(x), _ACT_TYPES[x.dtype],
+                                x.stride(0) * x.element_size(), top_k, n_tok, x.shape[1],
+                                n_local, n_rank, cap, _ptr(send_x), _ptr(send_e), _ptr(pos),
+                                _stream(stream)))
+
+
+def ep_combine(back, pos, w, y, stream=None):
+    """y[t] = sum_k w[t, k] * back[pos[t, k]]."""
+    n_tok, top_k = w.shape
+    check(lib().msb_ep_combine(_ptr(back), _ptr(pos), _ptr(w), top_k, n_tok, back.shape[1],
+                               _ptr(y), _stream(stream)))
+    return y

@@ -1,0 +1,294 @@
+"""CPU oracle bindings (TEST INFRASTRUCTURE ONLY).
+
+Loads oracle/liboracle.so (this project's C restatement, msb_oracle.c) and,
+when built, oracle/_ref/libref_cache.so (the reference's own ExpertCache with
+the ms_remap_fn loop restated over it, ref_shim.cpp). Only tests/,
+__graft_entry__.smoke() and bench.py's CPU-baseline leg import this module,
+as the checker or the timed CPU baseline.
+
+The per-slot grouping oracle is restated here in numpy: the pairs of each
+slot in increasing pair order (a stable sort by slot), slots ascending; this
+is the row order ggml's mul_mat_id groups by expert.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIBORACLE = os.path.join(HERE, "liboracle.so")
+LIBREF = os.path.join(HERE, "_ref", "libref_cache.so")
+
+IQ4_NL = 20
+MXFP4 = 39
+TYPES = {"iq4_nl": IQ4_NL, "mxfp4": MXFP4}
+BLOCK_BYTES = {IQ4_NL: 18, MXFP4: 17}
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_u64p = ctypes.POINTER(ctypes.c_uint64)
+_vp = ctypes.c_void_p
+
+_orc = None
+_ref = None
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _p(a, t):
+    return a.ctypes.data_as(t)
+
+
+def orc():
+    global _orc
+    if _orc is None:
+        if not os.path.exists(LIBORACLE):
+            build()
+        L = ctypes.CDLL(LIBORACLE)
+        L.orc_dequant_row.argtypes = [ctypes.c_int, _u8p, _f32p, ctypes.c_int64]
+        L.orc_quantize_rows.argtypes = [ctypes.c_int, _f32p, ctypes.c_int64, ctypes.c_int64, _u8p]
+        L.orc_mul_mat_id.argtypes = [ctypes.c_int, _u8p, ctypes.c_int64, ctypes.c_int64,
+                                     ctypes.c_int64, _f32p, ctypes.c_int64, _i32p, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
+        L.orc_moe_ffn.argtypes = [ctypes.c_int, _u8p, ctypes.c_int64, _u8p, ctypes.c_int64,
+                                  ctypes.c_int64, _u8p, ctypes.c_int64, ctypes.c_int64,
+                                  ctypes.c_int64, _f32p, _i32p, _f32p, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int, _f32p, _f32p, ctypes.c_int]
+        L.orc_quantize_q8.argtypes = [_f32p, ctypes.c_int64, ctypes.POINTER(ctypes.c_int8), _f32p]
+        L.orc_f32_to_f16.argtypes = [ctypes.c_float]
+        L.orc_f32_to_f16.restype = ctypes.c_uint16
+        L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.orc_f16_to_f32.restype = ctypes.c_float
+        _orc = L
+    return _orc
+
+
+def ref_available():
+    return os.path.exists(LIBREF)
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        L = ctypes.CDLL(LIBREF)
+        L.orc_cache_new_cfg.restype = _vp
+        L.orc_cache_new_cfg.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                        ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                        ctypes.c_uint32, ctypes.c_int, ctypes.c_uint32,
+                                        ctypes.c_double, ctypes.c_uint32]
+        L.orc_cache_free.argtypes = [_vp]
+        L.orc_cache_acquire.argtypes = [_vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int, _u32p]
+        L.orc_cache_mark_resident.argtypes = [_vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64]
+        L.orc_cache_release.argtypes = [_vp, ctypes.c_uint32, ctypes.c_uint32]
+        L.orc_cache_end_step.argtypes = [_vp]
+        L.orc_cache_slot_of.argtypes = [_vp, ctypes.c_uint32, ctypes.c_uint32]
+        L.orc_cache_slot_of.restype = ctypes.c_uint32
+        L.orc_cache_build_pinned.argtypes = [_vp, _u32p, ctypes.c_size_t]
+        L.orc_cache_quota.argtypes = [_vp, _u32p]
+        L.orc_cache_stats.argtypes = [_vp, _u64p]
+        L.orc_remap_new.restype = _vp
+        L.orc_remap_new.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
+        L.orc_remap_free.argtypes = [_vp]
+        L.orc_remap_call.argtypes = [_vp, _i32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_uint64, _i32p, _i32p, _i32p, _i32p]
+        L.orc_remap_stats.argtypes = [_vp, _u64p, _u64p]
+        _ref = L
+    return _ref
+
+
+STATS_FIELDS = ("hit", "miss", "hit_pinned", "hit_small", "hit_main", "ghost_hit", "admit",
+                "evict", "bypass", "promote", "bytes_fetched")
+
+
+class RefCache:
+    """The reference ExpertCache, compiled from its own source."""
+
+    def __init__(self, n_layer=40, n_expert=256, n_slot=0, cache_frac=0.25, pin_ratio=0.05,
+                 small_ratio=0.10, ghost_mult=2, layer_quota_adapt=True, quota_period=512,
+                 quota_eta=0.10, quota_min=8):
+        self.n_layer = n_layer
+        self.h = ref().orc_cache_new_cfg(n_layer, n_expert, n_slot, cache_frac, pin_ratio,
+                                         small_ratio, ghost_mult, int(layer_quota_adapt),
+                                         quota_period, quota_eta, quota_min)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            ref().orc_cache_free(self.h)
+            self.h = None
+
+    def acquire(self, layer, expert, origin=0):
+        s = ctypes.c_uint32(0)
+        hit = ref().orc_cache_acquire(self.h, layer, expert, origin, ctypes.byref(s))
+        return bool(hit), int(s.value)
+
+    def mark_resident(self, layer, expert, nbytes):
+        ref().orc_cache_mark_resident(self.h, layer, expert, nbytes)
+
+    def release(self, layer, expert):
+        ref().orc_cache_release(self.h, layer, expert)
+
+    def end_step(self):
+        ref().orc_cache_end_step(self.h)
+
+    def slot_of(self, layer, expert):
+        return int(ref().orc_cache_slot_of(self.h, layer, expert))
+
+    def build_pinned(self, freq):
+        a = np.ascontiguousarray(freq, dtype=np.uint32)
+        ref().orc_cache_build_pinned(self.h, _p(a, _u32p), a.size)
+
+    def layer_quota(self):
+        out = np.zeros(self.n_layer, dtype=np.uint32)
+        ref().orc_cache_quota(self.h, _p(out, _u32p))
+        return out
+
+    def stats(self):
+        out = np.zeros(11, dtype=np.uint64)
+        ref().orc_cache_stats(self.h, _p(out, _u64p))
+        return {f: int(v) for f, v in zip(STATS_FIELDS, out)}
+
+
+class RefRemap:
+    """ms_remap_fn's loop over the reference ExpertCache, one layer."""
+
+    def __init__(self, n_expert, n_slot, expert_bytes=0):
+        self.h = ref().orc_remap_new(n_expert, n_slot)
+        self.expert_bytes = expert_bytes
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            ref().orc_remap_free(self.h)
+            self.h = None
+
+    def __call__(self, ids):
+        ids = np.asarray(ids)
+        n_tok, top_k = ids.shape
+        out = np.empty((n_tok, top_k), dtype=np.int32)
+        pe = np.empty(max(n_tok * top_k, 1), dtype=np.int32)
+        ps = np.empty_like(pe)
+        n = ctypes.c_int32(0)
+        base = ids.__array_interface__["data"][0]
+        ref().orc_remap_call(self.h, ctypes.cast(base, _i32p), ids.strides[1], ids.strides[0],
+                             top_k, n_tok, self.expert_bytes, _p(out, _i32p), _p(pe, _i32p),
+                             _p(ps, _i32p), ctypes.byref(n))
+        return out, list(zip(pe[:n.value].tolist(), ps[:n.value].tolist()))
+
+    def stats(self):
+        out = np.zeros(11, dtype=np.uint64)
+        ex = ctypes.c_uint64(0)
+        ref().orc_remap_stats(self.h, _p(out, _u64p), ctypes.byref(ex))
+        d = {f: int(v) for f, v in zip(STATS_FIELDS, out)}
+        d["exhausted"] = int(ex.value)
+        return d
+
+
+# ---------------------------------------------------------------------------
+# Block formats and matmul
+# ---------------------------------------------------------------------------
+def expert_bytes(wtype, K, N):
+    return (K // 32) * BLOCK_BYTES[TYPES.get(wtype, wtype)] * N
+
+
+def quantize(wtype, x):
+    """f32 [n_rows, K] -> ggml block bytes (uint8, flat)."""
+    t = TYPES.get(wtype, wtype)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n_rows, K = x.shape
+    out = np.empty(n_rows * (K // 32) * BLOCK_BYTES[t], dtype=np.uint8)
+    assert orc().orc_quantize_rows(t, _p(x, _f32p), n_rows, K, _p(out, _u8p)) == 0
+    return out
+
+
+def dequantize(wtype, data, K):
+    """ggml block bytes -> f32 [n_rows, K]."""
+    t = TYPES.get(wtype, wtype)
+    data = np.ascontiguousarray(data, dtype=np.uint8).reshape(-1)
+    rb = (K // 32) * BLOCK_BYTES[t]
+    n_rows = data.size // rb
+    out = np.empty((n_rows, K), dtype=np.float32)
+    for r in range(n_rows):
+        row = data[r * rb:(r + 1) * rb]
+        assert orc().orc_dequant_row(t, _p(row, _u8p), _p(out[r], _f32p), K) == 0
+    return out
+
+
+def quantize_q8(x):
+    """ggml q8_0 of one f32 row -> (int8 codes, fp16-rounded scales)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    q = np.empty(x.size, dtype=np.int8)
+    d = np.empty(x.size // 32, dtype=np.float32)
+    orc().orc_quantize_q8(_p(x, _f32p), x.size, q.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)),
+                          _p(d, _f32p))
+    return q, d
+
+
+def mul_mat_id(wtype, slab, K, N, b, ids, mode="exact", nthreads=None):
+    """slab: uint8 [n_slots, expert_bytes] (ggml layout); b: f32 [T, b_ne1, K];
+    ids: int32 slot ids [T, top_k]. Returns f32 [T, top_k, N]."""
+    t = TYPES.get(wtype, wtype)
+    slab = np.ascontiguousarray(slab, dtype=np.uint8)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    T, top_k = ids.shape
+    out = np.empty((T, top_k, N), dtype=np.float32)
+    rc = orc().orc_mul_mat_id(t, _p(slab, _u8p), K, N, slab.shape[0], _p(b, _f32p), b.shape[1],
+                              _p(ids, _i32p), top_k, T, 0 if mode == "exact" else 1,
+                              _p(out, _f32p), nthreads or os.cpu_count() or 1)
+    assert rc == 0, rc
+    return out
+
+
+def moe_ffn(wtype, gate, up, down, K, n_ff, x, ids, w, mode="exact", up_row0=0, up_rows=None,
+            nthreads=None):
+    """gate/up/down: uint8 [n_slots, bytes]; x: f32 [T, K]; ids: [T, top_k] slot
+    ids; w: f32 [T, top_k]. Returns (y [T, K], h [T, top_k, n_ff])."""
+    t = TYPES.get(wtype, wtype)
+    gate, up, down = (np.ascontiguousarray(a, dtype=np.uint8) for a in (gate, up, down))
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    T, top_k = ids.shape
+    y = np.empty((T, K), dtype=np.float32)
+    h = np.empty((T, top_k, n_ff), dtype=np.float32)
+    rc = orc().orc_moe_ffn(t, _p(gate, _u8p), n_ff, _p(up, _u8p), up_rows or n_ff, up_row0,
+                           _p(down, _u8p), K, n_ff, gate.shape[0], _p(x, _f32p), _p(ids, _i32p),
+                           _p(w, _f32p), top_k, T, 0 if mode == "exact" else 1, _p(y, _f32p),
+                           _p(h, _f32p), nthreads or os.cpu_count() or 1)
+    assert rc == 0, rc
+    return y, h
+
+
+def group(slot_ids, n_slot):
+    """Grouping oracle: (counts[S], offsets[S+1], rows, active) for S = n_slot+1."""
+    s = np.asarray(slot_ids, dtype=np.int64).reshape(-1)
+    S = n_slot + 1
+    counts = np.bincount(s, minlength=S).astype(np.int32)
+    offsets = np.zeros(S + 1, dtype=np.int32)
+    offsets[1:] = np.cumsum(counts)
+    rows = np.argsort(s, kind="stable").astype(np.int32)
+    active = np.nonzero(counts)[0].astype(np.int32)
+    return counts, offsets, rows, active
+
+
+def remap_table(ids, table, n_slot):
+    """Slot of each id through an expert -> slot table (zero slot otherwise)."""
+    ids = np.asarray(ids, dtype=np.int64)
+    table = np.asarray(table, dtype=np.int64)
+    out = np.full(ids.shape, n_slot, dtype=np.int32)
+    ok = (ids >= 0) & (ids < table.size)
+    s = np.where(ok, table[np.clip(ids, 0, table.size - 1)], -1)
+    good = ok & (s >= 0) & (s < n_slot)
+    out[good] = s[good]
+    return out
+
+
+def max_abs_normalized(got, want):
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    den = np.max(np.abs(want))
+    return float(np.max(np.abs(got - want)) / (den if den > 0 else 1.0))

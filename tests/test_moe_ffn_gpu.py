@@ -1,0 +1,92 @@
+"""MoE FFN layer (gate/up mul_mat_id + SwiGLU, down mul_mat_id, weighted
+combine) against the CPU oracle, for separate gate/up tensors and for a
+fused gate_up tensor whose first N_ff rows are the gate.
+
+Tolerances (max |got - want| / max |want|): 1e-2 against the exact f64
+oracle (the bound stated for this path); 2e-3 against the q8-mode oracle
+(the same quantization chain; the re-quantized SwiGLU output can round a
+code differently where the f32 sums differ in their last bit).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests.helpers import experts, topk_ids
+
+pytestmark = pytest.mark.gpu
+
+
+def build_layer(wtype, K, n_ff, n_expert, n_slot, fused, seed):
+    from moestream_b200 import ops
+    rng = np.random.default_rng(seed)
+    resident = rng.permutation(n_expert)[:n_slot]
+    slot_of = {int(e): int(s) for e, s in zip(resident, rng.permutation(n_slot))}
+    if fused:
+        gu = experts(wtype, n_expert, K, 2 * n_ff, seed)
+        pools = {"gate": ops.SlotPool(wtype, K, 2 * n_ff, n_slot)}
+        pools["up"] = pools["gate"]
+        mats = {"gate": gu}
+    else:
+        mats = {"gate": experts(wtype, n_expert, K, n_ff, seed),
+                "up": experts(wtype, n_expert, K, n_ff, seed + 1)}
+        pools = {r: ops.SlotPool(wtype, K, n_ff, n_slot) for r in ("gate", "up")}
+    mats["down"] = experts(wtype, n_expert, n_ff, K, seed + 2)
+    pools["down"] = ops.SlotPool(wtype, n_ff, K, n_slot)
+    for role, m in mats.items():
+        srcs = [torch.from_numpy(m[e]).pin_memory() for e in slot_of]
+        pools[role].fill(list(slot_of.values()), srcs)
+    slabs = {}
+    for role, m in mats.items():
+        slab = np.zeros((n_slot + 1, m.shape[1]), dtype=np.uint8)
+        for e, s in slot_of.items():
+            slab[s] = m[e]
+        slabs[role] = slab
+    torch.cuda.synchronize()
+    return pools, slabs, slot_of
+
+
+CASES = [
+    # wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, fused
+    ("mxfp4", 2880, 2880, 6, 4, 2, 4, True),     # gpt-oss widths
+    ("iq4_nl", 2048, 512, 10, 8, 8, 8, False),   # 256-expert model widths
+    ("mxfp4", 512, 256, 8, 8, 40, 4, True),      # several passes per slot
+    ("iq4_nl", 256, 128, 6, 3, 5, 2, False),
+]
+
+
+@pytest.mark.parametrize("wtype,K,n_ff,n_expert,n_slot,n_tok,top_k,fused", CASES)
+@pytest.mark.parametrize("xdtype", [torch.float32, torch.bfloat16])
+def test_moe_ffn_matches_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, fused, xdtype):
+    from moestream_b200 import ops
+    pools, slabs, slot_of = build_layer(wtype, K, n_ff, n_expert, n_slot, fused, seed=K + n_ff)
+    rng = np.random.default_rng(n_tok)
+    x = rng.normal(0, 1, size=(n_tok, K)).astype(np.float32)
+    if xdtype == torch.bfloat16:
+        x = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    ids_e, w = topk_ids(rng, n_tok, n_expert, top_k)
+    table = np.full(n_expert, -1, dtype=np.int32)
+    for e, s in slot_of.items():
+        table[e] = s
+    slots = O.remap_table(ids_e, table, n_slot)  # non-resident experts -> zero slot
+
+    xt = torch.from_numpy(x).cuda().to(xdtype)
+    r = ops.remap_group(torch.from_numpy(ids_e).cuda(), n_slot,
+                        table=torch.from_numpy(table).cuda(), n_expert=n_expert)
+    act = torch.empty(n_tok, top_k, n_ff, dtype=torch.float32, device="cuda")
+    y = ops.moe_ffn(pools["gate"], pools["up"], pools["down"], xt, r,
+                    torch.from_numpy(w).cuda(), top_k, up_row0=n_ff if fused else 0, act=act)
+    torch.cuda.synchronize()
+    y = y.cpu().numpy()
+
+    up = slabs["gate"] if fused else slabs["up"]
+    up_rows = 2 * n_ff if fused else n_ff
+    kw = dict(up_row0=n_ff if fused else 0, up_rows=up_rows)
+    y_q8, h_q8 = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
+                           mode="q8", **kw)
+    y_ex, h_ex = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
+                           mode="exact", **kw)
+    assert O.max_abs_normalized(act.cpu().numpy(), h_q8) < 1e-5
+    assert O.max_abs_normalized(y, y_q8) < 2e-3
+    assert O.max_abs_normalized(y, y_ex) < 1e-2
+    assert O.max_abs_normalized(act.cpu().numpy(), h_ex) < 1e-2

@@ -1,0 +1,134 @@
+"""mul_mat_id over the slot pool against the CPU oracle.
+
+Tolerances (max |got - want| / max |want|):
+  - vs the oracle in q8 mode (same activation quantization, f32 block sums
+    in another order): 1e-5;
+  - vs the exact f64 oracle: 1e-2, the bound stated for this path.
+Properties from the reference's spikes: bit-identical results under slot
+permutation (s0 T3), unreferenced slots harmless (s0 T4), the zero slot
+gives exactly 0 (s3), split expert sets add up (s4).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests.helpers import experts, topk_ids
+
+pytestmark = pytest.mark.gpu
+
+TOL_Q8 = 1e-5
+TOL_EXACT = 1e-2
+
+
+def make_pool(wtype, K, N, n_slot, slab_bytes, slots):
+    from moestream_b200 import ops
+    pool = ops.SlotPool(wtype, K, N, n_slot)
+    srcs = [torch.from_numpy(slab_bytes[i]).pin_memory() for i in range(len(slots))]
+    pool.fill(slots, srcs)
+    torch.cuda.synchronize()
+    return pool
+
+
+def gpu_mmid(pool, b_np, ids_np, dtype=torch.float32):
+    from moestream_b200 import ops
+    b = torch.from_numpy(b_np).cuda().to(dtype)
+    ids = torch.from_numpy(ids_np).cuda()
+    r = ops.remap_group(ids, pool.n_slot)
+    out = ops.mul_mat_id(pool, b, r, ids_np.shape[1])
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def slab_for(ex, slot_of_expert, n_slot):
+    """ggml-layout slab [n_slot + 1, bytes] holding expert e in slot_of_expert[e]."""
+    slab = np.zeros((n_slot + 1, ex.shape[1]), dtype=np.uint8)
+    for e, s in slot_of_expert.items():
+        slab[s] = ex[e]
+    return slab
+
+
+SHAPES = [
+    # wtype, K, N, n_expert, n_slot, n_tok, top_k, b_ne1
+    ("iq4_nl", 2048, 768, 16, 8, 1, 8, 1),    # single-op shape (fewer experts)
+    ("iq4_nl", 512, 2048, 12, 8, 8, 8, 8),    # 256-expert model's down projection shape
+    ("mxfp4", 2880, 256, 10, 6, 4, 4, 1),     # gpt-oss K (90 blocks: uneven warp split)
+    ("mxfp4", 256, 96, 8, 5, 37, 4, 4),       # many pairs per slot (> 8: several passes)
+    ("iq4_nl", 96, 40, 6, 4, 5, 2, 1),        # N not a multiple of 32
+]
+
+
+@pytest.mark.parametrize("wtype,K,N,n_expert,n_slot,n_tok,top_k,b_ne1", SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_mul_mat_id_matches_oracle(wtype, K, N, n_expert, n_slot, n_tok, top_k, b_ne1, dtype):
+    rng = np.random.default_rng(K + N + n_tok)
+    ex = experts(wtype, n_expert, K, N, seed=0)
+    resident = rng.permutation(n_expert)[:n_slot]
+    slot_of = {int(resident[i]): int(s) for i, s in enumerate(rng.permutation(n_slot))}
+    pool = make_pool(wtype, K, N, n_slot, [ex[e] for e in slot_of], list(slot_of.values()))
+    ids = rng.integers(0, n_slot + 1, size=(n_tok, top_k)).astype(np.int32)  # incl. zero slot
+    b = rng.normal(0, 1, size=(n_tok, b_ne1, K)).astype(np.float32)
+    if dtype == torch.bfloat16:
+        b = torch.from_numpy(b).to(torch.bfloat16).float().numpy()  # oracle sees bf16 values
+    got = gpu_mmid(pool, b, ids, dtype)
+    slab = slab_for(ex, slot_of, n_slot)
+    want_q8 = O.mul_mat_id(wtype, slab, K, N, b, ids, mode="q8")
+    want = O.mul_mat_id(wtype, slab, K, N, b, ids, mode="exact")
+    assert O.max_abs_normalized(got, want_q8) < TOL_Q8
+    assert O.max_abs_normalized(got, want) < TOL_EXACT
+    # Rows routed to the zero slot are exactly zero.
+    z = ids == n_slot
+    assert np.all(got[z] == 0.0)
+
+
+def test_slot_permutation_is_bit_identical():
+    wtype, K, N, n_slot = "mxfp4", 512, 128, 6
+    ex = experts(wtype, 6, K, N, seed=1)
+    rng = np.random.default_rng(2)
+    b = rng.normal(0, 1, size=(9, 1, K)).astype(np.float32)
+    ids_e = rng.integers(0, 6, size=(9, 4)).astype(np.int32)  # expert ids
+    outs = []
+    for perm_seed in (0, 1):
+        perm = np.random.default_rng(perm_seed).permutation(n_slot)  # expert e -> slot perm[e]
+        pool = make_pool(wtype, K, N, n_slot, [ex[e] for e in range(6)], perm.tolist())
+        outs.append(gpu_mmid(pool, b, perm[ids_e].astype(np.int32)))
+    assert np.array_equal(outs[0], outs[1])
+
+
+def test_unreferenced_slots_do_not_matter():
+    wtype, K, N, n_slot = "iq4_nl", 256, 64, 5
+    ex = experts(wtype, 8, K, N, seed=3)
+    rng = np.random.default_rng(4)
+    b = rng.normal(0, 1, size=(4, 1, K)).astype(np.float32)
+    ids = np.array([[0, 2], [2, 0], [0, 2], [2, 0]], dtype=np.int32)
+    p1 = make_pool(wtype, K, N, n_slot, [ex[0], ex[1], ex[2]], [0, 1, 2])
+    p2 = make_pool(wtype, K, N, n_slot, [ex[0], ex[5], ex[2], ex[7]], [0, 1, 2, 3])
+    assert np.array_equal(gpu_mmid(p1, b, ids), gpu_mmid(p2, b, ids))
+
+
+def test_split_expert_sets_add_up():
+    """FFN-style additivity at the matmul: routing half the ids to the zero
+    slot in each of two calls sums to the full call (s4's property)."""
+    wtype, K, N, n_slot = "mxfp4", 256, 64, 8
+    ex = experts(wtype, 8, K, N, seed=5)
+    pool = make_pool(wtype, K, N, n_slot, [ex[e] for e in range(8)], list(range(8)))
+    rng = np.random.default_rng(6)
+    b = rng.normal(0, 1, size=(6, 1, K)).astype(np.float32)
+    ids = rng.integers(0, 8, size=(6, 4)).astype(np.int32)
+    full = gpu_mmid(pool, b, ids)
+    lo = np.where(ids < 4, ids, n_slot).astype(np.int32)
+    hi = np.where(ids >= 4, ids, n_slot).astype(np.int32)
+    s = gpu_mmid(pool, b, lo) + gpu_mmid(pool, b, hi)
+    assert np.array_equal(full, s)  # each row comes entirely from one call
+
+
+def test_zero_slot_exact_zero_even_from_memory():
+    """The zero slot's bytes are zeros and a row routed there is 0."""
+    from moestream_b200 import ops
+    pool = ops.SlotPool("iq4_nl", 128, 32, 3)
+    z = pool.read_slot(3)
+    torch.cuda.synchronize()
+    assert int(z.to(torch.int64).sum()) == 0
+    b = np.random.default_rng(0).normal(0, 1, size=(2, 1, 128)).astype(np.float32)
+    got = gpu_mmid(pool, b, np.full((2, 3), 3, dtype=np.int32))
+    assert np.all(got == 0.0)
