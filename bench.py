@@ -350,6 +350,11 @@ def main():
     # Dominant kernel timing: events around every fused gate/up launch.
     gate_ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 for _ in range(L)] for _ in range(args.steps)]
+    for pair in gate_ev:  # torch creates the CUDA event on its first record
+        for a, b in pair:
+            a.record()
+            b.record()
+    torch.cuda.synchronize()
     clocks = Clocks(local)
     clocks.start()
     launches0 = int(ops.lib().msb_kernel_launches())

@@ -147,6 +147,64 @@ __device__ __forceinline__ void decode_block(const uint4 &q, const Codebook &cb,
   decode_nibbles(q.w, cb, wq[6], wq[7]);
 }
 
+// K loop of one pass over C activation rows: each warp takes blocks
+// b = warp, warp + 8, ...; lane = output row. Partial sums go to s_red.
+template <int WT, bool SWIGLU, int C>
+__device__ __forceinline__ void k_loop(const GemvArgs &a, int slot, int64_t n, bool valid,
+                                       int warp, int lane, const int8_t *s_q, const float *s_d,
+                                       float *s_red) {
+  constexpr int NV = SWIGLU ? 2 : 1;
+  const int nb = int(a.w.nb);
+  const Codebook cb = codebook<WT>();
+  float acc[NV][C];
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int r = 0; r < C; ++r) acc[v][r] = 0.f;
+  // Rolling prefetch: kPrefetch block loads per view stay in flight; each
+  // consumed slot is refilled with the block kPrefetch iterations ahead.
+  const int n_iter = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0;
+  RawBlock buf[kPrefetch][NV];
+#pragma unroll
+  for (int p = 0; p < kPrefetch; ++p) {
+    const bool in = p < n_iter;
+    buf[p][0] = load_block<WT>(a.w, slot, warp + p * kWarps, n, valid && in);
+    if constexpr (SWIGLU) buf[p][NV - 1] = load_block<WT>(a.w2, slot, warp + p * kWarps, n, valid && in);
+  }
+  for (int base = 0; base < n_iter; base += kPrefetch) {
+#pragma unroll
+    for (int p = 0; p < kPrefetch; ++p) {
+      const int it = base + p;
+      if (it < n_iter) {
+        const int b = warp + it * kWarps;
+        uint32_t wq[NV][8];
+        float sw[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+          decode_block(buf[p][v].q, cb, wq[v]);
+          sw[v] = scale_of<WT>(buf[p][v].s);
+        }
+        const int nxt = it + kPrefetch;
+        const bool in = nxt < n_iter;
+        buf[p][0] = load_block<WT>(a.w, slot, warp + nxt * kWarps, n, valid && in);
+        if constexpr (SWIGLU) buf[p][NV - 1] = load_block<WT>(a.w2, slot, warp + nxt * kWarps, n, valid && in);
+#pragma unroll
+        for (int r = 0; r < C; ++r) {
+          const int4 *ap = reinterpret_cast<const int4 *>(s_q + (int64_t(r) * nb + b) * 32);
+          const float da = s_d[r * nb + b];
+#pragma unroll
+          for (int v = 0; v < NV; ++v)
+            acc[v][r] += __fmul_rn(sw[v], da) * float(dot_block(wq[v], ap));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int r = 0; r < C; ++r) s_red[((warp * NV + v) * kMaxPairs + r) * 32 + lane] = acc[v][r];
+}
+
 template <int WT, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
   constexpr int NV = SWIGLU ? 2 : 1;  // weight views per lane
@@ -182,7 +240,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     return;
   }
 
-  const Codebook cb = codebook<WT>();
   for (int c0 = 0; c0 < c_total; c0 += kMaxPairs) {
     const int cc = min(kMaxPairs, c_total - c0);
     __syncthreads();  // shared buffers of the previous pass are consumed
@@ -205,57 +262,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     }
     __syncthreads();
 
-    float acc[NV][kMaxPairs];
-#pragma unroll
-    for (int v = 0; v < NV; ++v)
-#pragma unroll
-      for (int r = 0; r < kMaxPairs; ++r) acc[v][r] = 0.f;
-
-    // Rolling prefetch: kPrefetch block loads per view stay in flight; each
-    // consumed slot is refilled with the block kPrefetch iterations ahead.
-    const int n_iter = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0;
-    RawBlock buf[kPrefetch][NV];
-#pragma unroll
-    for (int p = 0; p < kPrefetch; ++p) {
-      const bool in = p < n_iter;
-      buf[p][0] = load_block<WT>(a.w, slot, warp + p * kWarps, n, valid && in);
-      if constexpr (SWIGLU) buf[p][NV - 1] = load_block<WT>(a.w2, slot, warp + p * kWarps, n, valid && in);
+    // The K loop is specialized on the pass's pair count, so no instruction
+    // is issued for pairs the pass does not have.
+    switch (cc) {
+      case 1: k_loop<WT, SWIGLU, 1>(a, slot, n, valid, warp, lane, s_q, s_d, s_red); break;
+      case 2: k_loop<WT, SWIGLU, 2>(a, slot, n, valid, warp, lane, s_q, s_d, s_red); break;
+      case 3: k_loop<WT, SWIGLU, 3>(a, slot, n, valid, warp, lane, s_q, s_d, s_red); break;
+      case 4: k_loop<WT, SWIGLU, 4>(a, slot, n, valid, warp, lane, s_q, s_d, s_red); break;
+      case 5: k_loop<WT, SWIGLU, 5>(a, slot, n, valid, warp, lane, s_q, s_d, s_red); break;
+      case 6: k_loop<WT, SWIGLU, 6>(a, slot, n, valid, warp, lane, s_q, s_d, s_red); break;
+      case 7: k_loop<WT, SWIGLU, 7>(a, slot, n, valid, warp, lane, s_q, s_d, s_red); break;
+      default: k_loop<WT, SWIGLU, 8>(a, slot, n, valid, warp, lane, s_q, s_d, s_red); break;
     }
-    for (int base = 0; base < n_iter; base += kPrefetch) {
-#pragma unroll
-      for (int p = 0; p < kPrefetch; ++p) {
-        const int it = base + p;
-        if (it < n_iter) {
-          const int b = warp + it * kWarps;
-          uint32_t wq[NV][8];
-          float sw[NV];
-#pragma unroll
-          for (int v = 0; v < NV; ++v) {
-            decode_block(buf[p][v].q, cb, wq[v]);
-            sw[v] = scale_of<WT>(buf[p][v].s);
-          }
-          const int nxt = it + kPrefetch;
-          const bool in = nxt < n_iter;
-          buf[p][0] = load_block<WT>(a.w, slot, warp + nxt * kWarps, n, valid && in);
-          if constexpr (SWIGLU) buf[p][NV - 1] = load_block<WT>(a.w2, slot, warp + nxt * kWarps, n, valid && in);
-#pragma unroll
-          for (int r = 0; r < kMaxPairs; ++r) {
-            if (r < cc) {
-              const int4 *ap = reinterpret_cast<const int4 *>(s_q + (int64_t(r) * nb + b) * 32);
-              const float da = s_d[r * nb + b];
-#pragma unroll
-              for (int v = 0; v < NV; ++v)
-                acc[v][r] += __fmul_rn(sw[v], da) * float(dot_block(wq[v], ap));
-            }
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int v = 0; v < NV; ++v)
-#pragma unroll
-      for (int r = 0; r < kMaxPairs; ++r)
-        if (r < cc) s_red[((warp * NV + v) * kMaxPairs + r) * 32 + lane] = acc[v][r];
     __syncthreads();
 
     // Reduce over warps in fixed order; warp r finishes pair r of the pass.

@@ -124,54 +124,57 @@ __global__ void quantize_mxfp4_kernel(const float *src, uint8_t *dst,
   }
 }
 
-__device__ float iq4nl_block_sse(const float *x, float d, uint8_t *idx) {
-  float sse = 0.f;
+// Squared error of a block coded at scale d; optionally accumulates the
+// least-squares terms sum(x*l) and sum(l*l) of the chosen codes l.
+__device__ float iq4nl_block_sse(const float *x, float d, float *sxl, float *sll) {
+  float sse = 0.f, a = 0.f, b = 0.f;
   for (int j = 0; j < 32; ++j) {
-    idx[j] = uint8_t(nearest_code(x[j], d, c_kv_iq4nl));
-    const float r = __fsub_rn(x[j], __fmul_rn(d, float(c_kv_iq4nl[idx[j]])));
+    const float l = float(c_kv_iq4nl[nearest_code(x[j], d, c_kv_iq4nl)]);
+    const float r = __fsub_rn(x[j], __fmul_rn(d, l));
     sse = __fadd_rn(sse, __fmul_rn(r, r));
+    a = __fadd_rn(a, __fmul_rn(x[j], l));
+    b = __fadd_rn(b, __fmul_rn(l, l));
   }
+  if (sxl) *sxl = a;
+  if (sll) *sll = b;
   return sse;
 }
 
 // IQ4_NL scale search: start from the scale that maps the largest-magnitude
 // element onto the codebook's end (-127), refine once by least squares for
 // the chosen codes, keep whichever fp16 scale has the smaller squared error.
+// Codes are those nearest to each element at the kept scale.
 __global__ void quantize_iq4nl_kernel(const float *src, uint8_t *dst,
                                       int64_t n_blocks) {
   const int64_t blk = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (blk >= n_blocks) return;
   const float *x = src + blk * 32;
-  uint8_t *o = dst + blk * 18;
   float amax = 0.f, vmax = 0.f;
   for (int j = 0; j < 32; ++j) {
     const float a = fabsf(x[j]);
     if (a > amax) { amax = a; vmax = x[j]; }
   }
-  uint8_t idx[32], idx1[32];
-  float d;
-  if (amax == 0.f) {
-    d = 0.f;
-    for (int j = 0; j < 32; ++j) idx[j] = 8;
-  } else {
+  float d = 0.f;
+  if (amax != 0.f) {
     d = __half2float(__float2half_rn(vmax / -127.f));
-    const float sse0 = iq4nl_block_sse(x, d, idx);
-    float sxl = 0.f, sll = 0.f;
-    for (int j = 0; j < 32; ++j) {
-      const float l = float(c_kv_iq4nl[idx[j]]);
-      sxl = __fadd_rn(sxl, __fmul_rn(x[j], l));
-      sll = __fadd_rn(sll, __fmul_rn(l, l));
-    }
+    float sxl, sll;
+    const float sse0 = iq4nl_block_sse(x, d, &sxl, &sll);
     const float d1 = __half2float(__float2half_rn(sxl / sll));
-    const float sse1 = iq4nl_block_sse(x, d1, idx1);
-    if (sse1 < sse0) {
-      d = d1;
-      for (int j = 0; j < 32; ++j) idx[j] = idx1[j];
-    }
+    const float sse1 = iq4nl_block_sse(x, d1, nullptr, nullptr);
+    if (sse1 < sse0) d = d1;
   }
-  const __half dh = __float2half_rn(d);
-  memcpy(o, &dh, 2);
-  for (int j = 0; j < 16; ++j) o[2 + j] = uint8_t(idx[j] | (idx[j + 16] << 4));
+  // Block bytes as nine 16-bit words (the block starts on an even byte).
+  unsigned short *o = reinterpret_cast<unsigned short *>(dst + blk * 18);
+  o[0] = __half_as_ushort(__float2half_rn(d));
+  for (int j = 0; j < 16; j += 2) {
+    unsigned short w = 0;
+    for (int h = 0; h < 2; ++h) {
+      const int lo = amax != 0.f ? nearest_code(x[j + h], d, c_kv_iq4nl) : 8;
+      const int hi = amax != 0.f ? nearest_code(x[j + h + 16], d, c_kv_iq4nl) : 8;
+      w |= (unsigned short)((lo | (hi << 4)) << (8 * h));
+    }
+    o[1 + j / 2] = w;
+  }
 }
 
 }  // namespace msb
@@ -344,6 +347,8 @@ extern "C" int msb_quantize_rows(int wtype, const float *src_dev, int64_t n_rows
   const int64_t grid = (n_blocks + threads - 1) / threads;
   MSB_CHECK_ARG(grid < (int64_t(1) << 31), "msb_quantize_rows: too many blocks in one call");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MSB_CHECK_ARG((reinterpret_cast<uintptr_t>(dst_dev) & 1) == 0,
+                "msb_quantize_rows: dst must be 2-byte aligned");
   if (wtype == MSB_TYPE_MXFP4)
     quantize_mxfp4_kernel<<<unsigned(grid), threads, 0, st>>>(src_dev, static_cast<uint8_t *>(dst_dev), n_blocks);
   else if (wtype == MSB_TYPE_IQ4_NL)

@@ -357,18 +357,19 @@ int orc_moe_ffn(int type, const uint8_t *gate, int64_t gate_rows, const uint8_t 
   float *g = (float *)malloc(sizeof(float) * (size_t)(pairs * n_ff));
   float *u = (float *)malloc(sizeof(float) * (size_t)(pairs * n_ff));
   float *r = (float *)malloc(sizeof(float) * (size_t)(pairs * K));
-  int rc = orc_mul_mat_id(type, gate, K, n_ff, n_slots, x, 1, ids, top_k, T, mode, g, nthreads);
-  /* The up projection reads rows [up_row0, up_row0 + n_ff) of each slot. */
-  if (!rc) {
-    const int64_t up_slot = up_rows * (K / 32) * bb;
-    uint8_t *upv = (uint8_t *)malloc((size_t)(n_slots * n_ff * (K / 32) * bb));
-    for (int64_t s = 0; s < n_slots; ++s)
-      memcpy(upv + s * n_ff * (K / 32) * bb, up + s * up_slot + up_row0 * (K / 32) * bb,
-             (size_t)(n_ff * (K / 32) * bb));
-    rc = orc_mul_mat_id(type, upv, K, n_ff, n_slots, x, 1, ids, top_k, T, mode, u, nthreads);
-    free(upv);
+  /* Views of n_ff rows per slot: gate rows [0, n_ff) of a slot of gate_rows
+   * rows, up rows [up_row0, up_row0 + n_ff) of a slot of up_rows rows. */
+  const int64_t row_bytes = (K / 32) * bb, view = n_ff * row_bytes;
+  uint8_t *gv = (uint8_t *)malloc((size_t)(n_slots * view));
+  uint8_t *uv = (uint8_t *)malloc((size_t)(n_slots * view));
+  for (int64_t s = 0; s < n_slots; ++s) {
+    memcpy(gv + s * view, gate + s * gate_rows * row_bytes, (size_t)view);
+    memcpy(uv + s * view, up + s * up_rows * row_bytes + up_row0 * row_bytes, (size_t)view);
   }
-  (void)gate_rows;
+  int rc = orc_mul_mat_id(type, gv, K, n_ff, n_slots, x, 1, ids, top_k, T, mode, g, nthreads);
+  if (!rc) rc = orc_mul_mat_id(type, uv, K, n_ff, n_slots, x, 1, ids, top_k, T, mode, u, nthreads);
+  free(gv);
+  free(uv);
   if (!rc) {
     float *h = (float *)malloc(sizeof(float) * (size_t)(pairs * n_ff));
     for (int64_t i = 0; i < pairs * n_ff; ++i) h[i] = g[i] / (1.f + expf(-g[i])) * u[i];

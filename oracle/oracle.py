@@ -246,16 +246,21 @@ def mul_mat_id(wtype, slab, K, N, b, ids, mode="exact", nthreads=None):
 def moe_ffn(wtype, gate, up, down, K, n_ff, x, ids, w, mode="exact", up_row0=0, up_rows=None,
             nthreads=None):
     """gate/up/down: uint8 [n_slots, bytes]; x: f32 [T, K]; ids: [T, top_k] slot
-    ids; w: f32 [T, top_k]. Returns (y [T, K], h [T, top_k, n_ff])."""
+    ids; w: f32 [T, top_k]. The gate is rows [0, n_ff) and the up projection
+    rows [up_row0, up_row0 + n_ff) of their slots (the same array for a fused
+    gate_up tensor). Returns (y [T, K], h [T, top_k, n_ff])."""
     t = TYPES.get(wtype, wtype)
     gate, up, down = (np.ascontiguousarray(a, dtype=np.uint8) for a in (gate, up, down))
+    row_bytes = (K // 32) * BLOCK_BYTES[t]
+    gate_rows = gate.shape[1] // row_bytes
+    up_rows = up.shape[1] // row_bytes
     x = np.ascontiguousarray(x, dtype=np.float32)
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     w = np.ascontiguousarray(w, dtype=np.float32)
     T, top_k = ids.shape
     y = np.empty((T, K), dtype=np.float32)
     h = np.empty((T, top_k, n_ff), dtype=np.float32)
-    rc = orc().orc_moe_ffn(t, _p(gate, _u8p), n_ff, _p(up, _u8p), up_rows or n_ff, up_row0,
+    rc = orc().orc_moe_ffn(t, _p(gate, _u8p), gate_rows, _p(up, _u8p), up_rows, up_row0,
                            _p(down, _u8p), K, n_ff, gate.shape[0], _p(x, _f32p), _p(ids, _i32p),
                            _p(w, _f32p), top_k, T, 0 if mode == "exact" else 1, _p(y, _f32p),
                            _p(h, _f32p), nthreads or os.cpu_count() or 1)
