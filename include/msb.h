@@ -239,6 +239,16 @@ int msb_ep_combine(const float *back_dev, const int32_t *pos_dev,
 /* Measurement hooks                                                          */
 /* ======================================================================== */
 
+/* Options (msb_set_option). MSB_OPT_MXFP4_PATH selects the arithmetic of
+ * MXFP4 mul_mat_id: 0 (default) = tensor cores (tcgen05 block-scaled FP4,
+ * activations as four e2m1 terms per 32-element block) wherever the shapes
+ * allow (K a multiple of 64; gate/up views starting on 128-row boundaries),
+ * the CUDA-core path otherwise; 1 = the CUDA-core path everywhere (int8
+ * activations per 32-element block with an fp16 scale, ggml's q8_0 form).
+ * Process-wide. */
+#define MSB_OPT_MXFP4_PATH 1
+int msb_set_option(int option, int value);
+
 /* Kernels this library has launched in this process (all threads). */
 uint64_t msb_kernel_launches(void);
 

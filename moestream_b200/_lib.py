@@ -17,6 +17,7 @@ TYPE_MXFP4 = 39
 
 ORIGIN_DEMAND, ORIGIN_PREFETCH_HIGH, ORIGIN_PREFETCH_LOW, ORIGIN_SWEEP = 0, 1, 2, 3
 NO_SLOT = 0xFFFFFFFF
+OPT_MXFP4_PATH = 1
 
 c_i32p = ctypes.POINTER(ctypes.c_int32)
 c_u32p = ctypes.POINTER(ctypes.c_uint32)
@@ -92,6 +93,7 @@ SIGNATURES = {
     "msb_ep_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.c_int64, c_vp, c_vp]),
     "msb_kernel_launches": (ctypes.c_uint64, []),
+    "msb_set_option": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "msb_time_next_gate_up": (None, [c_vp, c_vp]),
     "msb_quantize_rows": (ctypes.c_int, [ctypes.c_int, c_vp, ctypes.c_int64, ctypes.c_int64,
                                          c_vp, c_vp]),

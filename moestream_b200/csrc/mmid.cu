@@ -27,6 +27,19 @@
 
 namespace msb {
 
+// Tensor-core path (mmid_tc.cu).
+int64_t tc_act_bytes(int64_t nb, int64_t rows);
+int tc_supported(const msb_pool_s *p);
+int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb2, int32_t top_k,
+                 const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st);
+int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
+                  const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
+                  uint8_t *act_out, float *act_f32, int *err, int max_active, cudaStream_t st);
+
+// MXFP4 arithmetic: 0 = tensor cores where the shapes allow, 1 = CUDA cores
+// with int8 activations (ggml's q8_0 form) everywhere.
+static int g_mxfp4_path = 0;
+
 static constexpr int kThreads = 256;
 static constexpr int kWarps = kThreads / 32;
 static constexpr int kMaxPairs = 8;  // activation rows held per pass
@@ -127,8 +140,9 @@ __device__ __forceinline__ RawBlock load_block(const PoolView &v, int slot, int6
     const uint8_t *sb = v.base + int64_t(slot) * v.slot_stride;
     const int64_t off = b * v.N + v.row0 + n;
     r.q = __ldg(reinterpret_cast<const uint4 *>(sb + off * 16));
-    if constexpr (WT == MSB_TYPE_MXFP4) r.s = __ldg(sb + v.nb * v.N * 16 + off);
-    else r.s = __ldg(reinterpret_cast<const unsigned short *>(sb + v.nb * v.N * 16) + off);
+    const uint8_t *sc = sb + v.nb * v.N * 16;
+    if constexpr (WT == MSB_TYPE_MXFP4) r.s = __ldg(sc + scale_offset(true, b, v.row0 + n, v.N));
+    else r.s = __ldg(reinterpret_cast<const unsigned short *>(sc) + off);
   }
   return r;
 }
@@ -396,13 +410,29 @@ extern "C" int64_t msb_workspace_bytes(int64_t K_max, int32_t n_tok, int32_t top
   (void)n_slot;
   if (K_max <= 0 || K_max % 32 || n_tok < 0 || top_k <= 0) return -1;
   const int64_t nb = K_max / 32, pairs = int64_t(n_tok) * top_k;
-  int64_t off = 0;
-  off = align_up(off + pairs * nb * 32, 256);  // activations in (up to one row per pair)
-  off = align_up(off + pairs * nb * 4, 256);
-  off = align_up(off + pairs * nb * 32, 256);  // SwiGLU output
-  off = align_up(off + pairs * nb * 4, 256);
-  off = align_up(off + pairs * K_max * 4, 256);  // down projection result
-  return off + 256;
+  // CUDA-core path: int8 activations in and SwiGLU out, down result.
+  int64_t q8 = 0;
+  q8 = align_up(q8 + pairs * nb * 32, 256);
+  q8 = align_up(q8 + pairs * nb * 4, 256);
+  q8 = align_up(q8 + pairs * nb * 32, 256);
+  q8 = align_up(q8 + pairs * nb * 4, 256);
+  q8 = align_up(q8 + pairs * K_max * 4, 256);
+  // Tensor-core path: activation terms in and SwiGLU out, down result, flag.
+  int64_t tcb = 0;
+  tcb = align_up(tcb + tc_act_bytes(nb, pairs), 256);
+  tcb = align_up(tcb + tc_act_bytes(nb, pairs), 256);
+  tcb = align_up(tcb + pairs * K_max * 4, 256);
+  tcb += 256;
+  return (q8 > tcb ? q8 : tcb) + 256;
+}
+
+extern "C" int msb_set_option(int option, int value) {
+  if (option == MSB_OPT_MXFP4_PATH) {
+    MSB_CHECK_ARG(value == 0 || value == 1, "msb_set_option: MXFP4 path must be 0 or 1");
+    g_mxfp4_path = value;
+    return MSB_OK;
+  }
+  return fail(MSB_ERR_INVALID, "msb_set_option: unknown option %d", option);
 }
 
 extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, int64_t b_ne1,
@@ -420,6 +450,24 @@ extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   int64_t off = 0;
+  const int64_t pairs = int64_t(n_tok) * top_k;
+  const int max_active = int(pairs < pool->n_slot + 1 ? pairs : pool->n_slot + 1);
+  if (g_mxfp4_path == 0 && tc_supported(pool)) {
+    // Tensor cores: activation terms per pair (grouped order), then one
+    // projection writing res directly.
+    uint8_t *act = ws;
+    int *err = reinterpret_cast<int *>(ws + align_up(tc_act_bytes(pool->nb, pairs), 256));
+    MSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
+    const size_t es = b_type == MSB_TYPE_BF16 ? 2 : 4;
+    (void)es;
+    if (int rc = tc_act_terms(b_dev, b_type, b_ne1, b_nb1, b_nb2, top_k, route->rows, pairs,
+                              pool->nb, act, st))
+      return rc;
+    const int64_t row0[2] = {0, 0};
+    const msb_pool_s *pools[2] = {pool, pool};
+    return tc_projection(pools, 1, row0, pool->N, route, pairs, act, res_dev, nullptr, nullptr, err,
+                         max_active, st);
+  }
   const int64_t n_rows = int64_t(n_tok) * b_ne1;
   ActQ8 in = carve_act(ws, &off, n_rows, pool->nb);
   if (int rc = quantize_act(b_dev, b_type, b_ne1, b_nb1, b_nb2, n_rows, in, st)) return rc;
@@ -434,8 +482,6 @@ extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, in
   g.b_ne1 = int32_t(b_ne1);
   g.in = in;
   g.res = res_dev;
-  const int64_t pairs = int64_t(n_tok) * top_k;
-  const int max_active = int(pairs < pool->n_slot + 1 ? pairs : pool->n_slot + 1);
   return launch_gemv(pool->wtype, false, g, max_active, st);
 }
 
@@ -465,6 +511,46 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   const int64_t pairs = int64_t(n_tok) * top_k;
+  const int max_active_tc = int(pairs < gate->n_slot + 1 ? pairs : gate->n_slot + 1);
+  if (g_mxfp4_path == 0 && tc_supported(gate) && tc_supported(up) && tc_supported(down) &&
+      n_ff % 64 == 0 && up_row0 % 128 == 0) {
+    // Tensor cores: x terms per pair -> fused gate/up + SwiGLU writing the
+    // down projection's terms -> down projection -> weighted combine.
+    int64_t o = 0;
+    uint8_t *xa = ws + o;
+    o = align_up(o + tc_act_bytes(gate->nb, pairs), 256);
+    uint8_t *ha = ws + o;
+    o = align_up(o + tc_act_bytes(n_ff / 32, pairs), 256);
+    float *rd = reinterpret_cast<float *>(ws + o);
+    o = align_up(o + pairs * down->N * 4, 256);
+    int *err = reinterpret_cast<int *>(ws + o);
+    MSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
+    if (int rc = tc_act_terms(x_dev, x_type, 1, x_nb1, x_nb1, top_k, route->rows, pairs, gate->nb,
+                              xa, st))
+      return rc;
+    const int64_t rows_gu[2] = {0, up_row0};
+    const msb_pool_s *gu_pools[2] = {gate, up};
+    const bool timed = g_gate_up_start && g_gate_up_stop;
+    if (timed) MSB_CUDA_TRY(cudaEventRecord(g_gate_up_start, st));
+    if (int rc = tc_projection(gu_pools, 2, rows_gu, n_ff, route, pairs, xa, nullptr, ha, act_dev,
+                               err, max_active_tc, st))
+      return rc;
+    if (timed) {
+      MSB_CUDA_TRY(cudaEventRecord(g_gate_up_stop, st));
+      g_gate_up_start = g_gate_up_stop = nullptr;
+    }
+    const int64_t rows_dn[2] = {0, 0};
+    const msb_pool_s *dn_pools[2] = {down, down};
+    if (int rc = tc_projection(dn_pools, 1, rows_dn, down->N, route, pairs, ha, rd, nullptr, nullptr,
+                               err, max_active_tc, st))
+      return rc;
+    const int64_t total = down->N * n_tok;
+    combine_kernel<<<unsigned((total + 255) / 256), 256, 0, st>>>(rd, w_dev, top_k, down->N, n_tok,
+                                                                  y_dev);
+    count_launch();
+    MSB_CUDA_TRY(cudaGetLastError());
+    return MSB_OK;
+  }
   int64_t off = 0;
   ActQ8 xq = carve_act(ws, &off, n_tok, gate->nb);
   ActQ8 hq = carve_act(ws, &off, pairs, n_ff / 32);

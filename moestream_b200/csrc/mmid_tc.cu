@@ -1,0 +1,433 @@
+// Tensor-core mul_mat_id for MXFP4 slot pools (tcgen05, kind::mxf4).
+//
+// Weights are consumed as stored: e2m1 nibbles with one e8m0 scale per 32
+// elements are exactly the tensor core's block-scaled FP4 format, so no
+// weight is decoded by the CUDA cores. ggml's nibble order (byte j = elements
+// j and j+16) is a fixed permutation of K inside each 32-element block; the
+// activations are written with the same permutation, so every product pairs
+// the right elements and the block scales line up.
+//
+// Activations are split into kTerms e2m1 terms per 32-element block, each
+// with its own power-of-two scale (a residual expansion: term t encodes what
+// terms 0..t-1 left over). Four terms are ~30x closer to exact than ggml's
+// int8 (q8_0) activations; each term is one more MMA, which decode has to
+// spare. D[row][pair] accumulates in f32 in tensor memory.
+//
+// One CTA (128 threads) computes a 128-row tile of one slot for up to 32 of
+// its (token, k) pairs per pass:
+//   warp 0, lane 0 : producer -- per stage, one tiled TMA copy per weight
+//                    view (128 rows x 4 blocks, 8 KB), one 512-byte bulk
+//                    copy of each view's scale-factor chunk, one tiled TMA
+//                    copy of the pairs' activation terms (4 terms x 4 blocks
+//                    x 32 pairs) and one of their scales, into a 4-stage
+//                    shared-memory ring;
+//   warp 1, lane 0 : copies each stage's scale factors into tensor memory
+//                    (tcgen05.cp) and issues the MMAs (M=128, N=32, K=64);
+//                    tcgen05.commit frees the stage;
+//   all 4 warps    : epilogue -- each warp reads its 32 TMEM lanes (rows).
+// With two views (gate and up) the epilogue applies SwiGLU and writes the
+// down projection's activation terms directly.
+// Every mbarrier wait is bounded; a wait that gives up sets *err and the CTA
+// stops issuing work and releases its tensor memory.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "msb_internal.h"
+#include "pool.cuh"
+#include "quant.cuh"
+#include "sm100.cuh"
+
+namespace msb {
+namespace tc {
+
+constexpr int kTerms = 4;        // e2m1 terms per activation block
+constexpr int kPairs = 32;       // MMA N: (token, k) pairs per pass
+constexpr int kStages = 4;       // shared-memory ring depth
+constexpr int kChunk = 4;        // 32-element blocks per stage (two K=64 MMAs)
+constexpr int kThreads = 128;
+
+template <int NV>
+struct Cfg {
+  static constexpr int kA = NV * kChunk * 2048;          // 128 rows x 16 B per block
+  static constexpr int kSFA = NV * 512;
+  static constexpr int kB = kTerms * kChunk * kPairs * 16;
+  static constexpr int kSFB = kTerms * 512;
+  static constexpr int kStage = kA + kSFA + kB + kSFB;
+  static constexpr int kBarOff = kStages * kStage;
+  static constexpr int kSmem = kBarOff + 256;
+  static constexpr int kSfCols = (NV + kTerms) * 4;      // TMEM columns per stage
+  static constexpr int kSfBase = NV * kPairs;            // after the accumulators
+  static constexpr int kTmemCols = NV == 2 ? 256 : 128;
+  static_assert(kSfBase + kStages * kSfCols <= kTmemCols, "tensor memory map");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
+};
+
+struct Args {
+  CUtensorMap tm_w[2];       // each view's pool: (8 B x 2 x rows, blocks, slots)
+  CUtensorMap tm_aq;         // activation terms: (8 B x 2 x pairs, blocks, terms)
+  CUtensorMap tm_asf;        // their scales: (8 B x 2 x pairs, chunks, terms)
+  const uint8_t *pool[2];    // slot 0 of each view's pool
+  int64_t slot_stride[2], N[2];
+  int64_t nb;                // blocks per row (K / 32), same for both views
+  int64_t row0[2];           // first row of each view, multiple of 128
+  int64_t n_out;             // rows per view
+  int tiles;                 // ceil(n_out / 128)
+  const int32_t *counts, *offsets, *rows, *active;
+  int32_t zero_slot;
+  const uint8_t *aq, *asf;   // activation terms (grouped pair order)
+  int64_t a_rows;            // rows of the activation buffers (= pairs)
+  float *res;                // one view: res[pair * n_out + n]
+  uint8_t *oq, *osf;         // two views: terms of silu(gate) * up
+  int64_t o_nb;              // n_out / 32
+  float *act;                // two views, optional: f32 silu(gate) * up
+  int *err;
+};
+
+__device__ __forceinline__ int64_t a4_q_off(int t, int64_t b, int64_t nb, int64_t rows, int64_t r) {
+  return ((int64_t(t) * nb + b) * rows + r) * 16;
+}
+__device__ __forceinline__ int64_t a4_sf_off(int t, int64_t c, int64_t nc, int64_t rows, int64_t r) {
+  return ((int64_t(t) * nc + c) * rows + r) * 16;
+}
+
+// Splits the block held by the warp (lane j = element j) into kTerms e2m1
+// terms and writes, per term, its 16 packed bytes (byte e = code(e) |
+// code(e + 16) << 4) and its scale byte k + 127.
+__device__ __forceinline__ void warp_e2m1_terms(float r, int lane, uint8_t *q_t0, int64_t q_step,
+                                                uint8_t *sf_t0, int64_t sf_step) {
+#pragma unroll
+  for (int t = 0; t < kTerms; ++t) {
+    float amax = fabsf(r);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    int k = -127;
+    if (amax > 0.f) {
+      int ex;
+      const float m = frexpf(amax, &ex);
+      k = m > 0.75f ? ex - 2 : ex - 3;
+    }
+    const bool skip = k < -126;
+    int code = 0, neg = 0;
+    if (!skip) {
+      const float v = fabsf(r) * __int_as_float((127 - k) << 23);  // |r| / 2^k, exact
+      code = (v >= 0.25f) + (v >= 0.75f) + (v >= 1.25f) + (v >= 1.75f) + (v >= 2.5f) +
+             (v >= 3.5f) + (v >= 5.f);
+      neg = (r < 0.f) && code > 0;
+      const float mag = code < 5 ? 0.5f * code : (code == 5 ? 3.f : (code == 6 ? 4.f : 6.f));
+      const float q = mag * __int_as_float((k + 127) << 23);        // exact
+      r = neg ? r + q : r - q;                                      // exact (Sterbenz)
+    }
+    const int nib = code | (neg << 3);
+    const int hi = __shfl_down_sync(0xffffffffu, nib, 16);
+    if (lane < 16) q_t0[t * q_step + lane] = uint8_t(nib | (hi << 4));
+    if (lane == 0) sf_t0[t * sf_step] = skip ? uint8_t(0) : uint8_t(k > 127 ? 254 : k + 127);
+  }
+}
+
+// Activations of every pair in grouped order into the term layout:
+// q [kTerms][nb][rows][16 B], sf [kTerms][ceil(nb/4)][rows][16 B] (byte b%4).
+template <typename T>
+__global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t nb1, int64_t nb2,
+                                                        int32_t ne1, int32_t top_k,
+                                                        const int32_t *rows, int64_t n_pairs,
+                                                        int64_t nb, uint8_t *q, uint8_t *sf) {
+  const int lane = threadIdx.x & 31;
+  const int64_t item = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (item >= n_pairs * nb) return;
+  const int64_t pos = item / nb, blk = item % nb;
+  const int64_t pair = rows[pos];
+  const int64_t t = pair / top_k, k1 = (pair % top_k) % ne1;
+  const char *p = b + t * nb2 + k1 * nb1 + (blk * 32 + lane) * int64_t(sizeof(T));
+  float v;
+  if constexpr (sizeof(T) == 4) v = *reinterpret_cast<const float *>(p);
+  else v = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(p));
+  const int64_t nc = (nb + 3) / 4;
+  warp_e2m1_terms(v, lane, q + a4_q_off(0, blk, nb, n_pairs, pos), nb * n_pairs * 16,
+                  sf + a4_sf_off(0, blk / 4, nc, n_pairs, pos) + (blk & 3), nc * n_pairs * 16);
+}
+
+template <int NV>
+__global__ void __launch_bounds__(kThreads) tc_kernel(const __grid_constant__ Args a) {
+  using C = Cfg<NV>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int ai = blockIdx.x / a.tiles;
+  const int tile = blockIdx.x - ai * a.tiles;
+  if (ai >= a.active[0]) return;
+  const int slot = a.active[1 + ai];
+  const int c_total = a.counts[slot];
+  const int64_t pos0 = a.offsets[slot];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n0 = int64_t(tile) * 128;
+  const int64_t n = n0 + threadIdx.x;     // epilogue row
+  const bool valid = n < a.n_out;
+  const int64_t nc_in = (a.nb + 3) / 4;
+
+  if (slot == a.zero_slot) {
+    // Every weight of the zero slot is 0: write the exact result directly.
+    for (int j = 0; j < c_total; ++j) {
+      const int64_t pair = a.rows[pos0 + j];
+      if constexpr (NV == 1) {
+        if (valid) a.res[pair * a.n_out + n] = 0.f;
+      } else {
+        if (a.act && valid) a.act[pair * a.n_out + n] = 0.f;
+        const int64_t blk = (n0 >> 5) + warp;
+        if (blk < a.o_nb)
+          warp_e2m1_terms(0.f, lane, a.oq + a4_q_off(0, blk, a.o_nb, a.a_rows, pos0 + j),
+                          a.o_nb * a.a_rows * 16,
+                          a.osf + a4_sf_off(0, blk / 4, (a.o_nb + 3) / 4, a.a_rows, pos0 + j) + (blk & 3),
+                          ((a.o_nb + 3) / 4) * a.a_rows * 16);
+      }
+    }
+    return;
+  }
+
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
+  uint64_t *empty = full + kStages;
+  uint64_t *done = empty + kStages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    sm100::mbar_init(done, 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tmem_slot, C::kTmemCols);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int64_t n_chunks = (a.nb + kChunk - 1) / kChunk;
+  uint32_t it_prod = 0, it_mma = 0;
+  int pass = 0;
+
+  for (int g0 = 0; g0 < c_total; g0 += kPairs, ++pass) {
+    const int cc = min(kPairs, c_total - g0);
+    const int64_t pos = pos0 + g0;
+    if (warp == 0 && lane == 0) {
+      // ---- producer ----
+      for (int64_t i = 0; i < n_chunks && !*(volatile int *)abort_flag; ++i, ++it_prod) {
+        const int s = it_prod % kStages;
+        const uint32_t ph = (it_prod / kStages) & 1;
+        if (!sm100::mbar_wait_bounded(&empty[s], ph ^ 1)) {
+          atomicOr(a.err, 1);
+          *(volatile int *)abort_flag = 1;
+          break;
+        }
+        uint8_t *st = smem + s * C::kStage;
+        uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
+        const int64_t b0 = i * kChunk;
+        const int kbn = int(a.nb - b0 < kChunk ? a.nb - b0 : kChunk);
+        // Full boxes are counted (rows or blocks outside the tensors arrive
+        // as zeros), so the byte count is the same for every stage.
+        constexpr uint32_t bytes = uint32_t(C::kStage);
+        (void)kbn;
+        sm100::mbar_expect_tx(&full[s], bytes);
+        for (int v = 0; v < NV; ++v) {
+          const int64_t r0 = a.row0[v] + n0;
+          sm100::tma_3d(sA + v * kChunk * 2048, &a.tm_w[v], int(r0) * 2, int(b0), slot, &full[s]);
+          const uint8_t *slot_base = a.pool[v] + int64_t(slot) * a.slot_stride[v];
+          const uint8_t *sf_base = slot_base + a.nb * a.N[v] * 16;
+          const int64_t sf_tiles = (a.N[v] + 127) / 128;
+          sm100::bulk_g2s(sSFA + v * 512, sf_base + (i * sf_tiles + (r0 >> 7)) * 512, 512, &full[s]);
+        }
+        sm100::tma_3d(sB, &a.tm_aq, int(pos) * 2, int(b0), 0, &full[s]);
+        sm100::tma_3d(sSFB, &a.tm_asf, int(pos) * 2, int(i), 0, &full[s]);
+      }
+    } else if (warp == 1 && lane == 0) {
+      // ---- scale-factor copies and MMA issue ----
+      sm100::tc_fence_after();
+      bool first = true;
+      for (int64_t i = 0; i < n_chunks; ++i, ++it_mma) {
+        const int s = it_mma % kStages;
+        const uint32_t ph = (it_mma / kStages) & 1;
+        if (*(volatile int *)abort_flag || !sm100::mbar_wait_bounded(&full[s], ph)) {
+          atomicOr(a.err, 2);
+          *(volatile int *)abort_flag = 1;
+          break;
+        }
+        const uint8_t *st = smem + s * C::kStage;
+        const uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
+        const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols;
+        for (int v = 0; v < NV; ++v)
+          sm100::tmem_cp_32x128b_x4(sf_col + v * 4, sm100::smem_desc(sm100::smem_u32(sSFA + v * 512), 0, 128));
+        for (int t = 0; t < kTerms; ++t)
+          sm100::tmem_cp_32x128b_x4(sf_col + (NV + t) * 4,
+                                    sm100::smem_desc(sm100::smem_u32(sSFB + t * 512), 0, 128));
+        const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
+        for (int j = 0; j < kbn / 2; ++j) {
+          for (int v = 0; v < NV; ++v) {
+            const uint64_t adesc =
+                sm100::smem_desc(sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
+            for (int t = 0; t < kTerms; ++t) {
+              const uint64_t bdesc = sm100::smem_desc(
+                  sm100::smem_u32(sB + (t * kChunk + 2 * j) * (kPairs * 16)), kPairs * 16, 128);
+              const uint32_t sel = uint32_t(2 * j);
+              sm100::mma_mxf4(tmem + v * kPairs, adesc, bdesc, sm100::idesc_mxf4(kPairs, sel, sel),
+                              (sf_col + v * 4) | (sel << 30), (sf_col + (NV + t) * 4) | (sel << 30),
+                              (first && t == 0) ? 0u : 1u);
+            }
+          }
+          first = false;
+        }
+        sm100::tc_commit(&empty[s]);
+      }
+      sm100::tc_commit(done);
+    }
+    __syncwarp();
+
+    // ---- epilogue ----
+    if (!sm100::mbar_wait_bounded(done, uint32_t(pass & 1))) {
+      atomicOr(a.err, 4);
+      *(volatile int *)abort_flag = 1;
+    }
+    sm100::tc_fence_after();
+    const bool ok = !*(volatile int *)abort_flag;
+    uint32_t dg[32], du[32];
+    const uint32_t lane_addr = uint32_t(warp * 32) << 16;
+    sm100::tmem_ld_32cols(tmem + lane_addr, dg);
+    if constexpr (NV == 2) sm100::tmem_ld_32cols(tmem + lane_addr + kPairs, du);
+    sm100::tmem_ld_wait();
+    if (ok) {
+#pragma unroll
+      for (int j = 0; j < kPairs; ++j) {
+        if (j >= cc) break;
+        const int64_t pair = a.rows[pos + j];
+        const float g = __uint_as_float(dg[j]);
+        if constexpr (NV == 1) {
+          if (valid) a.res[pair * a.n_out + n] = g;
+        } else {
+          const float u = __uint_as_float(du[j]);
+          const float h = valid ? g / (1.f + expf(-g)) * u : 0.f;
+          if (a.act && valid) a.act[pair * a.n_out + n] = h;
+          const int64_t blk = (n0 >> 5) + warp;
+          if (blk < a.o_nb) {
+            const int64_t onc = (a.o_nb + 3) / 4;
+            warp_e2m1_terms(h, lane, a.oq + a4_q_off(0, blk, a.o_nb, a.a_rows, pos + j),
+                            a.o_nb * a.a_rows * 16,
+                            a.osf + a4_sf_off(0, blk / 4, onc, a.a_rows, pos + j) + (blk & 3),
+                            onc * a.a_rows * 16);
+          }
+        }
+      }
+    }
+    // The next pass overwrites the accumulators: every TMEM read is done.
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (*(volatile int *)abort_flag) break;
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+}  // namespace tc
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+int64_t tc_act_bytes(int64_t nb, int64_t rows) {
+  return int64_t(tc::kTerms) * (nb + (nb + 3) / 4) * rows * 16;
+}
+
+int tc_supported(const msb_pool_s *p) {
+  return p->wtype == MSB_TYPE_MXFP4 && p->nb % 2 == 0;
+}
+
+int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb2, int32_t top_k,
+                 const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st) {
+  if (n_pairs == 0) return MSB_OK;
+  uint8_t *q = ws, *sf = ws + int64_t(tc::kTerms) * nb * n_pairs * 16;
+  const int64_t grid = (n_pairs * nb + 7) / 8;
+  const char *p = static_cast<const char *>(b);
+  if (b_type == MSB_TYPE_F32)
+    tc::act_terms_kernel<float><<<unsigned(grid), 256, 0, st>>>(p, nb1, nb2, int32_t(ne1), top_k,
+                                                                rows, n_pairs, nb, q, sf);
+  else if (b_type == MSB_TYPE_BF16)
+    tc::act_terms_kernel<__nv_bfloat16><<<unsigned(grid), 256, 0, st>>>(
+        p, nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, sf);
+  else
+    return fail(MSB_ERR_INVALID, "activation type %d is not F32 or BF16", b_type);
+  count_launch();
+  MSB_CUDA_TRY(cudaGetLastError());
+  return MSB_OK;
+}
+
+template <int NV>
+static int launch_tc_t(const tc::Args &a, int max_active, cudaStream_t st) {
+  using C = tc::Cfg<NV>;
+  MSB_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::kSmem));
+  const int64_t grid = int64_t(max_active) * a.tiles;
+  if (grid == 0) return MSB_OK;
+  tc::tc_kernel<NV><<<unsigned(grid), tc::kThreads, C::kSmem, st>>>(a);
+  count_launch();
+  MSB_CUDA_TRY(cudaGetLastError());
+  return MSB_OK;
+}
+
+// One projection over rows [row0[v], row0[v] + n_out) of each view's pool
+// (pools[1] is used only when nv == 2). act_in: the pairs' activation terms
+// (tc_act_terms); nv == 2 writes the terms of silu(view 0) * view 1 to
+// act_out, nv == 1 writes res.
+int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
+                  const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
+                  uint8_t *act_out, float *act_f32, int *err, int max_active, cudaStream_t st) {
+  const msb_pool_s *pool = pools[0];
+  tc::Args a{};
+  for (int v = 0; v < 2; ++v) {
+    const msb_pool_s *p = pools[nv == 2 ? v : 0];
+    if (!p->has_tmap) return fail(MSB_ERR_UNSUPPORTED, "tensor-core path: pool has no tensor map");
+    a.tm_w[v] = p->tmap_w;
+    a.pool[v] = p->data;
+    a.slot_stride[v] = p->slot_stride;
+    a.N[v] = p->N;
+    a.row0[v] = nv == 2 ? row0[v] : row0[0];
+  }
+  a.nb = pool->nb;
+  a.n_out = n_out;
+  a.tiles = int((n_out + 127) / 128);
+  a.counts = route->counts;
+  a.offsets = route->offsets;
+  a.rows = route->rows;
+  a.active = route->active;
+  a.zero_slot = pool->n_slot;
+  a.aq = act_in;
+  a.asf = act_in + int64_t(tc::kTerms) * pool->nb * n_pairs * 16;
+  a.a_rows = n_pairs;
+  a.res = res;
+  a.oq = act_out;
+  a.o_nb = n_out / 32;
+  a.osf = act_out ? act_out + int64_t(tc::kTerms) * a.o_nb * n_pairs * 16 : nullptr;
+  a.act = act_f32;
+  a.err = err;
+  {
+    // One 16-byte row per pair = two 8-byte elements; a box line is the 32
+    // pairs of one (term, block) -- 512 contiguous bytes.
+    const uint64_t nc = uint64_t((pool->nb + 3) / 4);
+    const uint64_t dq[3] = {uint64_t(n_pairs) * 2, uint64_t(pool->nb), uint64_t(tc::kTerms)};
+    const uint64_t sq[2] = {uint64_t(n_pairs) * 16, uint64_t(pool->nb * n_pairs) * 16};
+    const uint32_t bq[3] = {uint32_t(tc::kPairs) * 2, uint32_t(tc::kChunk), uint32_t(tc::kTerms)};
+    const uint64_t df[3] = {uint64_t(n_pairs) * 2, nc, uint64_t(tc::kTerms)};
+    const uint64_t sf[2] = {uint64_t(n_pairs) * 16, nc * uint64_t(n_pairs) * 16};
+    const uint32_t bf[3] = {uint32_t(tc::kPairs) * 2, 1, uint32_t(tc::kTerms)};
+    if (!encode_tmap_u64_3d(&a.tm_aq, a.aq, dq, sq, bq) ||
+        !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sf, bf))
+      return fail(MSB_ERR_CUDA, "tensor-core path: activation tensor maps could not be encoded");
+  }
+  return nv == 2 ? launch_tc_t<2>(a, max_active, st) : launch_tc_t<1>(a, max_active, st);
+}
+
+}  // namespace msb

@@ -46,6 +46,7 @@ __global__ void __launch_bounds__(256) repack_to_device_kernel(
   __syncthreads();
   uint8_t *dst = pool_base + int64_t(slots[ex]) * slot_stride;
   uint8_t *dst_scale = dst + nb * N * 16;
+  const bool mx = scale_bytes == 1;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (lane >= rows) return;
   const int64_t n = n0 + lane;
@@ -57,7 +58,7 @@ __global__ void __launch_bounds__(256) repack_to_device_kernel(
     uint4 v;
     memcpy(&v, q, 16);
     *reinterpret_cast<uint4 *>(dst + (b * N + n) * 16) = v;
-    uint8_t *sd = dst_scale + (b * N + n) * scale_bytes;
+    uint8_t *sd = dst_scale + scale_offset(mx, b, n, N);
     for (int j = 0; j < scale_bytes; ++j) sd[j] = blk[j];
   }
 }
@@ -70,7 +71,7 @@ __global__ void __launch_bounds__(256) repack_to_ggml_kernel(
   if (i >= N * nb) return;
   const int64_t n = i / nb, b = i % nb;
   const uint8_t *qs = slot_base + (b * N + n) * 16;
-  const uint8_t *sc = slot_base + nb * N * 16 + (b * N + n) * scale_bytes;
+  const uint8_t *sc = slot_base + nb * N * 16 + scale_offset(scale_bytes == 1, b, n, N);
   uint8_t *o = dst + (n * nb + b) * block_bytes;
   for (int j = 0; j < scale_bytes; ++j) o[j] = sc[j];
   for (int j = 0; j < 16; ++j) o[scale_bytes + j] = qs[j];
@@ -179,6 +180,34 @@ __global__ void quantize_iq4nl_kernel(const float *src, uint8_t *dst,
 
 }  // namespace msb
 
+namespace msb {
+
+bool encode_tmap_u64_3d(CUtensorMap *map, const void *base, const uint64_t dims[3],
+                        const uint64_t strides[2], const uint32_t box[3]) {
+  typedef CUresult (*EncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                               const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                               const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                               CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn fn = nullptr;
+  static bool looked = false;
+  if (!looked) {
+    looked = true;
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(ptr);
+  }
+  if (!fn) return false;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void *>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace msb
+
 using namespace msb;
 
 static int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
@@ -201,7 +230,7 @@ extern "C" int msb_pool_create(int wtype, int64_t K, int64_t N, int32_t n_slot,
   p->block_bytes = f.block_bytes;
   p->scale_bytes = f.scale_bytes;
   p->expert_bytes = p->nb * f.block_bytes * N;
-  p->slot_stride = round_up(p->expert_bytes, 256);
+  p->slot_stride = round_up(p->nb * N * 16 + scale_region_bytes(wtype == MSB_TYPE_MXFP4, p->nb, N), 256);
   p->max_fill = max_fill_batch;
   cudaGetDevice(&p->device);
   const int64_t slab = p->slot_stride * (int64_t(n_slot) + 1);
@@ -214,6 +243,12 @@ extern "C" int msb_pool_create(int wtype, int64_t K, int64_t N, int32_t n_slot,
   if (e != cudaSuccess) { cudaFree(p->stage_meta); cudaFree(p->data); delete p; return fail(MSB_ERR_NOMEM, "msb_pool_create: pinned metadata failed: %s", cudaGetErrorString(e)); }
   e = cudaEventCreateWithFlags(&p->meta_free, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaMemset(p->data, 0, slab);  // every slot starts as zeros
+  if (e == cudaSuccess && wtype == MSB_TYPE_MXFP4) {
+    const uint64_t dims[3] = {uint64_t(N) * 2, uint64_t(p->nb), uint64_t(n_slot) + 1};
+    const uint64_t strides[2] = {uint64_t(N) * 16, uint64_t(p->slot_stride)};
+    const uint32_t box[3] = {256, 4, 1};
+    p->has_tmap = encode_tmap_u64_3d(&p->tmap_w, p->data, dims, strides, box);
+  }
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) { msb_pool_destroy(p); return fail(MSB_ERR_CUDA, "msb_pool_create: init failed: %s", cudaGetErrorString(e)); }
   *out = p;

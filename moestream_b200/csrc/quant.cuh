@@ -11,9 +11,16 @@
 //
 // Device pool layout (this library's, per slot, written by the fill path):
 //   qs    : [K/32][N][16 B]   block-major, rows of one block contiguous
-//   scale : [K/32][N]         1 byte (e8m0) or 2 bytes (fp16) each
+//   scale : IQ4_NL: fp16 [K/32][N];
+//           MXFP4 : e8m0 bytes in 512-byte chunks, one per (4 blocks, 128
+//           rows): chunk (b/4, n/128) holds row r = n%128 of block b at
+//           byte (r%32)*16 + (r/32)*4 + b%4. That is the order the tensor
+//           core's scale-factor copy (tcgen05.cp 32x128b, 4-way broadcast)
+//           takes, so a chunk moves from the pool to tensor memory as is.
 // With lane = row, a warp reading one block column loads 32 x 16 contiguous
-// bytes, so every weight load in the matmul is a coalesced 128-bit load.
+// bytes, so every weight load in the CUDA-core matmul is a coalesced 128-bit
+// load; 128 rows of one block column (2 KB) are one bulk copy for the
+// tensor-core matmul.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -54,6 +61,19 @@ __device__ __forceinline__ void decode_nibbles(uint32_t q, const Codebook &cb,
   a = __byte_perm(cb.w0, cb.w1, idx_hi);
   b = __byte_perm(cb.w2, cb.w3, idx_hi);
   hi = __byte_perm(a, b, pick >> 16);
+}
+
+// Byte offset of the scale of (block b, row n) within a slot's scale region
+// (N = rows stored per slot).
+__host__ __device__ __forceinline__ int64_t scale_offset(bool mx, int64_t b, int64_t n,
+                                                         int64_t N) {
+  if (!mx) return (b * N + n) * 2;
+  const int64_t r = n & 127;
+  return ((b >> 2) * ((N + 127) >> 7) + (n >> 7)) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3);
+}
+
+__host__ __device__ __forceinline__ int64_t scale_region_bytes(bool mx, int64_t nb, int64_t N) {
+  return mx ? ((nb + 3) / 4) * ((N + 127) / 128) * 512 : nb * N * 2;
 }
 
 // Byte position of element j (0..31) of a block in the interleaved order.

@@ -7,8 +7,8 @@ import ctypes
 
 import torch
 
-from ._lib import (TYPE_BF16, TYPE_F32, TYPE_IQ4_NL, TYPE_MXFP4, PoolInfo, Route, c_vp,
-                   check, lib)
+from ._lib import (OPT_MXFP4_PATH, TYPE_BF16, TYPE_F32, TYPE_IQ4_NL, TYPE_MXFP4, PoolInfo,
+                   Route, c_vp, check, lib)
 
 WEIGHT_TYPES = {"iq4_nl": TYPE_IQ4_NL, "mxfp4": TYPE_MXFP4}
 _ACT_TYPES = {torch.float32: TYPE_F32, torch.bfloat16: TYPE_BF16}
@@ -21,6 +21,17 @@ def _stream(stream=None):
 
 def _ptr(t):
     return c_vp(t.data_ptr()) if t is not None else c_vp(0)
+
+
+def set_mxfp4_path(path):
+    """'tc' (tensor cores where shapes allow, the default) or 'q8' (CUDA cores,
+    int8 activations)."""
+    check(lib().msb_set_option(OPT_MXFP4_PATH, {"tc": 0, "q8": 1}[path]))
+
+
+def tc_eligible(wtype, K):
+    """Whether an MXFP4 projection with K inputs runs on the tensor cores."""
+    return WEIGHT_TYPES.get(wtype, wtype) == TYPE_MXFP4 and K % 64 == 0
 
 
 def expert_bytes(wtype, K, N):

@@ -27,6 +27,11 @@
  *     "q8" (ggml's CPU vec_dot form: activations quantized per 32-block to
  *     int8 with d = amax/127 stored as fp16, int32 dot per block, f32
  *     accumulation of d_w * d_a * isum in block order).
+ *     A third mode, "e2m1x4", is the activation form of this library's
+ *     tensor-core path for MXFP4: each 32-element block of activations is
+ *     split into 4 terms, each 32 e2m1 codes with a power-of-two scale; the
+ *     sum of the terms replaces the activations, and the products accumulate
+ *     in f64.
  *   - MoE FFN: research/spikes/s1_real_expert_stream/main.c:186-209 and
  *     research/spikes/s4_sweep_math/main.c:89-92 (SwiGLU, then down, then the
  *     router-weighted sum over k).
@@ -238,6 +243,55 @@ void orc_quantize_q8(const float *x, int64_t K, int8_t *q, float *d_out) {
   }
 }
 
+/* ---- e2m1 activation terms (tensor-core form) -------------------------- */
+static const float E2M1_MAG[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+
+/* Nearest e2m1 magnitude code of v in [0, 6], ties upward. */
+static int e2m1_code(float v) {
+  return (v >= 0.25f) + (v >= 0.75f) + (v >= 1.25f) + (v >= 1.75f) + (v >= 2.5f) +
+         (v >= 3.5f) + (v >= 5.f);
+}
+
+/* Splits each 32-element block of x (n elements) into `terms` e2m1 terms: per
+ * term, k = the smallest integer with max|r| <= 6 * 2^k (r the remaining
+ * residual; k taken exactly from the float's exponent), codes = nearest e2m1
+ * of |r| / 2^k with r's sign, r -= code * 2^k (exact). A term whose k would
+ * fall below -126 is skipped (contributes 0). Writes the sum of the terms to
+ * approx, and optionally the codes (nibbles, sign in bit 3) and the scale
+ * bytes k + 127 per (term, block). */
+void orc_e2m1_split(const float *x, int64_t n, int terms, float *approx,
+                    uint8_t *codes, uint8_t *exps) {
+  const int64_t nb = n / 32;
+  for (int64_t b = 0; b < nb; ++b) {
+    float r[32];
+    for (int j = 0; j < 32; ++j) r[j] = x[b * 32 + j];
+    for (int t = 0; t < terms; ++t) {
+      float amax = 0.f;
+      for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(r[j]));
+      int k = -127;
+      if (amax > 0.f) {
+        int ex;
+        const float m = frexpf(amax, &ex);
+        k = m > 0.75f ? ex - 2 : ex - 3;
+      }
+      const int skip = k < -126;
+      if (exps) exps[t * nb + b] = skip ? 0 : (uint8_t)(k > 127 ? 254 : k + 127);
+      for (int j = 0; j < 32; ++j) {
+        int code = 0, neg = 0;
+        if (!skip) {
+          const float v = fabsf(r[j]) * ldexpf(1.f, -k);
+          code = e2m1_code(v);
+          neg = r[j] < 0.f && code > 0;
+          const float q = ldexpf(E2M1_MAG[code], k);
+          r[j] = neg ? r[j] + q : r[j] - q;
+        }
+        if (codes) codes[(t * nb + b) * 32 + j] = (uint8_t)(code | (neg << 3));
+      }
+    }
+    for (int j = 0; j < 32; ++j) approx[b * 32 + j] = x[b * 32 + j] - r[j];
+  }
+}
+
 /* ---- mul_mat_id -------------------------------------------------------- */
 typedef struct {
   int type, mode;
@@ -251,6 +305,7 @@ typedef struct {
   int64_t lo, hi; /* range of (pair, n) items */
   const int8_t *bq; /* q8 mode: quantized activations [T*b_ne1][K] */
   const float *bd;  /*           scales [T*b_ne1][K/32]               */
+  const float *bx;  /* e2m1x4 mode: activations as the sum of 4 terms  */
 } mm_job;
 
 static void *mm_worker(void *arg) {
@@ -263,9 +318,9 @@ static void *mm_worker(void *arg) {
     const int32_t slot = j->ids[pair];
     const uint8_t *row = j->as + slot * j->slot_bytes + n * nb * bb;
     const int64_t arow = t * j->b_ne1 + (k % j->b_ne1);
-    if (j->mode == 0) {
+    if (j->mode == 0 || j->mode == 2) {
       orc_dequant_row(j->type, row, wrow, j->K);
-      const float *a = j->b + arow * j->K;
+      const float *a = (j->mode == 2 ? j->bx : j->b) + arow * j->K;
       double s = 0.0;
       for (int64_t i = 0; i < j->K; ++i) s += (double)wrow[i] * (double)a[i];
       j->res[pair * j->N + n] = (float)s;
@@ -316,10 +371,14 @@ int orc_mul_mat_id(int type, const uint8_t *as, int64_t K, int64_t N, int64_t n_
   int8_t *bq = NULL;
   float *bd = NULL;
   const int64_t rows = (int64_t)T * b_ne1;
+  float *bx = NULL;
   if (mode == 1) {
     bq = (int8_t *)malloc((size_t)(rows * K));
     bd = (float *)malloc(sizeof(float) * (size_t)(rows * (K / 32)));
     for (int64_t r = 0; r < rows; ++r) orc_quantize_q8(b + r * K, K, bq + r * K, bd + r * (K / 32));
+  } else if (mode == 2) {
+    bx = (float *)malloc(sizeof(float) * (size_t)(rows * K));
+    for (int64_t r = 0; r < rows; ++r) orc_e2m1_split(b + r * K, K, 4, bx + r * K, NULL, NULL);
   }
   if (nthreads < 1) nthreads = 1;
   const int64_t items = (int64_t)T * top_k * N;
@@ -328,7 +387,7 @@ int orc_mul_mat_id(int type, const uint8_t *as, int64_t K, int64_t N, int64_t n_
   mm_job *jobs = (mm_job *)malloc(sizeof(mm_job) * nthreads);
   for (int i = 0; i < nthreads; ++i) {
     mm_job j = {type, mode, as, K, N, slot_bytes, b, b_ne1, ids, top_k, T, res,
-                items * i / nthreads, items * (i + 1) / nthreads, bq, bd};
+                items * i / nthreads, items * (i + 1) / nthreads, bq, bd, bx};
     jobs[i] = j;
     if (nthreads == 1) mm_worker(&jobs[i]);
     else pthread_create(&th[i], NULL, mm_worker, &jobs[i]);
@@ -339,6 +398,7 @@ int orc_mul_mat_id(int type, const uint8_t *as, int64_t K, int64_t N, int64_t n_
   free(jobs);
   free(bq);
   free(bd);
+  free(bx);
   return 0;
 }
 

@@ -59,6 +59,7 @@ def orc():
                                   ctypes.c_int64, _u8p, ctypes.c_int64, ctypes.c_int64,
                                   ctypes.c_int64, _f32p, _i32p, _f32p, ctypes.c_int, ctypes.c_int,
                                   ctypes.c_int, _f32p, _f32p, ctypes.c_int]
+        L.orc_e2m1_split.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, _f32p, _u8p, _u8p]
         L.orc_quantize_q8.argtypes = [_f32p, ctypes.c_int64, ctypes.POINTER(ctypes.c_int8), _f32p]
         L.orc_f32_to_f16.argtypes = [ctypes.c_float]
         L.orc_f32_to_f16.restype = ctypes.c_uint16
@@ -227,6 +228,22 @@ def quantize_q8(x):
     return q, d
 
 
+MODES = {"exact": 0, "q8": 1, "e2m1x4": 2}
+
+
+def e2m1_split(x, terms=4):
+    """Tensor-core activation form: (sum of terms, codes [terms, nb, 32],
+    scale bytes [terms, nb]) for a 1-D f32 vector."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    nb = x.size // 32
+    approx = np.empty_like(x)
+    codes = np.empty((terms, nb, 32), dtype=np.uint8)
+    exps = np.empty((terms, nb), dtype=np.uint8)
+    orc().orc_e2m1_split(_p(x, _f32p), x.size, terms, _p(approx, _f32p), _p(codes, _u8p),
+                         _p(exps, _u8p))
+    return approx, codes, exps
+
+
 def mul_mat_id(wtype, slab, K, N, b, ids, mode="exact", nthreads=None):
     """slab: uint8 [n_slots, expert_bytes] (ggml layout); b: f32 [T, b_ne1, K];
     ids: int32 slot ids [T, top_k]. Returns f32 [T, top_k, N]."""
@@ -237,7 +254,7 @@ def mul_mat_id(wtype, slab, K, N, b, ids, mode="exact", nthreads=None):
     T, top_k = ids.shape
     out = np.empty((T, top_k, N), dtype=np.float32)
     rc = orc().orc_mul_mat_id(t, _p(slab, _u8p), K, N, slab.shape[0], _p(b, _f32p), b.shape[1],
-                              _p(ids, _i32p), top_k, T, 0 if mode == "exact" else 1,
+                              _p(ids, _i32p), top_k, T, MODES[mode],
                               _p(out, _f32p), nthreads or os.cpu_count() or 1)
     assert rc == 0, rc
     return out
@@ -262,7 +279,7 @@ def moe_ffn(wtype, gate, up, down, K, n_ff, x, ids, w, mode="exact", up_row0=0, 
     h = np.empty((T, top_k, n_ff), dtype=np.float32)
     rc = orc().orc_moe_ffn(t, _p(gate, _u8p), gate_rows, _p(up, _u8p), up_rows, up_row0,
                            _p(down, _u8p), K, n_ff, gate.shape[0], _p(x, _f32p), _p(ids, _i32p),
-                           _p(w, _f32p), top_k, T, 0 if mode == "exact" else 1, _p(y, _f32p),
+                           _p(w, _f32p), top_k, T, MODES[mode], _p(y, _f32p),
                            _p(h, _f32p), nthreads or os.cpu_count() or 1)
     assert rc == 0, rc
     return y, h

@@ -67,5 +67,6 @@ def test_side_stream_fill_ordered_by_event():
     torch.cuda.synchronize()
     slab = np.zeros((n_slot + 1, ex.shape[1]), dtype=np.uint8)
     slab[1] = ex[1]
-    want = O.mul_mat_id(wtype, slab, K, N, b, ids, mode="q8")
-    assert O.max_abs_normalized(got.cpu().numpy(), want) < 1e-5
+    # MXFP4 with K % 64 == 0 runs on the tensor cores (activations as e2m1 terms)
+    want = O.mul_mat_id(wtype, slab, K, N, b, ids, mode="e2m1x4")
+    assert O.max_abs_normalized(got.cpu().numpy(), want) < 1e-4

@@ -1,8 +1,11 @@
 """mul_mat_id over the slot pool against the CPU oracle.
 
+Two arithmetic paths: MXFP4 with K a multiple of 64 runs on the tensor
+cores (activations as four e2m1 terms per block), everything else on the
+CUDA cores (int8 activations, ggml's q8_0 form); MXFP4 cases run both.
 Tolerances (max |got - want| / max |want|):
-  - vs the oracle in q8 mode (same activation quantization, f32 block sums
-    in another order): 1e-5;
+  - vs the oracle in the path's own form: 1e-5 (q8; f32 block sums in
+    another order) or 1e-4 (e2m1x4; f32 tensor-core accumulation);
   - vs the exact f64 oracle: 1e-2, the bound stated for this path.
 Properties from the reference's spikes: bit-identical results under slot
 permutation (s0 T3), unreferenced slots harmless (s0 T4), the zero slot
@@ -18,7 +21,21 @@ from tests.helpers import experts, topk_ids
 pytestmark = pytest.mark.gpu
 
 TOL_Q8 = 1e-5
+TOL_TC = 1e-4
 TOL_EXACT = 1e-2
+
+
+@pytest.fixture(params=["tc", "q8"])
+def path(request):
+    from moestream_b200 import ops
+    ops.set_mxfp4_path(request.param)
+    yield request.param
+    ops.set_mxfp4_path("tc")
+
+
+def oracle_mode(wtype, K, path):
+    from moestream_b200 import ops
+    return "e2m1x4" if path == "tc" and ops.tc_eligible(wtype, K) else "q8"
 
 
 def make_pool(wtype, K, N, n_slot, slab_bytes, slots):
@@ -53,14 +70,17 @@ SHAPES = [
     ("iq4_nl", 2048, 768, 16, 8, 1, 8, 1),    # single-op shape (fewer experts)
     ("iq4_nl", 512, 2048, 12, 8, 8, 8, 8),    # 256-expert model's down projection shape
     ("mxfp4", 2880, 256, 10, 6, 4, 4, 1),     # gpt-oss K (90 blocks: uneven warp split)
-    ("mxfp4", 256, 96, 8, 5, 37, 4, 4),       # many pairs per slot (> 8: several passes)
+    ("mxfp4", 2880, 2880, 6, 4, 3, 4, 4),     # gpt-oss down: last 128-row tile half full
+    ("mxfp4", 256, 96, 8, 5, 60, 4, 4),       # many pairs per slot (> 8 and > 32: passes)
+    ("mxfp4", 96, 64, 6, 4, 5, 2, 1),         # K not a multiple of 64: CUDA cores
     ("iq4_nl", 96, 40, 6, 4, 5, 2, 1),        # N not a multiple of 32
 ]
 
 
 @pytest.mark.parametrize("wtype,K,N,n_expert,n_slot,n_tok,top_k,b_ne1", SHAPES)
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_mul_mat_id_matches_oracle(wtype, K, N, n_expert, n_slot, n_tok, top_k, b_ne1, dtype):
+def test_mul_mat_id_matches_oracle(wtype, K, N, n_expert, n_slot, n_tok, top_k, b_ne1, dtype,
+                                   path):
     rng = np.random.default_rng(K + N + n_tok)
     ex = experts(wtype, n_expert, K, N, seed=0)
     resident = rng.permutation(n_expert)[:n_slot]
@@ -72,16 +92,17 @@ def test_mul_mat_id_matches_oracle(wtype, K, N, n_expert, n_slot, n_tok, top_k, 
         b = torch.from_numpy(b).to(torch.bfloat16).float().numpy()  # oracle sees bf16 values
     got = gpu_mmid(pool, b, ids, dtype)
     slab = slab_for(ex, slot_of, n_slot)
-    want_q8 = O.mul_mat_id(wtype, slab, K, N, b, ids, mode="q8")
+    mode = oracle_mode(wtype, K, path)
+    want_form = O.mul_mat_id(wtype, slab, K, N, b, ids, mode=mode)
     want = O.mul_mat_id(wtype, slab, K, N, b, ids, mode="exact")
-    assert O.max_abs_normalized(got, want_q8) < TOL_Q8
+    assert O.max_abs_normalized(got, want_form) < (TOL_TC if mode == "e2m1x4" else TOL_Q8)
     assert O.max_abs_normalized(got, want) < TOL_EXACT
     # Rows routed to the zero slot are exactly zero.
     z = ids == n_slot
     assert np.all(got[z] == 0.0)
 
 
-def test_slot_permutation_is_bit_identical():
+def test_slot_permutation_is_bit_identical(path):
     wtype, K, N, n_slot = "mxfp4", 512, 128, 6
     ex = experts(wtype, 6, K, N, seed=1)
     rng = np.random.default_rng(2)
@@ -106,7 +127,7 @@ def test_unreferenced_slots_do_not_matter():
     assert np.array_equal(gpu_mmid(p1, b, ids), gpu_mmid(p2, b, ids))
 
 
-def test_split_expert_sets_add_up():
+def test_split_expert_sets_add_up(path):
     """FFN-style additivity at the matmul: routing half the ids to the zero
     slot in each of two calls sums to the full call (s4's property)."""
     wtype, K, N, n_slot = "mxfp4", 256, 64, 8
@@ -122,10 +143,10 @@ def test_split_expert_sets_add_up():
     assert np.array_equal(full, s)  # each row comes entirely from one call
 
 
-def test_zero_slot_exact_zero_even_from_memory():
+def test_zero_slot_exact_zero_even_from_memory(path):
     """The zero slot's bytes are zeros and a row routed there is 0."""
     from moestream_b200 import ops
-    pool = ops.SlotPool("iq4_nl", 128, 32, 3)
+    pool = ops.SlotPool("mxfp4", 128, 32, 3)
     z = pool.read_slot(3)
     torch.cuda.synchronize()
     assert int(z.to(torch.int64).sum()) == 0
