@@ -13,8 +13,11 @@
 // int8 (q8_0) activations; each term is one more MMA, which decode has to
 // spare. D[row][pair] accumulates in f32 in tensor memory.
 //
-// One CTA (128 threads) computes a 128-row tile of one slot for up to 32 of
-// its (token, k) pairs per pass:
+// Persistent CTAs (two per SM, 192 threads) walk the work items (active
+// slot x 128-row tile) with a stride of the grid; each item runs in passes of
+// up to 32 of the slot's (token, k) pairs. The pipeline never drains between
+// items: the producer streams the next item's tiles while the accumulators
+// of the previous one are read out. Roles:
 //   warp 0, lane 0 : producer -- per stage, one tiled TMA copy per weight
 //                    view (128 rows x 4 blocks, 8 KB), one 512-byte bulk
 //                    copy of each view's scale-factor chunk, one tiled TMA
@@ -22,9 +25,11 @@
 //                    x 32 pairs) and one of their scales, into a 4-stage
 //                    shared-memory ring;
 //   warp 1, lane 0 : copies each stage's scale factors into tensor memory
-//                    (tcgen05.cp) and issues the MMAs (M=128, N=32, K=64);
-//                    tcgen05.commit frees the stage;
-//   all 4 warps    : epilogue -- each warp reads its 32 TMEM lanes (rows).
+//                    (tcgen05.cp) and issues the MMAs (M=128, N=8 or 32,
+//                    K=64) into one of two accumulator buffers;
+//                    tcgen05.commit frees the stage / hands over a buffer;
+//   warps 2-5      : epilogue -- warp w reads TMEM lanes 32*(w%4)..+31
+//                    (rows), releases the buffer, then stores.
 // With two views (gate and up) the epilogue applies SwiGLU and writes the
 // down projection's activation terms directly.
 // Every mbarrier wait is bounded; a wait that gives up sets *err and the CTA
@@ -42,22 +47,25 @@ namespace tc {
 
 constexpr int kTerms = 4;        // e2m1 terms per activation block
 constexpr int kPairs = 32;       // MMA N: (token, k) pairs per pass
+constexpr int kPairsSmall = 8;   // MMA N for passes of at most 8 pairs
 constexpr int kStages = 4;       // shared-memory ring depth
 constexpr int kChunk = 4;        // 32-element blocks per stage (two K=64 MMAs)
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;   // producer warp, MMA warp, 4 epilogue warps
 
 template <int NV>
 struct Cfg {
   static constexpr int kA = NV * kChunk * 2048;          // 128 rows x 16 B per block
   static constexpr int kSFA = NV * 512;
   static constexpr int kB = kTerms * kChunk * kPairs * 16;
+  static constexpr int kBSmall = kTerms * kChunk * kPairsSmall * 16;
   static constexpr int kSFB = kTerms * 512;
   static constexpr int kStage = kA + kSFA + kB + kSFB;
   static constexpr int kBarOff = kStages * kStage;
   static constexpr int kSmem = kBarOff + 256;
+  static constexpr int kAccCols = NV * kPairs;           // one accumulator buffer
   static constexpr int kSfCols = (NV + kTerms) * 4;      // TMEM columns per stage
-  static constexpr int kSfBase = NV * kPairs;            // after the accumulators
-  static constexpr int kTmemCols = NV == 2 ? 256 : 128;
+  static constexpr int kSfBase = 2 * kAccCols;           // after both buffers
+  static constexpr int kTmemCols = 256;
   static_assert(kSfBase + kStages * kSfCols <= kTmemCols, "tensor memory map");
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
@@ -65,6 +73,7 @@ struct Cfg {
 struct Args {
   CUtensorMap tm_w[2];       // each view's pool: (8 B x 2 x rows, blocks, slots)
   CUtensorMap tm_aq;         // activation terms: (8 B x 2 x pairs, blocks, terms)
+  CUtensorMap tm_aq8;        // the same with an 8-pair box
   CUtensorMap tm_asf;        // their scales: (8 B x 2 x pairs, chunks, terms)
   const uint8_t *pool[2];    // slot 0 of each view's pool
   int64_t slot_stride[2], N[2];
@@ -147,51 +156,31 @@ __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t n
 }
 
 template <int NV>
-__global__ void __launch_bounds__(kThreads) tc_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__ Args a) {
   using C = Cfg<NV>;
   extern __shared__ __align__(1024) uint8_t smem[];
-  const int ai = blockIdx.x / a.tiles;
-  const int tile = blockIdx.x - ai * a.tiles;
-  if (ai >= a.active[0]) return;
-  const int slot = a.active[1 + ai];
-  const int c_total = a.counts[slot];
-  const int64_t pos0 = a.offsets[slot];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n0 = int64_t(tile) * 128;
-  const int64_t n = n0 + threadIdx.x;     // epilogue row
-  const bool valid = n < a.n_out;
   const int64_t nc_in = (a.nb + 3) / 4;
-
-  if (slot == a.zero_slot) {
-    // Every weight of the zero slot is 0: write the exact result directly.
-    for (int j = 0; j < c_total; ++j) {
-      const int64_t pair = a.rows[pos0 + j];
-      if constexpr (NV == 1) {
-        if (valid) a.res[pair * a.n_out + n] = 0.f;
-      } else {
-        if (a.act && valid) a.act[pair * a.n_out + n] = 0.f;
-        const int64_t blk = (n0 >> 5) + warp;
-        if (blk < a.o_nb)
-          warp_e2m1_terms(0.f, lane, a.oq + a4_q_off(0, blk, a.o_nb, a.a_rows, pos0 + j),
-                          a.o_nb * a.a_rows * 16,
-                          a.osf + a4_sf_off(0, blk / 4, (a.o_nb + 3) / 4, a.a_rows, pos0 + j) + (blk & 3),
-                          ((a.o_nb + 3) / 4) * a.a_rows * 16);
-      }
-    }
-    return;
-  }
+  const int64_t n_chunks = (a.nb + kChunk - 1) / kChunk;
+  const int64_t n_items = int64_t(a.active[0]) * a.tiles;
 
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
   uint64_t *empty = full + kStages;
-  uint64_t *done = empty + kStages;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  uint64_t *acc_full = empty + kStages;   // [2] MMA -> epilogue
+  uint64_t *acc_empty = acc_full + 2;     // [2] epilogue -> MMA
+  uint64_t *drained = acc_empty + 2;      // MMA issuer's last commit
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drained + 1);
   int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       sm100::mbar_init(&full[s], 1);
       sm100::mbar_init(&empty[s], 1);
     }
-    sm100::mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&acc_full[b], 1);
+      sm100::mbar_init(&acc_empty[b], 4);
+    }
+    sm100::mbar_init(drained, 1);
     *abort_flag = 0;
     sm100::fence_mbar_init();
   }
@@ -203,128 +192,190 @@ __global__ void __launch_bounds__(kThreads) tc_kernel(const __grid_constant__ Ar
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  volatile int *abort_v = abort_flag;
 
-  const int64_t n_chunks = (a.nb + kChunk - 1) / kChunk;
-  uint32_t it_prod = 0, it_mma = 0;
-  int pass = 0;
-
-  for (int g0 = 0; g0 < c_total; g0 += kPairs, ++pass) {
-    const int cc = min(kPairs, c_total - g0);
-    const int64_t pos = pos0 + g0;
-    if (warp == 0 && lane == 0) {
-      // ---- producer ----
-      for (int64_t i = 0; i < n_chunks && !*(volatile int *)abort_flag; ++i, ++it_prod) {
-        const int s = it_prod % kStages;
-        const uint32_t ph = (it_prod / kStages) & 1;
-        if (!sm100::mbar_wait_bounded(&empty[s], ph ^ 1)) {
-          atomicOr(a.err, 1);
-          *(volatile int *)abort_flag = 1;
-          break;
+  if (warp == 0) {
+    // ---- producer ----
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
+        const int slot = a.active[1 + w / a.tiles];
+        if (slot == a.zero_slot) continue;
+        const int64_t n0 = (w % a.tiles) * 128;
+        const int c_total = a.counts[slot];
+        const int64_t pos0 = a.offsets[slot];
+        for (int g0 = 0; g0 < c_total && !*abort_v; g0 += kPairs) {
+          const bool small = c_total - g0 <= kPairsSmall;
+          const int64_t pos = pos0 + g0;
+          for (int64_t i = 0; i < n_chunks; ++i, ++it) {
+            const int s = it % kStages;
+            if (!sm100::mbar_wait_bounded(&empty[s], ((it / kStages) & 1) ^ 1)) {
+              atomicOr(a.err, 1);
+              *abort_v = 1;
+              break;
+            }
+            uint8_t *st = smem + s * C::kStage;
+            uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
+            const int64_t b0 = i * kChunk;
+            // Full boxes are counted (rows or blocks outside the tensors
+            // arrive as zeros).
+            sm100::mbar_expect_tx(&full[s], uint32_t(C::kStage - (small ? C::kB - C::kBSmall : 0)));
+            for (int v = 0; v < NV; ++v) {
+              const int64_t r0 = a.row0[v] + n0;
+              sm100::tma_3d(sA + v * kChunk * 2048, &a.tm_w[v], int(r0) * 2, int(b0), slot,
+                            &full[s]);
+              const uint8_t *slot_base = a.pool[v] + int64_t(slot) * a.slot_stride[v];
+              const uint8_t *sf_base = slot_base + a.nb * a.N[v] * 16;
+              const int64_t sf_tiles = (a.N[v] + 127) / 128;
+              sm100::bulk_g2s(sSFA + v * 512, sf_base + (i * sf_tiles + (r0 >> 7)) * 512, 512,
+                              &full[s]);
+            }
+            sm100::tma_3d(sB, small ? &a.tm_aq8 : &a.tm_aq, int(pos) * 2, int(b0), 0, &full[s]);
+            sm100::tma_3d(sSFB, &a.tm_asf, int(pos) * 2, int(i), 0, &full[s]);
+          }
         }
-        uint8_t *st = smem + s * C::kStage;
-        uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
-        const int64_t b0 = i * kChunk;
-        const int kbn = int(a.nb - b0 < kChunk ? a.nb - b0 : kChunk);
-        // Full boxes are counted (rows or blocks outside the tensors arrive
-        // as zeros), so the byte count is the same for every stage.
-        constexpr uint32_t bytes = uint32_t(C::kStage);
-        (void)kbn;
-        sm100::mbar_expect_tx(&full[s], bytes);
-        for (int v = 0; v < NV; ++v) {
-          const int64_t r0 = a.row0[v] + n0;
-          sm100::tma_3d(sA + v * kChunk * 2048, &a.tm_w[v], int(r0) * 2, int(b0), slot, &full[s]);
-          const uint8_t *slot_base = a.pool[v] + int64_t(slot) * a.slot_stride[v];
-          const uint8_t *sf_base = slot_base + a.nb * a.N[v] * 16;
-          const int64_t sf_tiles = (a.N[v] + 127) / 128;
-          sm100::bulk_g2s(sSFA + v * 512, sf_base + (i * sf_tiles + (r0 >> 7)) * 512, 512, &full[s]);
-        }
-        sm100::tma_3d(sB, &a.tm_aq, int(pos) * 2, int(b0), 0, &full[s]);
-        sm100::tma_3d(sSFB, &a.tm_asf, int(pos) * 2, int(i), 0, &full[s]);
       }
-    } else if (warp == 1 && lane == 0) {
-      // ---- scale-factor copies and MMA issue ----
-      sm100::tc_fence_after();
-      bool first = true;
-      for (int64_t i = 0; i < n_chunks; ++i, ++it_mma) {
-        const int s = it_mma % kStages;
-        const uint32_t ph = (it_mma / kStages) & 1;
-        if (*(volatile int *)abort_flag || !sm100::mbar_wait_bounded(&full[s], ph)) {
-          atomicOr(a.err, 2);
-          *(volatile int *)abort_flag = 1;
-          break;
-        }
-        const uint8_t *st = smem + s * C::kStage;
-        const uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
-        const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols;
-        for (int v = 0; v < NV; ++v)
-          sm100::tmem_cp_32x128b_x4(sf_col + v * 4, sm100::smem_desc(sm100::smem_u32(sSFA + v * 512), 0, 128));
-        for (int t = 0; t < kTerms; ++t)
-          sm100::tmem_cp_32x128b_x4(sf_col + (NV + t) * 4,
-                                    sm100::smem_desc(sm100::smem_u32(sSFB + t * 512), 0, 128));
-        const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
-        for (int j = 0; j < kbn / 2; ++j) {
-          for (int v = 0; v < NV; ++v) {
-            const uint64_t adesc =
-                sm100::smem_desc(sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
-            for (int t = 0; t < kTerms; ++t) {
-              const uint64_t bdesc = sm100::smem_desc(
-                  sm100::smem_u32(sB + (t * kChunk + 2 * j) * (kPairs * 16)), kPairs * 16, 128);
+      // No copy may still be landing in shared memory when the CTA exits
+      // (only possible after an abort): wait for the last stages issued.
+      for (uint32_t k = it > uint32_t(kStages) ? it - kStages : 0; k < it; ++k)
+        if (!sm100::mbar_wait_bounded(&full[k % kStages], (k / kStages) & 1)) atomicOr(a.err, 16);
+    }
+  } else if (warp == 1) {
+    // ---- scale-factor copies and MMA issue ----
+    if (lane == 0) {
+      uint32_t it = 0, acc = 0;
+      for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
+        const int slot = a.active[1 + w / a.tiles];
+        if (slot == a.zero_slot) continue;
+        const int c_total = a.counts[slot];
+        for (int g0 = 0; g0 < c_total && !*abort_v; g0 += kPairs, ++acc) {
+          const int np = c_total - g0 <= kPairsSmall ? kPairsSmall : kPairs;
+          const int buf = acc & 1;
+          if (!sm100::mbar_wait_bounded(&acc_empty[buf], ((acc >> 1) & 1) ^ 1)) {
+            atomicOr(a.err, 2);
+            *abort_v = 1;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t d0 = tmem + buf * C::kAccCols;
+          for (int64_t i = 0; i < n_chunks; ++i, ++it) {
+            const int s = it % kStages;
+            if (!sm100::mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
+              atomicOr(a.err, 4);
+              *abort_v = 1;
+              break;
+            }
+            const uint8_t *st = smem + s * C::kStage;
+            const uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
+            const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols;
+            for (int v = 0; v < NV; ++v)
+              sm100::tmem_cp_32x128b_x4(sf_col + v * 4,
+                                        sm100::smem_desc(sm100::smem_u32(sSFA + v * 512), 0, 128));
+            for (int t = 0; t < kTerms; ++t)
+              sm100::tmem_cp_32x128b_x4(sf_col + (NV + t) * 4,
+                                        sm100::smem_desc(sm100::smem_u32(sSFB + t * 512), 0, 128));
+            const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
+            for (int j = 0; j < kbn / 2; ++j) {
               const uint32_t sel = uint32_t(2 * j);
-              sm100::mma_mxf4(tmem + v * kPairs, adesc, bdesc, sm100::idesc_mxf4(kPairs, sel, sel),
-                              (sf_col + v * 4) | (sel << 30), (sf_col + (NV + t) * 4) | (sel << 30),
-                              (first && t == 0) ? 0u : 1u);
+              for (int v = 0; v < NV; ++v) {
+                const uint64_t adesc =
+                    sm100::smem_desc(sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
+                for (int t = 0; t < kTerms; ++t) {
+                  const uint64_t bdesc = sm100::smem_desc(
+                      sm100::smem_u32(sB + (t * kChunk + 2 * j) * (np * 16)), np * 16, 128);
+                  sm100::mma_mxf4(d0 + v * kPairs, adesc, bdesc, sm100::idesc_mxf4(np, sel, sel),
+                                  (sf_col + v * 4) | (sel << 30),
+                                  (sf_col + (NV + t) * 4) | (sel << 30),
+                                  (i == 0 && j == 0 && t == 0) ? 0u : 1u);
+                }
+              }
+            }
+            sm100::tc_commit(&empty[s]);
+          }
+          sm100::tc_commit(&acc_full[buf]);
+        }
+      }
+      // Every MMA and scale-factor copy is complete before tensor memory is
+      // released.
+      sm100::tc_commit(drained);
+      if (!sm100::mbar_wait_bounded(drained, 0)) atomicOr(a.err, 16);
+    }
+  } else {
+    // ---- epilogue (warps 2-5) ----
+    const int quad = warp & 3;            // TMEM lane quadrant of this warp
+    const uint32_t lane_addr = uint32_t(quad * 32) << 16;
+    uint32_t acc = 0;
+    for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
+      const int slot = a.active[1 + w / a.tiles];
+      const int64_t n0 = (w % a.tiles) * 128;
+      const int64_t n = n0 + quad * 32 + lane;
+      const bool valid = n < a.n_out;
+      const int64_t blk = (n0 >> 5) + quad;   // SwiGLU output block of this warp
+      const int c_total = a.counts[slot];
+      const int64_t pos0 = a.offsets[slot];
+      if (slot == a.zero_slot) {
+        // Every weight of the zero slot is 0: write the exact result.
+        for (int j = 0; j < c_total; ++j) {
+          const int64_t pair = a.rows[pos0 + j];
+          if constexpr (NV == 1) {
+            if (valid) a.res[pair * a.n_out + n] = 0.f;
+          } else {
+            if (a.act && valid) a.act[pair * a.n_out + n] = 0.f;
+            if (blk < a.o_nb) {
+              const int64_t onc = (a.o_nb + 3) / 4;
+              warp_e2m1_terms(0.f, lane, a.oq + a4_q_off(0, blk, a.o_nb, a.a_rows, pos0 + j),
+                              a.o_nb * a.a_rows * 16,
+                              a.osf + a4_sf_off(0, blk / 4, onc, a.a_rows, pos0 + j) + (blk & 3),
+                              onc * a.a_rows * 16);
             }
           }
-          first = false;
         }
-        sm100::tc_commit(&empty[s]);
+        continue;
       }
-      sm100::tc_commit(done);
-    }
-    __syncwarp();
-
-    // ---- epilogue ----
-    if (!sm100::mbar_wait_bounded(done, uint32_t(pass & 1))) {
-      atomicOr(a.err, 4);
-      *(volatile int *)abort_flag = 1;
-    }
-    sm100::tc_fence_after();
-    const bool ok = !*(volatile int *)abort_flag;
-    uint32_t dg[32], du[32];
-    const uint32_t lane_addr = uint32_t(warp * 32) << 16;
-    sm100::tmem_ld_32cols(tmem + lane_addr, dg);
-    if constexpr (NV == 2) sm100::tmem_ld_32cols(tmem + lane_addr + kPairs, du);
-    sm100::tmem_ld_wait();
-    if (ok) {
+      for (int g0 = 0; g0 < c_total && !*abort_v; g0 += kPairs, ++acc) {
+        const int cc = min(kPairs, c_total - g0);
+        const int64_t pos = pos0 + g0;
+        const int buf = acc & 1;
+        if (!sm100::mbar_wait_bounded(&acc_full[buf], (acc >> 1) & 1)) {
+          atomicOr(a.err, 8);
+          *abort_v = 1;
+          break;
+        }
+        sm100::tc_fence_after();
+        uint32_t dg[32], du[32];
+        sm100::tmem_ld_32cols(tmem + lane_addr + buf * C::kAccCols, dg);
+        if constexpr (NV == 2) sm100::tmem_ld_32cols(tmem + lane_addr + buf * C::kAccCols + kPairs, du);
+        sm100::tmem_ld_wait();
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                                        sm100::smem_u32(&acc_empty[buf]))
+                                    : "memory");
 #pragma unroll
-      for (int j = 0; j < kPairs; ++j) {
-        if (j >= cc) break;
-        const int64_t pair = a.rows[pos + j];
-        const float g = __uint_as_float(dg[j]);
-        if constexpr (NV == 1) {
-          if (valid) a.res[pair * a.n_out + n] = g;
-        } else {
-          const float u = __uint_as_float(du[j]);
-          const float h = valid ? g / (1.f + expf(-g)) * u : 0.f;
-          if (a.act && valid) a.act[pair * a.n_out + n] = h;
-          const int64_t blk = (n0 >> 5) + warp;
-          if (blk < a.o_nb) {
-            const int64_t onc = (a.o_nb + 3) / 4;
-            warp_e2m1_terms(h, lane, a.oq + a4_q_off(0, blk, a.o_nb, a.a_rows, pos + j),
-                            a.o_nb * a.a_rows * 16,
-                            a.osf + a4_sf_off(0, blk / 4, onc, a.a_rows, pos + j) + (blk & 3),
-                            onc * a.a_rows * 16);
+        for (int j = 0; j < kPairs; ++j) {
+          if (j >= cc) break;
+          const int64_t pair = a.rows[pos + j];
+          const float g = __uint_as_float(dg[j]);
+          if constexpr (NV == 1) {
+            if (valid) a.res[pair * a.n_out + n] = g;
+          } else {
+            const float u = __uint_as_float(du[j]);
+            const float h = valid ? g / (1.f + expf(-g)) * u : 0.f;
+            if (a.act && valid) a.act[pair * a.n_out + n] = h;
+            if (blk < a.o_nb) {
+              const int64_t onc = (a.o_nb + 3) / 4;
+              warp_e2m1_terms(h, lane, a.oq + a4_q_off(0, blk, a.o_nb, a.a_rows, pos + j),
+                              a.o_nb * a.a_rows * 16,
+                              a.osf + a4_sf_off(0, blk / 4, onc, a.a_rows, pos + j) + (blk & 3),
+                              onc * a.a_rows * 16);
+            }
           }
         }
       }
     }
-    // The next pass overwrites the accumulators: every TMEM read is done.
-    sm100::tc_fence_before();
-    __syncthreads();
-    sm100::tc_fence_after();
-    if (*(volatile int *)abort_flag) break;
   }
 
+  // Teardown: every role is done issuing; release tensor memory.
   sm100::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -370,7 +421,16 @@ static int launch_tc_t(const tc::Args &a, int max_active, cudaStream_t st) {
   using C = tc::Cfg<NV>;
   MSB_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     C::kSmem));
-  const int64_t grid = int64_t(max_active) * a.tiles;
+  // Persistent grid: two CTAs per SM (shared memory allows two), never more
+  // than the work items the route can produce.
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0;
+    MSB_CUDA_TRY(cudaGetDevice(&dev));
+    MSB_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+  }
+  int64_t grid = int64_t(max_active) * a.tiles;
+  if (grid > 2 * n_sm) grid = 2 * n_sm;
   if (grid == 0) return MSB_OK;
   tc::tc_kernel<NV><<<unsigned(grid), tc::kThreads, C::kSmem, st>>>(a);
   count_launch();
@@ -423,7 +483,10 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
     const uint64_t df[3] = {uint64_t(n_pairs) * 2, nc, uint64_t(tc::kTerms)};
     const uint64_t sf[2] = {uint64_t(n_pairs) * 16, nc * uint64_t(n_pairs) * 16};
     const uint32_t bf[3] = {uint32_t(tc::kPairs) * 2, 1, uint32_t(tc::kTerms)};
+    const uint32_t bq8[3] = {uint32_t(tc::kPairsSmall) * 2, uint32_t(tc::kChunk),
+                             uint32_t(tc::kTerms)};
     if (!encode_tmap_u64_3d(&a.tm_aq, a.aq, dq, sq, bq) ||
+        !encode_tmap_u64_3d(&a.tm_aq8, a.aq, dq, sq, bq8) ||
         !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sf, bf))
       return fail(MSB_ERR_CUDA, "tensor-core path: activation tensor maps could not be encoded");
   }
