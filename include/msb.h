@@ -187,6 +187,23 @@ int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type,
                    float *res_dev, void *workspace, int64_t workspace_bytes,
                    void *stream);
 
+/* msb_mul_mat_id for callers that cannot allocate device memory: code
+ * running inside another runtime's allocator or memory hooks, where calling
+ * cudaMalloc would re-enter them, and hosts whose device memory is all
+ * reserved up front. Same arguments and result as msb_mul_mat_id, minus the
+ * workspace: it uses a fixed 8 MiB device array inside this library
+ * (msb_workspace_bytes(K, n_tok, top_k, n_slot) must not exceed 8 MiB,
+ * e.g. K = 2880 at 64 tokens x top-4; larger requests return
+ * MSB_ERR_INVALID). The pool's device must be current. The array is held
+ * on every GPU that loads the library until exit and is shared by all calls
+ * on a device, so calls that overlap on the GPU race on it. The first call
+ * on a device looks up the array's device address; make it before any
+ * stream capture on that device. No counterpart in the reference. */
+int msb_mul_mat_id_noalloc(msb_pool_t pool, const void *b_dev, int b_type,
+                           int64_t b_ne1, int64_t b_nb1, int64_t b_nb2,
+                           const msb_route_t *route, int32_t top_k,
+                           int32_t n_tok, float *res_dev, void *stream);
+
 /* ======================================================================== */
 /* MoE FFN layer                                                              */
 /* ======================================================================== */

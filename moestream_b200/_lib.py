@@ -84,6 +84,10 @@ SIGNATURES = {
     "msb_mul_mat_id": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
                                       ctypes.c_int64, ctypes.POINTER(Route), ctypes.c_int32,
                                       ctypes.c_int32, c_vp, c_vp, ctypes.c_int64, c_vp]),
+    "msb_mul_mat_id_noalloc": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int, ctypes.c_int64,
+                                              ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.POINTER(Route), ctypes.c_int32,
+                                              ctypes.c_int32, c_vp, c_vp]),
     "msb_moe_ffn": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, c_vp, c_vp, ctypes.c_int,
                                    ctypes.c_int64, ctypes.POINTER(Route), c_vp, ctypes.c_int32,
                                    ctypes.c_int32, c_vp, c_vp, c_vp, ctypes.c_int64, c_vp]),

@@ -21,6 +21,8 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include <mutex>
+
 #include "msb_internal.h"
 #include "pool.cuh"
 #include "quant.cuh"
@@ -591,4 +593,73 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
   combine_kernel<<<unsigned((total + 255) / 256), 256, 0, st>>>(rdown, w_dev, top_k, down->N, n_tok, y_dev); count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;
+}
+
+// ---- mul_mat_id without allocation ------------------------------------------
+// Some callers cannot call cudaMalloc at all: code that runs inside another
+// runtime's allocator or memory-accounting hooks (where re-entering the
+// allocator deadlocks or is forbidden), and hosts whose device memory is
+// carved up in advance, where a late allocation fails under memory
+// pressure. For them, msb_mul_mat_id_noalloc takes its workspace from the
+// fixed device array below instead of from the caller.
+//
+// The array lives in this library's module: every GPU that loads the library
+// holds kNoAllocScratchBytes of it until the process exits. Every call on a
+// device shares it and finds the previous call's contents there; calls whose
+// kernels overlap on the GPU (different streams, no ordering between them)
+// race on it.
+namespace {
+constexpr int64_t kNoAllocScratchBytes = int64_t(8) << 20;   // 8 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the array on `dev` (the current device). The host-side
+// symbol is only a stand-in, so the address is looked up once per device
+// with that device current; the first call on a device therefore does this
+// set-up and should come before any stream capture on that device.
+int noalloc_scratch(int dev, void **out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return fail(MSB_ERR_CUDA, "msb_mul_mat_id_noalloc: cudaGetSymbolAddress failed on device %d: %s",
+                  dev, cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return MSB_OK;
+}
+}  // namespace
+
+extern "C" int msb_mul_mat_id_noalloc(msb_pool_t pool, const void *b_dev, int b_type,
+                                      int64_t b_ne1, int64_t b_nb1, int64_t b_nb2,
+                                      const msb_route_t *route, int32_t top_k, int32_t n_tok,
+                                      float *res_dev, void *stream) {
+  MSB_CHECK_ARG(pool && route && res_dev, "msb_mul_mat_id_noalloc: null argument");
+  MSB_CHECK_ARG(top_k > 0 && n_tok >= 0, "msb_mul_mat_id_noalloc: bad shape");
+  const int64_t need = msb_workspace_bytes(pool->K, n_tok, top_k, pool->n_slot);
+  MSB_CHECK_ARG(need >= 0 && need <= kNoAllocScratchBytes,
+                "msb_mul_mat_id_noalloc: K=%lld with %d tokens x top-%d needs %lld workspace "
+                "bytes, more than its fixed %lld-byte scratch; use msb_mul_mat_id with a "
+                "caller-provided workspace",
+                (long long)pool->K, n_tok, top_k, (long long)need,
+                (long long)kNoAllocScratchBytes);
+  int dev = -1;
+  MSB_CUDA_TRY(cudaGetDevice(&dev));
+  MSB_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "msb_mul_mat_id_noalloc: device %d out of range",
+                dev);
+  MSB_CHECK_ARG(dev == pool->device,
+                "msb_mul_mat_id_noalloc: current device %d is not the pool's device %d", dev,
+                pool->device);
+  void *scratch = nullptr;
+  if (int rc = noalloc_scratch(dev, &scratch)) return rc;
+  // The only workspace word that must start at zero, the kernels' error
+  // flag, is cleared by msb_mul_mat_id on every call; everything else in
+  // the workspace is written before it is read.
+  return msb_mul_mat_id(pool, b_dev, b_type, b_ne1, b_nb1, b_nb2, route, top_k, n_tok, res_dev,
+                        scratch, kNoAllocScratchBytes, stream);
 }
