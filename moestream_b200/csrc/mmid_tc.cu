@@ -10,23 +10,26 @@
 // Activations are split into kTerms e2m1 terms per 32-element block, each
 // with its own power-of-two scale (a residual expansion: term t encodes what
 // terms 0..t-1 left over). Four terms are ~30x closer to exact than ggml's
-// int8 (q8_0) activations; each term is one more MMA, which decode has to
-// spare. D[row][pair] accumulates in f32 in tensor memory.
+// int8 (q8_0) activations. The terms of a pass's 8 pairs are stacked along
+// the MMA's N (row t * 8 + p of B is term t of pair p, each row with its own
+// block scales), so one M=128 N=32 K=64 MMA reads each weight tile from
+// shared memory once for all four terms; the epilogue adds the four f32
+// partial sums of a pair.
 //
 // Persistent CTAs (two per SM, 192 threads) walk the work items (active
 // slot x 128-row tile) with a stride of the grid; each item runs in passes of
-// up to 32 of the slot's (token, k) pairs. The pipeline never drains between
+// 8 of the slot's (token, k) pairs. The pipeline never drains between
 // items: the producer streams the next item's tiles while the accumulators
 // of the previous one are read out. Roles:
 //   warp 0, lane 0 : producer -- per stage, one tiled TMA copy per weight
 //                    view (128 rows x 4 blocks, 8 KB), one 512-byte bulk
 //                    copy of each view's scale-factor chunk, one tiled TMA
-//                    copy of the pairs' activation terms (4 terms x 4 blocks
-//                    x 32 pairs) and one of their scales, into a 4-stage
-//                    shared-memory ring;
+//                    copy of the pass's activation terms (4 blocks x 4
+//                    terms x 8 pairs, 2 KB) and one of their scales (512 B),
+//                    into a shared-memory ring;
 //   warp 1, lane 0 : copies each stage's scale factors into tensor memory
-//                    (tcgen05.cp) and issues the MMAs (M=128, N=8 or 32,
-//                    K=64) into one of two accumulator buffers;
+//                    (tcgen05.cp) and issues the MMAs (one per view and
+//                    K=64 step) into one of two accumulator buffers;
 //                    tcgen05.commit frees the stage / hands over a buffer;
 //   warps 2-5      : epilogue -- warp w reads TMEM lanes 32*(w%4)..+31
 //                    (rows), releases the buffer, then stores.
@@ -46,35 +49,35 @@ namespace msb {
 namespace tc {
 
 constexpr int kTerms = 4;        // e2m1 terms per activation block
-constexpr int kPairs = 32;       // MMA N: (token, k) pairs per pass
-constexpr int kPairsSmall = 8;   // MMA N for passes of at most 8 pairs
-constexpr int kStages = 4;       // shared-memory ring depth
+constexpr int kPairs = 8;        // (token, k) pairs per pass
+constexpr int kN = kTerms * kPairs;   // MMA N: the pass's terms stacked
 constexpr int kChunk = 4;        // 32-element blocks per stage (two K=64 MMAs)
-constexpr int kThreads = 192;   // producer warp, MMA warp, 4 epilogue warps
+constexpr int kThreads = 192;    // producer warp, MMA warp, 4 epilogue warps
 
 template <int NV>
 struct Cfg {
+  // Ring depth: two CTAs per SM share 228 KB of shared memory.
+  static constexpr int kStages = NV == 2 ? 5 : 8;
   static constexpr int kA = NV * kChunk * 2048;          // 128 rows x 16 B per block
   static constexpr int kSFA = NV * 512;
-  static constexpr int kB = kTerms * kChunk * kPairs * 16;
-  static constexpr int kBSmall = kTerms * kChunk * kPairsSmall * 16;
-  static constexpr int kSFB = kTerms * 512;
+  static constexpr int kB = kChunk * kN * 16;            // [block][term][pair] 16 B rows
+  static constexpr int kSFB = 512;                       // [term][pair] 16 B rows
   static constexpr int kStage = kA + kSFA + kB + kSFB;
   static constexpr int kBarOff = kStages * kStage;
   static constexpr int kSmem = kBarOff + 256;
-  static constexpr int kAccCols = NV * kPairs;           // one accumulator buffer
-  static constexpr int kSfCols = (NV + kTerms) * 4;      // TMEM columns per stage
+  static constexpr int kAccCols = NV * kN;               // one accumulator buffer
+  static constexpr int kSfCols = (NV + 1) * 4;           // TMEM columns per stage
   static constexpr int kSfBase = 2 * kAccCols;           // after both buffers
   static constexpr int kTmemCols = 256;
   static_assert(kSfBase + kStages * kSfCols <= kTmemCols, "tensor memory map");
-  static_assert(kSmem <= 227 * 1024, "shared memory");
+  static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
+  static_assert(kStage % 128 == 0, "TMA destinations stay 128-byte aligned");
 };
 
 struct Args {
   CUtensorMap tm_w[2];       // each view's pool: (8 B x 2 x rows, blocks, slots)
-  CUtensorMap tm_aq;         // activation terms: (8 B x 2 x pairs, blocks, terms)
-  CUtensorMap tm_aq8;        // the same with an 8-pair box
-  CUtensorMap tm_asf;        // their scales: (8 B x 2 x pairs, chunks, terms)
+  CUtensorMap tm_aq;         // activation terms: (8 B x 2 x pairs, terms, blocks)
+  CUtensorMap tm_asf;        // their scales: (8 B x 2 x pairs, terms, chunks)
   const uint8_t *pool[2];    // slot 0 of each view's pool
   int64_t slot_stride[2], N[2];
   int64_t nb;                // blocks per row (K / 32), same for both views
@@ -92,11 +95,12 @@ struct Args {
   int *err;
 };
 
-__device__ __forceinline__ int64_t a4_q_off(int t, int64_t b, int64_t nb, int64_t rows, int64_t r) {
-  return ((int64_t(t) * nb + b) * rows + r) * 16;
-}
-__device__ __forceinline__ int64_t a4_sf_off(int t, int64_t c, int64_t nc, int64_t rows, int64_t r) {
-  return ((int64_t(t) * nc + c) * rows + r) * 16;
+// Byte offset of the 16-byte record of (term t, block or chunk b, row r) in
+// an activation-term buffer of `rows` rows: [b][t][r][16 B]. The records of
+// one pass (8 consecutive rows, all terms) of one block are 512 contiguous
+// bytes: the stacked B operand of one MMA K-half, or its 32 scale rows.
+__device__ __forceinline__ int64_t a4_off(int t, int64_t b, int64_t rows, int64_t r) {
+  return ((b * kTerms + t) * rows + r) * 16;
 }
 
 // Splits the block held by the warp (lane j = element j) into kTerms e2m1
@@ -134,7 +138,7 @@ __device__ __forceinline__ void warp_e2m1_terms(float r, int lane, uint8_t *q_t0
 }
 
 // Activations of every pair in grouped order into the term layout:
-// q [kTerms][nb][rows][16 B], sf [kTerms][ceil(nb/4)][rows][16 B] (byte b%4).
+// q [nb][kTerms][rows][16 B], sf [ceil(nb/4)][kTerms][rows][16 B] (byte b%4).
 template <typename T>
 __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t nb1, int64_t nb2,
                                                         int32_t ne1, int32_t top_k,
@@ -150,14 +154,14 @@ __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t n
   float v;
   if constexpr (sizeof(T) == 4) v = *reinterpret_cast<const float *>(p);
   else v = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(p));
-  const int64_t nc = (nb + 3) / 4;
-  warp_e2m1_terms(v, lane, q + a4_q_off(0, blk, nb, n_pairs, pos), nb * n_pairs * 16,
-                  sf + a4_sf_off(0, blk / 4, nc, n_pairs, pos) + (blk & 3), nc * n_pairs * 16);
+  warp_e2m1_terms(v, lane, q + a4_off(0, blk, n_pairs, pos), n_pairs * 16,
+                  sf + a4_off(0, blk / 4, n_pairs, pos) + (blk & 3), n_pairs * 16);
 }
 
 template <int NV>
 __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__ Args a) {
   using C = Cfg<NV>;
+  constexpr int kStages = C::kStages;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t nc_in = (a.nb + 3) / 4;
@@ -205,7 +209,6 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
         const int c_total = a.counts[slot];
         const int64_t pos0 = a.offsets[slot];
         for (int g0 = 0; g0 < c_total && !*abort_v; g0 += kPairs) {
-          const bool small = c_total - g0 <= kPairsSmall;
           const int64_t pos = pos0 + g0;
           for (int64_t i = 0; i < n_chunks; ++i, ++it) {
             const int s = it % kStages;
@@ -219,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
             const int64_t b0 = i * kChunk;
             // Full boxes are counted (rows or blocks outside the tensors
             // arrive as zeros).
-            sm100::mbar_expect_tx(&full[s], uint32_t(C::kStage - (small ? C::kB - C::kBSmall : 0)));
+            sm100::mbar_expect_tx(&full[s], uint32_t(C::kStage));
             for (int v = 0; v < NV; ++v) {
               const int64_t r0 = a.row0[v] + n0;
               sm100::tma_3d(sA + v * kChunk * 2048, &a.tm_w[v], int(r0) * 2, int(b0), slot,
@@ -230,8 +233,8 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
               sm100::bulk_g2s(sSFA + v * 512, sf_base + (i * sf_tiles + (r0 >> 7)) * 512, 512,
                               &full[s]);
             }
-            sm100::tma_3d(sB, small ? &a.tm_aq8 : &a.tm_aq, int(pos) * 2, int(b0), 0, &full[s]);
-            sm100::tma_3d(sSFB, &a.tm_asf, int(pos) * 2, int(i), 0, &full[s]);
+            sm100::tma_3d(sB, &a.tm_aq, int(pos) * 2, 0, int(b0), &full[s]);
+            sm100::tma_3d(sSFB, &a.tm_asf, int(pos) * 2, 0, int(i), &full[s]);
           }
         }
       }
@@ -249,7 +252,6 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
         if (slot == a.zero_slot) continue;
         const int c_total = a.counts[slot];
         for (int g0 = 0; g0 < c_total && !*abort_v; g0 += kPairs, ++acc) {
-          const int np = c_total - g0 <= kPairsSmall ? kPairsSmall : kPairs;
           const int buf = acc & 1;
           if (!sm100::mbar_wait_bounded(&acc_empty[buf], ((acc >> 1) & 1) ^ 1)) {
             atomicOr(a.err, 2);
@@ -271,23 +273,20 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
             for (int v = 0; v < NV; ++v)
               sm100::tmem_cp_32x128b_x4(sf_col + v * 4,
                                         sm100::smem_desc(sm100::smem_u32(sSFA + v * 512), 0, 128));
-            for (int t = 0; t < kTerms; ++t)
-              sm100::tmem_cp_32x128b_x4(sf_col + (NV + t) * 4,
-                                        sm100::smem_desc(sm100::smem_u32(sSFB + t * 512), 0, 128));
+            sm100::tmem_cp_32x128b_x4(sf_col + NV * 4,
+                                      sm100::smem_desc(sm100::smem_u32(sSFB), 0, 128));
             const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
             for (int j = 0; j < kbn / 2; ++j) {
               const uint32_t sel = uint32_t(2 * j);
+              // B: 32 stacked rows of 16 B per block; K-halves one block apart.
+              const uint64_t bdesc =
+                  sm100::smem_desc(sm100::smem_u32(sB + 2 * j * (kN * 16)), kN * 16, 128);
               for (int v = 0; v < NV; ++v) {
                 const uint64_t adesc =
                     sm100::smem_desc(sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
-                for (int t = 0; t < kTerms; ++t) {
-                  const uint64_t bdesc = sm100::smem_desc(
-                      sm100::smem_u32(sB + (t * kChunk + 2 * j) * (np * 16)), np * 16, 128);
-                  sm100::mma_mxf4(d0 + v * kPairs, adesc, bdesc, sm100::idesc_mxf4(np, sel, sel),
-                                  (sf_col + v * 4) | (sel << 30),
-                                  (sf_col + (NV + t) * 4) | (sel << 30),
-                                  (i == 0 && j == 0 && t == 0) ? 0u : 1u);
-                }
+                sm100::mma_mxf4(d0 + v * kN, adesc, bdesc, sm100::idesc_mxf4(kN, sel, sel),
+                                (sf_col + v * 4) | (sel << 30), (sf_col + NV * 4) | (sel << 30),
+                                (i == 0 && j == 0) ? 0u : 1u);
               }
             }
             sm100::tc_commit(&empty[s]);
@@ -321,13 +320,11 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
             if (valid) a.res[pair * a.n_out + n] = 0.f;
           } else {
             if (a.act && valid) a.act[pair * a.n_out + n] = 0.f;
-            if (blk < a.o_nb) {
-              const int64_t onc = (a.o_nb + 3) / 4;
-              warp_e2m1_terms(0.f, lane, a.oq + a4_q_off(0, blk, a.o_nb, a.a_rows, pos0 + j),
-                              a.o_nb * a.a_rows * 16,
-                              a.osf + a4_sf_off(0, blk / 4, onc, a.a_rows, pos0 + j) + (blk & 3),
-                              onc * a.a_rows * 16);
-            }
+            if (blk < a.o_nb)
+              warp_e2m1_terms(0.f, lane, a.oq + a4_off(0, blk, a.a_rows, pos0 + j),
+                              a.a_rows * 16,
+                              a.osf + a4_off(0, blk / 4, a.a_rows, pos0 + j) + (blk & 3),
+                              a.a_rows * 16);
           }
         }
         continue;
@@ -344,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
         sm100::tc_fence_after();
         uint32_t dg[32], du[32];
         sm100::tmem_ld_32cols(tmem + lane_addr + buf * C::kAccCols, dg);
-        if constexpr (NV == 2) sm100::tmem_ld_32cols(tmem + lane_addr + buf * C::kAccCols + kPairs, du);
+        if constexpr (NV == 2) sm100::tmem_ld_32cols(tmem + lane_addr + buf * C::kAccCols + kN, du);
         sm100::tmem_ld_wait();
         sm100::tc_fence_before();
         __syncwarp();
@@ -355,20 +352,20 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
         for (int j = 0; j < kPairs; ++j) {
           if (j >= cc) break;
           const int64_t pair = a.rows[pos + j];
-          const float g = __uint_as_float(dg[j]);
+          // Column t * 8 + j holds term t of pair j.
+          const float g = (__uint_as_float(dg[j]) + __uint_as_float(dg[kPairs + j])) +
+                          (__uint_as_float(dg[2 * kPairs + j]) + __uint_as_float(dg[3 * kPairs + j]));
           if constexpr (NV == 1) {
             if (valid) a.res[pair * a.n_out + n] = g;
           } else {
-            const float u = __uint_as_float(du[j]);
+            const float u = (__uint_as_float(du[j]) + __uint_as_float(du[kPairs + j])) +
+                            (__uint_as_float(du[2 * kPairs + j]) + __uint_as_float(du[3 * kPairs + j]));
             const float h = valid ? g / (1.f + expf(-g)) * u : 0.f;
             if (a.act && valid) a.act[pair * a.n_out + n] = h;
-            if (blk < a.o_nb) {
-              const int64_t onc = (a.o_nb + 3) / 4;
-              warp_e2m1_terms(h, lane, a.oq + a4_q_off(0, blk, a.o_nb, a.a_rows, pos + j),
-                              a.o_nb * a.a_rows * 16,
-                              a.osf + a4_sf_off(0, blk / 4, onc, a.a_rows, pos + j) + (blk & 3),
-                              onc * a.a_rows * 16);
-            }
+            if (blk < a.o_nb)
+              warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, pos + j), a.a_rows * 16,
+                              a.osf + a4_off(0, blk / 4, a.a_rows, pos + j) + (blk & 3),
+                              a.a_rows * 16);
           }
         }
       }
@@ -474,20 +471,17 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   a.act = act_f32;
   a.err = err;
   {
-    // One 16-byte row per pair = two 8-byte elements; a box line is the 32
-    // pairs of one (term, block) -- 512 contiguous bytes.
+    // One 16-byte row per pair = two 8-byte elements; a box line is the 8
+    // pairs of one (block, term) -- 128 contiguous bytes. Boxes land as
+    // [block][term][pair] (terms) and [term][pair] (scales).
     const uint64_t nc = uint64_t((pool->nb + 3) / 4);
-    const uint64_t dq[3] = {uint64_t(n_pairs) * 2, uint64_t(pool->nb), uint64_t(tc::kTerms)};
-    const uint64_t sq[2] = {uint64_t(n_pairs) * 16, uint64_t(pool->nb * n_pairs) * 16};
-    const uint32_t bq[3] = {uint32_t(tc::kPairs) * 2, uint32_t(tc::kChunk), uint32_t(tc::kTerms)};
-    const uint64_t df[3] = {uint64_t(n_pairs) * 2, nc, uint64_t(tc::kTerms)};
-    const uint64_t sf[2] = {uint64_t(n_pairs) * 16, nc * uint64_t(n_pairs) * 16};
-    const uint32_t bf[3] = {uint32_t(tc::kPairs) * 2, 1, uint32_t(tc::kTerms)};
-    const uint32_t bq8[3] = {uint32_t(tc::kPairsSmall) * 2, uint32_t(tc::kChunk),
-                             uint32_t(tc::kTerms)};
+    const uint64_t dq[3] = {uint64_t(n_pairs) * 2, uint64_t(tc::kTerms), uint64_t(pool->nb)};
+    const uint64_t sq[2] = {uint64_t(n_pairs) * 16, uint64_t(tc::kTerms * n_pairs) * 16};
+    const uint32_t bq[3] = {uint32_t(tc::kPairs) * 2, uint32_t(tc::kTerms), uint32_t(tc::kChunk)};
+    const uint64_t df[3] = {uint64_t(n_pairs) * 2, uint64_t(tc::kTerms), nc};
+    const uint32_t bf[3] = {uint32_t(tc::kPairs) * 2, uint32_t(tc::kTerms), 1};
     if (!encode_tmap_u64_3d(&a.tm_aq, a.aq, dq, sq, bq) ||
-        !encode_tmap_u64_3d(&a.tm_aq8, a.aq, dq, sq, bq8) ||
-        !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sf, bf))
+        !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sq, bf))
       return fail(MSB_ERR_CUDA, "tensor-core path: activation tensor maps could not be encoded");
   }
   return nv == 2 ? launch_tc_t<2>(a, max_active, st) : launch_tc_t<1>(a, max_active, st);
