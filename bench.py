@@ -179,27 +179,6 @@ def build_layers(n_layer, e_lo, e_hi, K, n_ff, seed):
     return layers
 
 
-class EPState:
-    """Buffers for one rank's expert-parallel layer."""
-
-    def __init__(self, world, rank, tokens, top_k, K, n_loc):
-        import torch
-        self.world, self.rank = world, rank
-        self.t_loc = tokens // world
-        self.pairs = self.t_loc * top_k
-        self.cap = self.pairs  # rows any single destination can receive from this rank
-        R = world * self.cap
-        self.send_x = torch.empty(R, K, dtype=torch.bfloat16, device="cuda")
-        self.recv_x = torch.empty_like(self.send_x)
-        self.send_e = torch.empty(R, 1, dtype=torch.int32, device="cuda")
-        self.recv_e = torch.empty_like(self.send_e)
-        self.y_loc = torch.empty(R, K, dtype=torch.float32, device="cuda")
-        self.y_back = torch.empty_like(self.y_loc)
-        self.pos = torch.empty(self.pairs, dtype=torch.int32, device="cuda")
-        self.ones = torch.ones(R, 1, dtype=torch.float32, device="cuda")
-        self.n_loc = n_loc
-
-
 def run_layer(ctx, layer, x, ids, w, y, timed_events=None):
     """One MoE FFN layer on this rank. x: [t_loc, K] bf16, ids/w: [t_loc, top_k]."""
     from moestream_b200 import ops
@@ -213,15 +192,13 @@ def run_layer(ctx, layer, x, ids, w, y, timed_events=None):
         r = ops.remap_group(ids, ga.n_slot, route=ctx["route"])
         ops.moe_ffn(ga, up, dn, x, r, w, top_k, ws=ctx["ws"], out=y)
         return
-    import torch.distributed as dist
     ep = ctx["ep"]
-    ops.ep_dispatch(ids, x, ep.n_loc, ep.world, ep.cap, ep.send_x, ep.send_e, ep.pos)
-    dist.all_to_all_single(ep.recv_x, ep.send_x)
-    dist.all_to_all_single(ep.recv_e, ep.send_e)
-    r = ops.remap_group(ep.recv_e, ga.n_slot, route=ctx["route"])
-    ops.moe_ffn(ga, up, dn, ep.recv_x, r, ep.ones, 1, ws=ctx["ws"], out=ep.y_loc)
-    dist.all_to_all_single(ep.y_back, ep.y_loc)
-    ops.ep_combine(ep.y_back, ep.pos, w, y)
+
+    def local_ffn(rows, local_ids, ones, out):
+        r = ops.remap_group(local_ids, ga.n_slot, route=ctx["route"])
+        ops.moe_ffn(ga, up, dn, rows, r, ones, 1, ws=ctx["ws"], out=out)
+
+    ep.layer(x, ids, w, local_ffn, y)
 
 
 def cpu_sample(layer0, tokens, top_k, K, n_ff, n_expert, ids0, w0, x0, threads):
@@ -318,6 +295,7 @@ def main():
     import torch
 
     from moestream_b200 import ops
+    from moestream_b200.ep import ExpertParallel
     K, n_ff, E, top_k = SHAPE["hidden"], SHAPE["n_ff"], SHAPE["n_expert"], SHAPE["top_k"]
     T, L = args.tokens, args.layers
     assert T % world == 0 and E % world == 0
@@ -337,7 +315,7 @@ def main():
     ctx = {"layers": layers, "world": world,
            "route": ops.RouteBuffers(rows_max, n_loc),
            "ws": ops.workspace(K, rows_max if world > 1 else T, 1 if world > 1 else top_k, n_loc),
-           "ep": EPState(world, rank, T, top_k, K, n_loc) if world > 1 else None}
+           "ep": ExpertParallel(world, rank, E, T, top_k, K, "cuda") if world > 1 else None}
     y = torch.empty(L, t_loc, K, dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
     t_setup = time.time() - t_setup

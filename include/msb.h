@@ -204,6 +204,15 @@ int msb_mul_mat_id_noalloc(msb_pool_t pool, const void *b_dev, int b_type,
                            const msb_route_t *route, int32_t top_k,
                            int32_t n_tok, float *res_dev, void *stream);
 
+/* Status bits of the tensor-core kernels on the current device: nonzero
+ * when a kernel's bounded wait (about one second) on its own pipeline gave
+ * up, in which case that kernel stopped early and its outputs are
+ * incomplete (1 producer, 2 accumulator release, 4 stage arrival,
+ * 8 accumulator arrival, 16 teardown drain). Kernels only set bits; call
+ * after synchronizing the streams that ran them. clear != 0 resets the
+ * word. No counterpart in the reference (ggml's CPU matmul has no waits). */
+int msb_device_status(int32_t *status, int32_t clear);
+
 /* ======================================================================== */
 /* MoE FFN layer                                                              */
 /* ======================================================================== */
@@ -233,17 +242,20 @@ int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0,
  * e / n_local as local slot e % n_local).
  *
  * Packs this rank's (token, k) rows for an equal-split all-to-all: row of
- * pair p = t*top_k + k goes to block dest = ids[p] / n_local of send_x
- * (bf16 [n_rank * cap, K]) at dest*cap + (its rank among earlier pairs with
- * that destination); send_e (int32 [n_rank * cap]) gets the local expert id,
- * -1 for unused rows; pos (int32 [n_tok * top_k]) records each pair's row,
- * -1 for invalid ids or rows beyond cap. x is f32 or bf16 [n_tok, K] with
- * byte stride x_nb1 between tokens. */
+ * pair p = t*top_k + k goes to block dest = ids[p] / n_local of the send
+ * buffer at row dest*cap + (its rank among earlier pairs with that
+ * destination). Row r's bf16 activations (K values) start at
+ * send_x + r*send_nb1 and its local expert id (int32, -1 for unused rows) is
+ * at send_e + r*send_e_nb (byte strides; the id may live in the same row as
+ * the activations, so that one exchange carries both). pos (int32
+ * [n_tok * top_k]) records each pair's row, -1 for invalid ids or rows
+ * beyond cap. x is f32 or bf16 [n_tok, K] with byte stride x_nb1 between
+ * tokens. */
 int msb_ep_dispatch(const int32_t *ids_dev, const void *x_dev, int x_type,
                     int64_t x_nb1, int32_t top_k, int32_t n_tok, int64_t K,
                     int32_t n_local, int32_t n_rank, int32_t cap,
-                    void *send_x_dev, int32_t *send_e_dev, int32_t *pos_dev,
-                    void *stream);
+                    void *send_x_dev, int64_t send_nb1, int32_t *send_e_dev,
+                    int64_t send_e_nb, int32_t *pos_dev, void *stream);
 
 /* y[t, :] = sum_k w[t, k] * back[pos[t*top_k + k], :] (k ascending), where
  * back (f32 [n_rank * cap, K]) holds the expert outputs returned by the

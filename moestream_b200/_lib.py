@@ -88,12 +88,14 @@ SIGNATURES = {
                                               ctypes.c_int64, ctypes.c_int64,
                                               ctypes.POINTER(Route), ctypes.c_int32,
                                               ctypes.c_int32, c_vp, c_vp]),
+    "msb_device_status": (ctypes.c_int, [c_i32p, ctypes.c_int32]),
     "msb_moe_ffn": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, c_vp, c_vp, ctypes.c_int,
                                    ctypes.c_int64, ctypes.POINTER(Route), c_vp, ctypes.c_int32,
                                    ctypes.c_int32, c_vp, c_vp, c_vp, ctypes.c_int64, c_vp]),
     "msb_ep_dispatch": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
-                                       ctypes.c_int32, ctypes.c_int32, c_vp, c_vp, c_vp, c_vp]),
+                                       ctypes.c_int32, ctypes.c_int32, c_vp, ctypes.c_int64,
+                                       c_vp, ctypes.c_int64, c_vp, c_vp]),
     "msb_ep_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.c_int64, c_vp, c_vp]),
     "msb_kernel_launches": (ctypes.c_uint64, []),

@@ -22,8 +22,8 @@ static constexpr int kEpThreads = 256;
 template <typename T>
 __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
     const int32_t *ids, const char *x, int64_t x_nb1, int32_t top_k, int32_t n_pairs,
-    int64_t K, int32_t n_local, int32_t n_rank, int32_t cap, __nv_bfloat16 *send_x,
-    int32_t *send_e, int32_t *pos) {
+    int64_t K, int32_t n_local, int32_t n_rank, int32_t cap, char *send_x, int64_t send_nb1,
+    char *send_e, int64_t send_e_nb, int32_t *pos) {
   __shared__ int warp_cnt[kEpThreads / 32];
   const int p = blockIdx.x;
   const int e = ids[p];
@@ -48,11 +48,11 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
   const int row = dest * cap + rank;
   if (threadIdx.x == 0) {
     pos[p] = row;
-    send_e[row] = e - dest * n_local;
+    *reinterpret_cast<int32_t *>(send_e + int64_t(row) * send_e_nb) = e - dest * n_local;
   }
   const int t = p / top_k;
   const T *src = reinterpret_cast<const T *>(x + int64_t(t) * x_nb1);
-  __nv_bfloat16 *dst = send_x + int64_t(row) * K;
+  __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(send_x + int64_t(row) * send_nb1);
   for (int64_t i = threadIdx.x; i < K; i += kEpThreads) {
     if constexpr (sizeof(T) == 2) dst[i] = src[i];
     else dst[i] = __float2bfloat16_rn(src[i]);
@@ -78,23 +78,32 @@ __global__ void ep_combine_kernel(const float *back, const int32_t *pos, const f
 extern "C" int msb_ep_dispatch(const int32_t *ids_dev, const void *x_dev, int x_type,
                                int64_t x_nb1, int32_t top_k, int32_t n_tok, int64_t K,
                                int32_t n_local, int32_t n_rank, int32_t cap, void *send_x_dev,
-                               int32_t *send_e_dev, int32_t *pos_dev, void *stream) {
+                               int64_t send_nb1, int32_t *send_e_dev, int64_t send_e_nb,
+                               int32_t *pos_dev, void *stream) {
   MSB_CHECK_ARG(top_k > 0 && n_tok >= 0 && K > 0 && n_local > 0 && n_rank > 0 && cap > 0,
                 "msb_ep_dispatch: bad shape");
   MSB_CHECK_ARG(send_x_dev && send_e_dev && pos_dev && (n_tok == 0 || (ids_dev && x_dev)),
                 "msb_ep_dispatch: null argument");
+  MSB_CHECK_ARG(send_nb1 >= 2 * K && send_nb1 % 2 == 0 && send_e_nb >= 4 && send_e_nb % 4 == 0 &&
+                    reinterpret_cast<uintptr_t>(send_e_dev) % 4 == 0,
+                "msb_ep_dispatch: bad send strides");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  MSB_CUDA_TRY(cudaMemsetAsync(send_e_dev, 0xFF, sizeof(int32_t) * size_t(n_rank) * cap, st));
+  // Every id starts as -1 (unused row): one 4-byte column of send_e_nb pitch.
+  MSB_CUDA_TRY(cudaMemset2DAsync(send_e_dev, size_t(send_e_nb), 0xFF, sizeof(int32_t),
+                                 size_t(n_rank) * cap, st));
   const int n_pairs = top_k * n_tok;
   if (n_pairs == 0) return MSB_OK;
   const char *x = static_cast<const char *>(x_dev);
-  auto *sx = static_cast<__nv_bfloat16 *>(send_x_dev);
+  auto *sx = static_cast<char *>(send_x_dev);
+  auto *se = reinterpret_cast<char *>(send_e_dev);
   if (x_type == MSB_TYPE_BF16)
     msb::ep_dispatch_kernel<__nv_bfloat16><<<n_pairs, msb::kEpThreads, 0, st>>>(
-        ids_dev, x, x_nb1, top_k, n_pairs, K, n_local, n_rank, cap, sx, send_e_dev, pos_dev);
+        ids_dev, x, x_nb1, top_k, n_pairs, K, n_local, n_rank, cap, sx, send_nb1, se, send_e_nb,
+        pos_dev);
   else if (x_type == MSB_TYPE_F32)
     msb::ep_dispatch_kernel<float><<<n_pairs, msb::kEpThreads, 0, st>>>(
-        ids_dev, x, x_nb1, top_k, n_pairs, K, n_local, n_rank, cap, sx, send_e_dev, pos_dev);
+        ids_dev, x, x_nb1, top_k, n_pairs, K, n_local, n_rank, cap, sx, send_nb1, se, send_e_nb,
+        pos_dev);
   else
     return msb::fail(MSB_ERR_INVALID, "msb_ep_dispatch: activation type %d", x_type);
   msb::count_launch();

@@ -36,7 +36,7 @@ int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb
                  const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st);
 int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
-                  uint8_t *act_out, float *act_f32, int *err, int max_active, cudaStream_t st);
+                  uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st);
 
 // MXFP4 arithmetic: 0 = tensor cores where the shapes allow, 1 = CUDA cores
 // with int8 activations (ggml's q8_0 form) everywhere.
@@ -419,12 +419,11 @@ extern "C" int64_t msb_workspace_bytes(int64_t K_max, int32_t n_tok, int32_t top
   q8 = align_up(q8 + pairs * nb * 32, 256);
   q8 = align_up(q8 + pairs * nb * 4, 256);
   q8 = align_up(q8 + pairs * K_max * 4, 256);
-  // Tensor-core path: activation terms in and SwiGLU out, down result, flag.
+  // Tensor-core path: activation terms in and SwiGLU out, down result.
   int64_t tcb = 0;
   tcb = align_up(tcb + tc_act_bytes(nb, pairs), 256);
   tcb = align_up(tcb + tc_act_bytes(nb, pairs), 256);
   tcb = align_up(tcb + pairs * K_max * 4, 256);
-  tcb += 256;
   return (q8 > tcb ? q8 : tcb) + 256;
 }
 
@@ -458,8 +457,6 @@ extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, in
     // Tensor cores: activation terms per pair (grouped order), then one
     // projection writing res directly.
     uint8_t *act = ws;
-    int *err = reinterpret_cast<int *>(ws + align_up(tc_act_bytes(pool->nb, pairs), 256));
-    MSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
     const size_t es = b_type == MSB_TYPE_BF16 ? 2 : 4;
     (void)es;
     if (int rc = tc_act_terms(b_dev, b_type, b_ne1, b_nb1, b_nb2, top_k, route->rows, pairs,
@@ -467,7 +464,7 @@ extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, in
       return rc;
     const int64_t row0[2] = {0, 0};
     const msb_pool_s *pools[2] = {pool, pool};
-    return tc_projection(pools, 1, row0, pool->N, route, pairs, act, res_dev, nullptr, nullptr, err,
+    return tc_projection(pools, 1, row0, pool->N, route, pairs, act, res_dev, nullptr, nullptr,
                          max_active, st);
   }
   const int64_t n_rows = int64_t(n_tok) * b_ne1;
@@ -525,8 +522,6 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
     o = align_up(o + tc_act_bytes(n_ff / 32, pairs), 256);
     float *rd = reinterpret_cast<float *>(ws + o);
     o = align_up(o + pairs * down->N * 4, 256);
-    int *err = reinterpret_cast<int *>(ws + o);
-    MSB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
     if (int rc = tc_act_terms(x_dev, x_type, 1, x_nb1, x_nb1, top_k, route->rows, pairs, gate->nb,
                               xa, st))
       return rc;
@@ -535,7 +530,7 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
     const bool timed = g_gate_up_start && g_gate_up_stop;
     if (timed) MSB_CUDA_TRY(cudaEventRecord(g_gate_up_start, st));
     if (int rc = tc_projection(gu_pools, 2, rows_gu, n_ff, route, pairs, xa, nullptr, ha, act_dev,
-                               err, max_active_tc, st))
+                               max_active_tc, st))
       return rc;
     if (timed) {
       MSB_CUDA_TRY(cudaEventRecord(g_gate_up_stop, st));
@@ -544,7 +539,7 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
     const int64_t rows_dn[2] = {0, 0};
     const msb_pool_s *dn_pools[2] = {down, down};
     if (int rc = tc_projection(dn_pools, 1, rows_dn, down->N, route, pairs, ha, rd, nullptr, nullptr,
-                               err, max_active_tc, st))
+                               max_active_tc, st))
       return rc;
     const int64_t total = down->N * n_tok;
     combine_kernel<<<unsigned((total + 255) / 256), 256, 0, st>>>(rd, w_dev, top_k, down->N, n_tok,
@@ -657,9 +652,8 @@ extern "C" int msb_mul_mat_id_noalloc(msb_pool_t pool, const void *b_dev, int b_
                 pool->device);
   void *scratch = nullptr;
   if (int rc = noalloc_scratch(dev, &scratch)) return rc;
-  // The only workspace word that must start at zero, the kernels' error
-  // flag, is cleared by msb_mul_mat_id on every call; everything else in
-  // the workspace is written before it is read.
+  // Nothing in the workspace has to start at zero: every byte a call reads
+  // is written earlier in the same call.
   return msb_mul_mat_id(pool, b_dev, b_type, b_ne1, b_nb1, b_nb2, route, top_k, n_tok, res_dev,
                         scratch, kNoAllocScratchBytes, stream);
 }

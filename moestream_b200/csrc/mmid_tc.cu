@@ -35,8 +35,10 @@
 //                    (rows), releases the buffer, then stores.
 // With two views (gate and up) the epilogue applies SwiGLU and writes the
 // down projection's activation terms directly.
-// Every mbarrier wait is bounded; a wait that gives up sets *err and the CTA
-// stops issuing work and releases its tensor memory.
+// Every mbarrier wait is bounded (about a second); a wait that gives up sets
+// a bit of the device status word (msb_device_status) and the CTA stops
+// issuing work, waits (bounded) for its copies and MMAs in flight and
+// releases its tensor memory.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -92,8 +94,13 @@ struct Args {
   uint8_t *oq, *osf;         // two views: terms of silu(gate) * up
   int64_t o_nb;              // n_out / 32
   float *act;                // two views, optional: f32 silu(gate) * up
-  int *err;
 };
+
+// Status bits of the tensor-core kernels on this device (see
+// msb_device_status): which bounded wait gave up.
+__device__ int g_status;
+constexpr int kStatusProducer = 1, kStatusAccEmpty = 2, kStatusFull = 4, kStatusAccFull = 8,
+              kStatusDrain = 16;
 
 // Byte offset of the 16-byte record of (term t, block or chunk b, row r) in
 // an activation-term buffer of `rows` rows: [b][t][r][16 B]. The records of
@@ -137,25 +144,73 @@ __device__ __forceinline__ void warp_e2m1_terms(float r, int lane, uint8_t *q_t0
   }
 }
 
+// The same split with 8 lanes per block: lane l of the group holds elements
+// 2l, 2l+1, 2l+16, 2l+17 (r[0..3]) and writes packed bytes 2l and 2l+1 of
+// each term. All 32 lanes of the warp must call it (the amax reduction
+// shuffles within each 8-lane group); `store` masks the writes.
+__device__ __forceinline__ void group_e2m1_terms(float (&r)[4], int l, bool store, uint8_t *q_t0,
+                                                 int64_t q_step, uint8_t *sf_t0, int64_t sf_step) {
+#pragma unroll
+  for (int t = 0; t < kTerms; ++t) {
+    float amax = fmaxf(fmaxf(fabsf(r[0]), fabsf(r[1])), fmaxf(fabsf(r[2]), fabsf(r[3])));
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    int k = -127;
+    if (amax > 0.f) {
+      int ex;
+      const float m = frexpf(amax, &ex);
+      k = m > 0.75f ? ex - 2 : ex - 3;
+    }
+    const bool skip = k < -126;
+    uint32_t nib[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int code = 0, neg = 0;
+      if (!skip) {
+        const float v = fabsf(r[e]) * __int_as_float((127 - k) << 23);  // exact
+        code = (v >= 0.25f) + (v >= 0.75f) + (v >= 1.25f) + (v >= 1.75f) + (v >= 2.5f) +
+               (v >= 3.5f) + (v >= 5.f);
+        neg = (r[e] < 0.f) && code > 0;
+        const float mag = code < 5 ? 0.5f * code : (code == 5 ? 3.f : (code == 6 ? 4.f : 6.f));
+        const float q = mag * __int_as_float((k + 127) << 23);          // exact
+        r[e] = neg ? r[e] + q : r[e] - q;                               // exact
+      }
+      nib[e] = uint32_t(code | (neg << 3));
+    }
+    if (store) {
+      *reinterpret_cast<uint16_t *>(q_t0 + t * q_step + 2 * l) =
+          uint16_t(nib[0] | (nib[2] << 4) | (nib[1] << 8) | (nib[3] << 12));
+      if (l == 0) sf_t0[t * sf_step] = skip ? uint8_t(0) : uint8_t(k > 127 ? 254 : k + 127);
+    }
+  }
+}
+
 // Activations of every pair in grouped order into the term layout:
 // q [nb][kTerms][rows][16 B], sf [ceil(nb/4)][kTerms][rows][16 B] (byte b%4).
+// One warp per (pair position, chunk of 4 blocks); 8 lanes per block.
 template <typename T>
 __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t nb1, int64_t nb2,
                                                         int32_t ne1, int32_t top_k,
                                                         const int32_t *rows, int64_t n_pairs,
                                                         int64_t nb, uint8_t *q, uint8_t *sf) {
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, grp = lane >> 3, l = lane & 7;
+  const int64_t nc = (nb + 3) / 4;
   const int64_t item = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (item >= n_pairs * nb) return;
-  const int64_t pos = item / nb, blk = item % nb;
+  if (item >= n_pairs * nc) return;   // whole warps only
+  const int64_t pos = item / nc, blk = (item % nc) * 4 + grp;
+  const bool live = blk < nb;
   const int64_t pair = rows[pos];
-  const int64_t t = pair / top_k, k1 = (pair % top_k) % ne1;
-  const char *p = b + t * nb2 + k1 * nb1 + (blk * 32 + lane) * int64_t(sizeof(T));
-  float v;
-  if constexpr (sizeof(T) == 4) v = *reinterpret_cast<const float *>(p);
-  else v = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(p));
-  warp_e2m1_terms(v, lane, q + a4_off(0, blk, n_pairs, pos), n_pairs * 16,
-                  sf + a4_off(0, blk / 4, n_pairs, pos) + (blk & 3), n_pairs * 16);
+  const int64_t tok = pair / top_k, k1 = (pair % top_k) % ne1;
+  const T *x = reinterpret_cast<const T *>(b + tok * nb2 + k1 * nb1) + (live ? blk : 0) * 32;
+  float r[4];
+  const int el[4] = {2 * l, 2 * l + 1, 2 * l + 16, 2 * l + 17};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if constexpr (sizeof(T) == 4) r[e] = live ? float(x[el[e]]) : 0.f;
+    else r[e] = live ? __bfloat162float(x[el[e]]) : 0.f;
+  }
+  group_e2m1_terms(r, l, live, q + a4_off(0, blk, n_pairs, pos), n_pairs * 16,
+                   sf + a4_off(0, blk / 4, n_pairs, pos) + (blk & 3), n_pairs * 16);
 }
 
 template <int NV>
@@ -164,7 +219,6 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
   constexpr int kStages = C::kStages;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t nc_in = (a.nb + 3) / 4;
   const int64_t n_chunks = (a.nb + kChunk - 1) / kChunk;
   const int64_t n_items = int64_t(a.active[0]) * a.tiles;
 
@@ -213,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
           for (int64_t i = 0; i < n_chunks; ++i, ++it) {
             const int s = it % kStages;
             if (!sm100::mbar_wait_bounded(&empty[s], ((it / kStages) & 1) ^ 1)) {
-              atomicOr(a.err, 1);
+              atomicOr(&g_status, kStatusProducer);
               *abort_v = 1;
               break;
             }
@@ -241,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
       // No copy may still be landing in shared memory when the CTA exits
       // (only possible after an abort): wait for the last stages issued.
       for (uint32_t k = it > uint32_t(kStages) ? it - kStages : 0; k < it; ++k)
-        if (!sm100::mbar_wait_bounded(&full[k % kStages], (k / kStages) & 1)) atomicOr(a.err, 16);
+        if (!sm100::mbar_wait_bounded(&full[k % kStages], (k / kStages) & 1)) atomicOr(&g_status, kStatusDrain);
     }
   } else if (warp == 1) {
     // ---- scale-factor copies and MMA issue ----
@@ -254,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
         for (int g0 = 0; g0 < c_total && !*abort_v; g0 += kPairs, ++acc) {
           const int buf = acc & 1;
           if (!sm100::mbar_wait_bounded(&acc_empty[buf], ((acc >> 1) & 1) ^ 1)) {
-            atomicOr(a.err, 2);
+            atomicOr(&g_status, kStatusAccEmpty);
             *abort_v = 1;
             break;
           }
@@ -263,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
           for (int64_t i = 0; i < n_chunks; ++i, ++it) {
             const int s = it % kStages;
             if (!sm100::mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
-              atomicOr(a.err, 4);
+              atomicOr(&g_status, kStatusFull);
               *abort_v = 1;
               break;
             }
@@ -297,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
       // Every MMA and scale-factor copy is complete before tensor memory is
       // released.
       sm100::tc_commit(drained);
-      if (!sm100::mbar_wait_bounded(drained, 0)) atomicOr(a.err, 16);
+      if (!sm100::mbar_wait_bounded(drained, 0)) atomicOr(&g_status, kStatusDrain);
     }
   } else {
     // ---- epilogue (warps 2-5) ----
@@ -313,18 +367,25 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
       const int c_total = a.counts[slot];
       const int64_t pos0 = a.offsets[slot];
       if (slot == a.zero_slot) {
-        // Every weight of the zero slot is 0: write the exact result.
+        // Every weight of the zero slot is 0, so the exact result is 0; for
+        // the down projection's input, 0 splits into four zero terms with
+        // scale byte 0 (stored directly, 8 pairs x 4 terms per warp step).
         for (int j = 0; j < c_total; ++j) {
           const int64_t pair = a.rows[pos0 + j];
           if constexpr (NV == 1) {
             if (valid) a.res[pair * a.n_out + n] = 0.f;
           } else {
             if (a.act && valid) a.act[pair * a.n_out + n] = 0.f;
-            if (blk < a.o_nb)
-              warp_e2m1_terms(0.f, lane, a.oq + a4_off(0, blk, a.a_rows, pos0 + j),
-                              a.a_rows * 16,
-                              a.osf + a4_off(0, blk / 4, a.a_rows, pos0 + j) + (blk & 3),
-                              a.a_rows * 16);
+          }
+        }
+        if constexpr (NV == 2) {
+          if (blk < a.o_nb) {
+            const int t = lane & 3;
+            for (int j = lane >> 2; j < c_total; j += 8) {
+              *reinterpret_cast<uint4 *>(a.oq + a4_off(t, blk, a.a_rows, pos0 + j)) =
+                  make_uint4(0u, 0u, 0u, 0u);
+              a.osf[a4_off(t, blk / 4, a.a_rows, pos0 + j) + (blk & 3)] = 0;
+            }
           }
         }
         continue;
@@ -334,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
         const int64_t pos = pos0 + g0;
         const int buf = acc & 1;
         if (!sm100::mbar_wait_bounded(&acc_full[buf], (acc >> 1) & 1)) {
-          atomicOr(a.err, 8);
+          atomicOr(&g_status, kStatusAccFull);
           *abort_v = 1;
           break;
         }
@@ -398,7 +459,7 @@ int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb
                  const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st) {
   if (n_pairs == 0) return MSB_OK;
   uint8_t *q = ws, *sf = ws + int64_t(tc::kTerms) * nb * n_pairs * 16;
-  const int64_t grid = (n_pairs * nb + 7) / 8;
+  const int64_t grid = (n_pairs * ((nb + 3) / 4) + 7) / 8;
   const char *p = static_cast<const char *>(b);
   if (b_type == MSB_TYPE_F32)
     tc::act_terms_kernel<float><<<unsigned(grid), 256, 0, st>>>(p, nb1, nb2, int32_t(ne1), top_k,
@@ -441,7 +502,7 @@ static int launch_tc_t(const tc::Args &a, int max_active, cudaStream_t st) {
 // act_out, nv == 1 writes res.
 int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
-                  uint8_t *act_out, float *act_f32, int *err, int max_active, cudaStream_t st) {
+                  uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st) {
   const msb_pool_s *pool = pools[0];
   tc::Args a{};
   for (int v = 0; v < 2; ++v) {
@@ -469,7 +530,6 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   a.o_nb = n_out / 32;
   a.osf = act_out ? act_out + int64_t(tc::kTerms) * a.o_nb * n_pairs * 16 : nullptr;
   a.act = act_f32;
-  a.err = err;
   {
     // One 16-byte row per pair = two 8-byte elements; a box line is the 8
     // pairs of one (block, term) -- 128 contiguous bytes. Boxes land as
@@ -488,3 +548,15 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
 }
 
 }  // namespace msb
+
+extern "C" int msb_device_status(int32_t *status, int32_t clear) {
+  MSB_CHECK_ARG(status, "msb_device_status: null status");
+  int v = 0;
+  MSB_CUDA_TRY(cudaMemcpyFromSymbol(&v, msb::tc::g_status, sizeof(int)));
+  *status = v;
+  if (clear && v) {
+    const int zero = 0;
+    MSB_CUDA_TRY(cudaMemcpyToSymbol(msb::tc::g_status, &zero, sizeof(int)));
+  }
+  return MSB_OK;
+}

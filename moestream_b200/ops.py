@@ -34,6 +34,14 @@ def tc_eligible(wtype, K):
     return WEIGHT_TYPES.get(wtype, wtype) == TYPE_MXFP4 and K % 64 == 0
 
 
+def device_status(clear=False):
+    """Status bits of the tensor-core kernels on the current device (0 when
+    every bounded wait completed). Synchronize the streams first."""
+    v = ctypes.c_int32(0)
+    check(lib().msb_device_status(ctypes.byref(v), 1 if clear else 0))
+    return v.value
+
+
 def expert_bytes(wtype, K, N):
     return int(lib().msb_expert_bytes(WEIGHT_TYPES.get(wtype, wtype), K, N))
 
@@ -164,13 +172,17 @@ def quantize_rows(wtype, src, stream=None):
 
 
 def ep_dispatch(ids, x, n_local, n_rank, cap, send_x, send_e, pos, stream=None):
-    """Packs this rank's (token, k) rows for an equal-split all-to-all."""
+    """Packs this rank's (token, k) rows for an equal-split all-to-all.
+    send_x: bf16 [n_rank * cap, >= K] (row stride free); send_e: int32
+    [n_rank * cap] view with any row stride (it may alias a column of the
+    send_x rows, so that one exchange carries both)."""
     n_tok, top_k = ids.shape
     assert ids.is_contiguous() and x.stride(1) == 1 and send_x.dtype == torch.bfloat16
+    assert send_x.stride(1) == 1 and send_e.dtype == torch.int32
     check(lib().msb_ep_dispatch(_ptr(ids), _ptr(x), _ACT_TYPES[x.dtype],
                                 x.stride(0) * x.element_size(), top_k, n_tok, x.shape[1],
-                                n_local, n_rank, cap, _ptr(send_x), _ptr(send_e), _ptr(pos),
-                                _stream(stream)))
+                                n_local, n_rank, cap, _ptr(send_x), send_x.stride(0) * 2,
+                                _ptr(send_e), send_e.stride(0) * 4, _ptr(pos), _stream(stream)))
 
 
 def ep_combine(back, pos, w, y, stream=None):

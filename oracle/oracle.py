@@ -314,3 +314,48 @@ def max_abs_normalized(got, want):
     want = np.asarray(want, dtype=np.float64)
     den = np.max(np.abs(want))
     return float(np.max(np.abs(got - want)) / (den if den > 0 else 1.0))
+
+
+# --------------------------------------------------------------------------
+# Expert-parallel packing (no counterpart in the reference, which is
+# single-process): restates the meaning of msb_ep_dispatch / msb_ep_combine
+# on CPU torch tensors, with the same signatures as moestream_b200.ops, so
+# the host-side exchange logic can run with gloo ranks on CPU.
+# --------------------------------------------------------------------------
+def ep_dispatch(ids, x, n_local, n_rank, cap, send_x, send_e, pos):
+    """Row of pair p = t*top_k + k goes to block ids[p] // n_local at its rank
+    among earlier pairs with that destination; unused rows get id -1."""
+    import torch
+    n_tok, top_k = ids.shape
+    flat = ids.reshape(-1).tolist()
+    send_e.fill_(-1)
+    used = [0] * n_rank
+    for p, e in enumerate(flat):
+        dest = e // n_local if 0 <= e < n_local * n_rank else -1
+        if dest < 0 or used[dest] >= cap:
+            if dest >= 0:
+                used[dest] += 1
+            pos[p] = -1
+            continue
+        row = dest * cap + used[dest]
+        used[dest] += 1
+        pos[p] = row
+        send_e[row] = e - dest * n_local
+        send_x[row] = x[p // top_k].to(torch.bfloat16)
+
+
+def ep_combine(back, pos, w, y):
+    """y[t] = sum_k w[t, k] * back[pos[t, k]] in k order, each step one f32
+    fused multiply-add (pos -1 adds nothing)."""
+    import torch
+    n_tok, top_k = w.shape
+    p = pos.reshape(n_tok, top_k)
+    acc = torch.zeros(n_tok, back.shape[1], dtype=torch.float32)
+    for k in range(top_k):
+        r = p[:, k].long()
+        ok = (r >= 0).unsqueeze(1)
+        rows = back[r.clamp(min=0)].to(torch.float32)
+        fused = (w[:, k:k + 1].double() * rows.double() + acc.double()).to(torch.float32)
+        acc = torch.where(ok, fused, acc)
+    y.copy_(acc)
+    return y

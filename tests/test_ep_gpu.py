@@ -1,0 +1,129 @@
+"""Expert-parallel kernels and layer on GPUs.
+
+- msb_ep_dispatch / msb_ep_combine against the oracle's restatement
+  (bit-exact: a row copy, and f32 fused multiply-adds in k order), on one GPU.
+- The whole expert-parallel MoE layer (moestream_b200.ep over NCCL, two
+  ranks, tensor-core FFN on each) against the oracle's single-process layer;
+  needs two GPUs and is skipped with fewer.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import oracle as O
+from tests.helpers import experts
+
+pytestmark = pytest.mark.gpu
+
+
+def test_dispatch_and_combine_match_oracle():
+    from moestream_b200 import ops
+    from moestream_b200.ep import ExpertParallel
+    world, n_expert, n_tok, top_k, K = 4, 16, 12, 3, 96
+    g = torch.Generator().manual_seed(3)
+    ids = torch.stack([torch.randperm(n_expert, generator=g)[:top_k] for _ in range(n_tok)])
+    ids = ids.to(torch.int32)
+    ids[2, 1] = -1
+    ids[5, 0] = n_expert          # out of range: dropped
+    x = torch.randn(n_tok, K, generator=g)
+    w = torch.rand(n_tok, top_k, generator=g)
+    # Device path (rank 0 of 4 only packs; every block is checked).
+    dev = ExpertParallel(world, 0, n_expert, n_tok * world, top_k, K, "cuda")
+    dev.send.zero_()
+    ops.ep_dispatch(ids.cuda(), x.cuda(), dev.n_local, world, dev.cap, dev.send[:, :K],
+                    dev.send_ids()[:, 0], dev.pos)
+    cpu = ExpertParallel(world, 0, n_expert, n_tok * world, top_k, K, "cpu",
+                         dispatch=O.ep_dispatch, combine=O.ep_combine)
+    cpu.send.zero_()
+    O.ep_dispatch(ids, x, cpu.n_local, world, cpu.cap, cpu.send[:, :K], cpu.send_ids()[:, 0],
+                  cpu.pos)
+    torch.cuda.synchronize()
+    assert torch.equal(dev.pos.cpu(), cpu.pos)
+    assert torch.equal(dev.send.cpu().view(torch.int16), cpu.send.view(torch.int16))
+    back = torch.randn(world * cpu.cap, K, generator=g)
+    y_dev = ops.ep_combine(back.cuda(), dev.pos, w.cuda(), torch.empty(n_tok, K, device="cuda"))
+    y_cpu = O.ep_combine(back, cpu.pos, w, torch.empty(n_tok, K))
+    assert torch.equal(y_dev.cpu(), y_cpu)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+N_EXPERT, N_TOK, TOP_K, K, N_FF = 8, 8, 2, 512, 256
+
+
+def _layer_inputs():
+    rng = np.random.default_rng(21)
+    gate = experts("mxfp4", N_EXPERT, K, N_FF, seed=31)
+    up = experts("mxfp4", N_EXPERT, K, N_FF, seed=32)
+    down = experts("mxfp4", N_EXPERT, N_FF, K, seed=33)
+    x = torch.from_numpy(rng.normal(0, 1, size=(N_TOK, K)).astype(np.float32)).to(torch.bfloat16)
+    ids = np.stack([rng.permutation(N_EXPERT)[:TOP_K] for _ in range(N_TOK)]).astype(np.int32)
+    w = rng.random((N_TOK, TOP_K)).astype(np.float32)
+    return gate, up, down, x, ids, w
+
+
+def _rank_main(rank, world, port, out_q):
+    import torch.distributed as dist
+
+    from moestream_b200 import ops
+    from moestream_b200.ep import ExpertParallel
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        gate, up, down, x, ids, w = _layer_inputs()
+        ep = ExpertParallel(world, rank, N_EXPERT, N_TOK, TOP_K, K, "cuda")
+        mine = range(rank * ep.n_local, (rank + 1) * ep.n_local)
+        pools = {}
+        for role, mats, kk, nn in (("gate", gate, K, N_FF), ("up", up, K, N_FF),
+                                   ("down", down, N_FF, K)):
+            pools[role] = ops.SlotPool("mxfp4", kk, nn, ep.n_local)
+            pools[role].fill(list(range(ep.n_local)),
+                             [torch.from_numpy(mats[e]).pin_memory() for e in mine])
+        route = ops.RouteBuffers(world * ep.cap, ep.n_local)
+
+        def local_ffn(rows, local_ids, ones, out):
+            r = ops.remap_group(local_ids, ep.n_local, route=route)
+            ops.moe_ffn(pools["gate"], pools["up"], pools["down"], rows, r, ones, 1, out=out)
+
+        lo = rank * ep.t_loc
+        y = torch.empty(ep.t_loc, K, device="cuda")
+        ep.layer(x[lo:lo + ep.t_loc].cuda(), torch.from_numpy(ids[lo:lo + ep.t_loc]).cuda(),
+                 torch.from_numpy(w[lo:lo + ep.t_loc]).cuda(), local_ffn, y)
+        torch.cuda.synchronize()
+        slab = {r: np.concatenate([m, np.zeros((1, m.shape[1]), np.uint8)])
+                for r, m in (("gate", gate), ("up", up), ("down", down))}
+        want, _ = O.moe_ffn("mxfp4", slab["gate"], slab["up"], slab["down"], K, N_FF,
+                            x.float().numpy(), ids, w, mode="e2m1x4")
+        err = O.max_abs_normalized(y.cpu().numpy(), want[lo:lo + ep.t_loc])
+        out_q.put((rank, float(err)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_layer_matches_oracle():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    codes = [p.exitcode for p in procs]
+    assert codes == [0] * world, codes
+    errs = dict(q.get(timeout=5) for _ in range(world))
+    # Same tolerance as the single-GPU layer in the tensor-core form.
+    assert all(e < 1e-3 for e in errs.values()), errs

@@ -153,3 +153,19 @@ def test_zero_slot_exact_zero_even_from_memory(path):
     b = np.random.default_rng(0).normal(0, 1, size=(2, 1, 128)).astype(np.float32)
     got = gpu_mmid(pool, b, np.full((2, 3), 3, dtype=np.int32))
     assert np.all(got == 0.0)
+
+
+def test_device_status_clear_after_tensor_core_runs():
+    """Every bounded wait of the tensor-core kernels completed in the runs
+    above and in this one (the status word holds no bit)."""
+    from moestream_b200 import ops
+    ops.set_mxfp4_path("tc")
+    wtype, K, N, n_slot = "mxfp4", 512, 256, 6
+    ex = experts(wtype, n_slot, K, N, seed=11)
+    pool = make_pool(wtype, K, N, n_slot, [ex[e] for e in range(n_slot)], list(range(n_slot)))
+    rng = np.random.default_rng(12)
+    b = rng.normal(0, 1, size=(20, 1, K)).astype(np.float32)
+    ids = rng.integers(0, n_slot + 1, size=(20, 4)).astype(np.int32)
+    gpu_mmid(pool, b, ids)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
