@@ -24,9 +24,7 @@ path (the oracle) on the host cores on a bounded sample of the workload.
 import argparse
 import json
 import os
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -47,6 +45,10 @@ def parse():
     ap.add_argument("--layers", type=int, default=SHAPE["n_layer"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--transport", default="peers", choices=["peers", "collective"],
+                    help="expert-parallel exchange: NVLink peer-memory kernels or NCCL all-to-all")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch every kernel from the host instead of replaying CUDA graphs")
     return ap.parse_args()
 
 
@@ -54,52 +56,64 @@ def parse():
 # Clock sampling during the timed region
 # ---------------------------------------------------------------------------
 class Clocks:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock, power and clock-event reasons of one GPU every 10 ms
+    from a thread (NVML reads only; nothing is changed). Falls back to
+    nvidia-smi when NVML cannot be loaded."""
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, device):
+        import threading
         self.device = device
-        self.f = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
-        self.p = None
+        self.rows = []
+        self.stop_ev = threading.Event()
+        self.thread = None
+        self.err = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        p = torch.cuda.get_device_properties(self.device)
+        bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+
+    def _run(self, nv, h):
+        bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        while not self.stop_ev.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((sm, pw, [n for n, b in zip(self.REASONS, bits) if rs & b]))
+            except Exception as e:  # keep the bench running; report why
+                self.err = str(e)
+                return
+            self.stop_ev.wait(0.01)
 
     def start(self):
+        import threading
         try:
-            self.p = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=self.f, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.p = None
+            nv, h = self._handle()
+            self.max_sm = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        except Exception as e:
+            self.err = f"NVML unavailable: {e}"
+            return
+        self.thread = threading.Thread(target=self._run, args=(nv, h), daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if self.p is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.p.terminate()
-        try:
-            self.p.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.p.kill()
-        self.f.flush()
-        rows = []
-        with open(self.f.name) as fh:
-            for line in fh:
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
-        os.unlink(self.f.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = sorted(float(r[1]) for r in rows)
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for n, v in zip(names, r[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][2]),
-                "reasons": sorted(reasons), "samples": len(rows),
-                "power_w_max": max(float(r[3]) for r in rows)}
+        if self.thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "no sampler"]}
+        self.stop_ev.set()
+        self.thread.join(timeout=5)
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "no samples"]}
+        sm = sorted(r[0] for r in self.rows)
+        reasons = sorted({n for r in self.rows for n in r[2]})
+        return {"sm_mhz": float(sm[len(sm) // 2]), "sm_max_mhz": float(self.max_sm),
+                "reasons": reasons, "samples": len(self.rows),
+                "power_w_max": round(max(r[1] for r in self.rows), 1)}
 
 
 # ---------------------------------------------------------------------------
@@ -315,21 +329,34 @@ def main():
     ctx = {"layers": layers, "world": world,
            "route": ops.RouteBuffers(rows_max, n_loc),
            "ws": ops.workspace(K, rows_max if world > 1 else T, 1 if world > 1 else top_k, n_loc),
-           "ep": ExpertParallel(world, rank, E, T, top_k, K, "cuda") if world > 1 else None}
+           "ep": (ExpertParallel(world, rank, E, T, top_k, K, "cuda", transport=args.transport)
+                  if world > 1 else None)}
     y = torch.empty(L, t_loc, K, dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
     t_setup = time.time() - t_setup
 
-    def step(s, events=None):
+    def step(x_s, ids_s, w_s, events=None):
         for layer in range(L):
             ev = events[layer] if events is not None else None
-            run_layer(ctx, layer, x_loc[s], ids_loc[s, layer], w_loc[s, layer], y[layer], ev)
+            run_layer(ctx, layer, x_s, ids_s[layer], w_s[layer], y[layer], ev)
+
+    lib = ops.lib()
+
+    def capture(fn):
+        """CUDA graph of one step (the launches of 36 layers replay without
+        host work); returns the graph and the library kernels it holds."""
+        graph = torch.cuda.CUDAGraph()
+        c0 = int(lib.msb_kernel_launches())
+        with torch.cuda.graph(graph):
+            fn()
+        return graph, int(lib.msb_kernel_launches()) - c0
 
     for s in range(args.warmup):
-        step(s)
+        step(x_loc[s], ids_loc[s], w_loc[s])
     torch.cuda.synchronize()
     barrier(world)
-    # Dominant kernel timing: events around every fused gate/up launch.
+    # Dominant kernel timing: events around every fused gate/up launch,
+    # recorded by the graphs as external event nodes.
     gate_ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 for _ in range(L)] for _ in range(args.steps)]
     for pair in gate_ev:  # torch creates the CUDA event on its first record
@@ -337,20 +364,38 @@ def main():
             a.record()
             b.record()
     torch.cuda.synchronize()
+    graphs, launches = [], 0
+    if args.eager:
+        launches0 = int(lib.msb_kernel_launches())
+    else:
+        for i in range(args.steps):
+            s = args.warmup + i
+            g_i, n_i = capture(lambda: step(x_loc[s], ids_loc[s], w_loc[s], gate_ev[i]))
+            graphs.append(g_i)
+            launches += n_i
+        # First replay of each graph uploads it; not timed.
+        for g_i in graphs:
+            g_i.replay()
+    torch.cuda.synchronize()
     clocks = Clocks(local)
     clocks.start()
-    launches0 = int(ops.lib().msb_kernel_launches())
+    time.sleep(0.05)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     t0.record()
     for i in range(args.steps):
-        step(args.warmup + i, gate_ev[i])
+        if args.eager:
+            s = args.warmup + i
+            step(x_loc[s], ids_loc[s], w_loc[s], gate_ev[i])
+        else:
+            graphs[i].replay()
     t1.record()
     torch.cuda.synchronize()
     barrier(world)
-    launches = int(ops.lib().msb_kernel_launches()) - launches0
+    if args.eager:
+        launches = int(lib.msb_kernel_launches()) - launches0
     clk = clocks.stop()
     ms = t0.elapsed_time(t1)
     ms = max_over_ranks(ms, world)
@@ -378,8 +423,14 @@ def main():
     except OSError:
         pass
     hbm = float(peaks.get("hbm_gbs", 6650.0))
+    # Graphs holding NCCL calls must be gone before the process group is
+    # destroyed.
+    graphs.clear()
+    g_i = None
 
-    # End to end through the public API with host buffers.
+    # End to end with host buffers: every step copies its activations and
+    # routing from pinned host memory into the buffers a captured step reads,
+    # replays it, and reads every layer's output back to pinned host memory.
     e2e = None
     if not args.no_e2e:
         x_h = x_loc.cpu().pin_memory()
@@ -391,6 +442,12 @@ def main():
         w_d = torch.empty_like(w_loc[0])
         h2d = x_h[0].numel() * 2 + ids_h[0].numel() * 4 + w_h[0].numel() * 4
         d2h = y_h.numel() * 4
+        g_e2e = None
+        if args.eager:
+            run = lambda: step(x_d, ids_d, w_d)
+        else:
+            g_e2e, _ = capture(lambda: step(x_d, ids_d, w_d))
+            run = g_e2e.replay
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         barrier(world)
@@ -401,8 +458,7 @@ def main():
             x_d.copy_(x_h[s], non_blocking=True)
             ids_d.copy_(ids_h[s], non_blocking=True)
             w_d.copy_(w_h[s], non_blocking=True)
-            for layer in range(L):
-                run_layer(ctx, layer, x_d, ids_d[layer], w_d[layer], y[layer])
+            run()
             y_h.copy_(y, non_blocking=True)
             torch.cuda.current_stream().synchronize()  # the step's result is on the host
         e1.record()
@@ -411,6 +467,7 @@ def main():
         e_ms = max_over_ranks(e0.elapsed_time(e1), world)
         e2e = {"value": T * args.steps / (e_ms / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+        run = g_e2e = None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -437,7 +494,11 @@ def main():
                            "routing": "top-4 softmax over N(0,1) logits",
                            "activations": "bf16 N(0,1)",
                            "l2": "inputs larger than L2 (60.9 GB of expert weights)",
-                           "parallelism": f"ep{world}"},
+                           "parallelism": f"ep{world}",
+                           "exchange": (None if world == 1 else
+                                        "NVLink peer-memory kernels" if args.transport == "peers"
+                                        else "NCCL all-to-all"),
+                           "launch": "eager" if args.eager else "one CUDA graph per step"},
                 "roofline": {"bound": "hbm", "achieved": gate_gbs, "peak": hbm, "unit": "GB/s",
                              "frac": gate_gbs / hbm, "traffic": None,
                              "kernel": "tc_kernel<2> (fused gate/up mul_mat_id, tcgen05 mxf4)",
@@ -446,7 +507,12 @@ def main():
                 "setup_s": round(t_setup, 1)}
         print(json.dumps(line), flush=True)
     if world > 1:
+        import gc
+
         import torch.distributed as dist
+        gc.collect()
+        torch.cuda.synchronize()
+        ctx["ep"].close()
         barrier(world)
         dist.destroy_process_group()
     return 0

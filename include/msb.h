@@ -264,6 +264,50 @@ int msb_ep_combine(const float *back_dev, const int32_t *pos_dev,
                    const float *w_dev, int32_t top_k, int32_t n_tok, int64_t K,
                    float *y_dev, void *stream);
 
+/* ---- Exchange over NVLink peer memory (no counterpart in the reference) --
+ * Replaces the two all-to-alls above for ranks of one node whose GPUs reach
+ * each other's memory. Each rank creates one exchange buffer
+ * (msb_ep_buffer_bytes), shares its IPC handle with the other ranks (any
+ * host channel) and opens theirs; msb_ep_peers_t lists every rank's buffer
+ * as mapped on this rank (its own buffer for its own rank). Per layer:
+ *   msb_ep_dispatch_peers  rows to the experts' ranks, written directly into
+ *                          their buffers (block `rank`, msb_ep_dispatch's
+ *                          row order; K bf16 then the int32 local expert id,
+ *                          rows msb_ep_row_bytes(K) apart; unused rows -1)
+ *   msb_ep_wait(0)         until every rank's rows for this rank arrived
+ *   ... local FFN over the received rows (buffer offset 0) ...
+ *   msb_ep_return_peers    results back into the sources' buffers
+ *   msb_ep_wait(1)         until every result for this rank arrived; they
+ *                          are f32 rows at offset msb_ep_yback_offset, in the
+ *                          row order msb_ep_combine's pos refers to
+ * All ranks must make the same calls in the same order. A wait gives up
+ * after about a second and sets status bit 32 (phase 0) or 64 (phase 1)
+ * (msb_device_status). The sequence counters live in the buffers, so the
+ * calls may be captured in a CUDA graph and replayed. */
+#define MSB_EP_MAX_RANKS 8
+#define MSB_EP_HANDLE_BYTES 64
+
+typedef struct {
+  int32_t n_rank, rank, cap;       /* ranks, this rank, rows per block      */
+  int64_t K;                       /* activation width, multiple of 4       */
+  void *peer[MSB_EP_MAX_RANKS];    /* every rank's buffer as mapped here    */
+} msb_ep_peers_t;
+
+int64_t msb_ep_buffer_bytes(int32_t n_rank, int32_t cap, int64_t K);
+int64_t msb_ep_row_bytes(int64_t K);
+int64_t msb_ep_yback_offset(int32_t n_rank, int32_t cap, int64_t K);
+int msb_ep_buffer_create(int64_t bytes, void **buf, void *ipc_handle);
+int msb_ep_buffer_open(const void *ipc_handle, void **peer_buf);
+int msb_ep_buffer_close(void *peer_buf);
+int msb_ep_buffer_destroy(void *buf);
+int msb_ep_dispatch_peers(const msb_ep_peers_t *peers, const int32_t *ids_dev,
+                          const void *x_dev, int x_type, int64_t x_nb1,
+                          int32_t top_k, int32_t n_tok, int32_t n_local,
+                          int32_t *pos_dev, void *stream);
+int msb_ep_return_peers(const msb_ep_peers_t *peers, const float *y_loc_dev,
+                        void *stream);
+int msb_ep_wait(const msb_ep_peers_t *peers, int32_t phase, void *stream);
+
 /* ======================================================================== */
 /* Measurement hooks                                                          */
 /* ======================================================================== */

@@ -36,6 +36,15 @@ class PoolInfo(ctypes.Structure):
                 ("data", c_vp)]
 
 
+EP_MAX_RANKS = 8
+EP_HANDLE_BYTES = 64
+
+
+class EpPeers(ctypes.Structure):
+    _fields_ = [("n_rank", ctypes.c_int32), ("rank", ctypes.c_int32), ("cap", ctypes.c_int32),
+                ("K", ctypes.c_int64), ("peer", c_vp * EP_MAX_RANKS)]
+
+
 class Route(ctypes.Structure):
     _fields_ = [("slot_ids", c_vp), ("counts", c_vp), ("offsets", c_vp),
                 ("rows", c_vp), ("active", c_vp)]
@@ -96,6 +105,18 @@ SIGNATURES = {
                                        ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_int32, c_vp, ctypes.c_int64,
                                        c_vp, ctypes.c_int64, c_vp, c_vp]),
+    "msb_ep_buffer_bytes": (ctypes.c_int64, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64]),
+    "msb_ep_row_bytes": (ctypes.c_int64, [ctypes.c_int64]),
+    "msb_ep_yback_offset": (ctypes.c_int64, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64]),
+    "msb_ep_buffer_create": (ctypes.c_int, [ctypes.c_int64, ctypes.POINTER(c_vp), c_vp]),
+    "msb_ep_buffer_open": (ctypes.c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "msb_ep_buffer_close": (ctypes.c_int, [c_vp]),
+    "msb_ep_buffer_destroy": (ctypes.c_int, [c_vp]),
+    "msb_ep_dispatch_peers": (ctypes.c_int, [ctypes.POINTER(EpPeers), c_vp, c_vp, ctypes.c_int,
+                                             ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                             ctypes.c_int32, c_vp, c_vp]),
+    "msb_ep_return_peers": (ctypes.c_int, [ctypes.POINTER(EpPeers), c_vp, c_vp]),
+    "msb_ep_wait": (ctypes.c_int, [ctypes.POINTER(EpPeers), ctypes.c_int32, c_vp]),
     "msb_ep_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.c_int64, c_vp, c_vp]),
     "msb_kernel_launches": (ctypes.c_uint64, []),

@@ -361,6 +361,15 @@ static int quantize_act(const void *b, int b_type, int64_t b_ne1, int64_t b_nb1,
 // One-shot timing request for the next fused gate/up launch on this thread.
 static thread_local cudaEvent_t g_gate_up_start = nullptr, g_gate_up_stop = nullptr;
 
+// Under stream capture the event becomes an external event node of the
+// graph, so it is recorded (and timeable) at every replay.
+static cudaError_t record_timing_event(cudaEvent_t ev, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaError_t e = cudaStreamIsCapturing(st, &cs)) return e;
+  return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal)
+                                             : cudaEventRecord(ev, st);
+}
+
 template <int WT, bool SWIGLU>
 static int launch_gemv_t(const GemvArgs &a, int max_active, cudaStream_t st) {
   const int NV = SWIGLU ? 2 : 1;
@@ -370,10 +379,10 @@ static int launch_gemv_t(const GemvArgs &a, int max_active, cudaStream_t st) {
   const int64_t grid = int64_t(max_active) * a.tiles;
   if (grid == 0) return MSB_OK;
   const bool timed = SWIGLU && g_gate_up_start && g_gate_up_stop;
-  if (timed) MSB_CUDA_TRY(cudaEventRecord(g_gate_up_start, st));
+  if (timed) MSB_CUDA_TRY(record_timing_event(g_gate_up_start, st));
   gemv_kernel<WT, SWIGLU><<<unsigned(grid), kThreads, smem, st>>>(a); count_launch();
   if (timed) {
-    MSB_CUDA_TRY(cudaEventRecord(g_gate_up_stop, st));
+    MSB_CUDA_TRY(record_timing_event(g_gate_up_stop, st));
     g_gate_up_start = g_gate_up_stop = nullptr;
   }
   MSB_CUDA_TRY(cudaGetLastError());
@@ -528,12 +537,12 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
     const int64_t rows_gu[2] = {0, up_row0};
     const msb_pool_s *gu_pools[2] = {gate, up};
     const bool timed = g_gate_up_start && g_gate_up_stop;
-    if (timed) MSB_CUDA_TRY(cudaEventRecord(g_gate_up_start, st));
+    if (timed) MSB_CUDA_TRY(record_timing_event(g_gate_up_start, st));
     if (int rc = tc_projection(gu_pools, 2, rows_gu, n_ff, route, pairs, xa, nullptr, ha, act_dev,
                                max_active_tc, st))
       return rc;
     if (timed) {
-      MSB_CUDA_TRY(cudaEventRecord(g_gate_up_stop, st));
+      MSB_CUDA_TRY(record_timing_event(g_gate_up_stop, st));
       g_gate_up_start = g_gate_up_stop = nullptr;
     }
     const int64_t rows_dn[2] = {0, 0};

@@ -42,6 +42,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "msb_internal.h"
 #include "pool.cuh"
 #include "quant.cuh"
@@ -547,6 +549,26 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   return nv == 2 ? launch_tc_t<2>(a, max_active, st) : launch_tc_t<1>(a, max_active, st);
 }
 
+}  // namespace msb
+
+namespace msb {
+// Device address of the status word on the current device, for kernels of
+// other translation units (looked up once per device).
+int status_word(int **out) {
+  static std::mutex mu;
+  static int *addr[64] = {};
+  int dev = 0;
+  MSB_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(MSB_ERR_INVALID, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void *p = nullptr;
+    MSB_CUDA_TRY(cudaGetSymbolAddress(&p, tc::g_status));
+    addr[dev] = static_cast<int *>(p);
+  }
+  *out = addr[dev];
+  return MSB_OK;
+}
 }  // namespace msb
 
 extern "C" int msb_device_status(int32_t *status, int32_t clear) {

@@ -16,6 +16,10 @@ void clear_error();
 // Counts a kernel launch (reported by msb_kernel_launches).
 void count_launch(int n = 1);
 
+// Device address of the library's status word on the current device (bits
+// set by kernels whose bounded waits gave up; msb_device_status reads it).
+int status_word(int **out);
+
 // ggml block geometry of the two weight types.
 struct BlockFormat {
   int block_bytes;  // bytes per 32-element block in ggml layout

@@ -185,6 +185,29 @@ def ep_dispatch(ids, x, n_local, n_rank, cap, send_x, send_e, pos, stream=None):
                                 _ptr(send_e), send_e.stride(0) * 4, _ptr(pos), _stream(stream)))
 
 
+def ep_dispatch_peers(peers, ids, x, n_local, pos, stream=None):
+    """Stores this rank's (token, k) rows into the owning ranks' exchange
+    buffers (peers: an EpPeers)."""
+    n_tok, top_k = ids.shape
+    assert ids.is_contiguous() and x.stride(1) == 1
+    check(lib().msb_ep_dispatch_peers(ctypes.byref(peers), _ptr(ids), _ptr(x), _ACT_TYPES[x.dtype],
+                                      x.stride(0) * x.element_size(), top_k, n_tok, n_local,
+                                      _ptr(pos), _stream(stream)))
+
+
+def ep_return_peers(peers, y_loc, stream=None):
+    """Stores the local results of received rows back into their source
+    ranks' exchange buffers."""
+    assert y_loc.dtype == torch.float32 and y_loc.is_contiguous()
+    check(lib().msb_ep_return_peers(ctypes.byref(peers), _ptr(y_loc), _stream(stream)))
+
+
+def ep_wait(peers, phase, stream=None):
+    """Waits (on the device, bounded) for every rank's rows (phase 0) or
+    results (phase 1) to arrive in this rank's exchange buffer."""
+    check(lib().msb_ep_wait(ctypes.byref(peers), phase, _stream(stream)))
+
+
 def ep_combine(back, pos, w, y, stream=None):
     """y[t] = sum_k w[t, k] * back[pos[t, k]]."""
     n_tok, top_k = w.shape

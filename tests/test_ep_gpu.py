@@ -2,10 +2,13 @@
 
 - msb_ep_dispatch / msb_ep_combine against the oracle's restatement
   (bit-exact: a row copy, and f32 fused multiply-adds in k order), on one GPU.
-- The whole expert-parallel MoE layer (moestream_b200.ep over NCCL, two
-  ranks, tensor-core FFN on each) against the oracle's single-process layer;
-  needs two GPUs and is skipped with fewer.
+- The whole expert-parallel MoE layer (moestream_b200.ep, two ranks,
+  tensor-core FFN on each) against the oracle's single-process layer, with
+  the rows exchanged by NCCL all-to-all and by the NVLink peer-memory
+  kernels (run twice in a row, and from a replayed CUDA graph); needs two
+  GPUs and is skipped with fewer.
 """
+import datetime
 import os
 import socket
 
@@ -70,7 +73,7 @@ def _layer_inputs():
     return gate, up, down, x, ids, w
 
 
-def _rank_main(rank, world, port, out_q):
+def _rank_main(rank, world, port, transport, out_q):
     import torch.distributed as dist
 
     from moestream_b200 import ops
@@ -79,10 +82,11 @@ def _rank_main(rank, world, port, out_q):
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
-                            device_id=torch.device("cuda", rank))
+                            device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
     try:
         gate, up, down, x, ids, w = _layer_inputs()
-        ep = ExpertParallel(world, rank, N_EXPERT, N_TOK, TOP_K, K, "cuda")
+        ep = ExpertParallel(world, rank, N_EXPERT, N_TOK, TOP_K, K, "cuda", transport=transport)
         mine = range(rank * ep.n_local, (rank + 1) * ep.n_local)
         pools = {}
         for role, mats, kk, nn in (("gate", gate, K, N_FF), ("up", up, K, N_FF),
@@ -97,31 +101,54 @@ def _rank_main(rank, world, port, out_q):
             ops.moe_ffn(pools["gate"], pools["up"], pools["down"], rows, r, ones, 1, out=out)
 
         lo = rank * ep.t_loc
-        y = torch.empty(ep.t_loc, K, device="cuda")
-        ep.layer(x[lo:lo + ep.t_loc].cuda(), torch.from_numpy(ids[lo:lo + ep.t_loc]).cuda(),
-                 torch.from_numpy(w[lo:lo + ep.t_loc]).cuda(), local_ffn, y)
+        xs = x[lo:lo + ep.t_loc].cuda()
+        ids_d = torch.from_numpy(ids[lo:lo + ep.t_loc]).cuda()
+        w_d = torch.from_numpy(w[lo:lo + ep.t_loc]).cuda()
+        ys = [torch.empty(ep.t_loc, K, device="cuda") for _ in range(3)]
+        ep.layer(xs, ids_d, w_d, local_ffn, ys[0])
+        ep.layer(xs, ids_d, w_d, local_ffn, ys[1])
+        graph = None
+        if transport == "peers":
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                ep.layer(xs, ids_d, w_d, local_ffn, ys[2])
+            graph.replay()
+            graph.replay()
+        else:
+            ep.layer(xs, ids_d, w_d, local_ffn, ys[2])
         torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
+        y = ys[0]
         slab = {r: np.concatenate([m, np.zeros((1, m.shape[1]), np.uint8)])
                 for r, m in (("gate", gate), ("up", up), ("down", down))}
         want, _ = O.moe_ffn("mxfp4", slab["gate"], slab["up"], slab["down"], K, N_FF,
                             x.float().numpy(), ids, w, mode="e2m1x4")
         err = O.max_abs_normalized(y.cpu().numpy(), want[lo:lo + ep.t_loc])
         out_q.put((rank, float(err)))
+        graph = None
+        ep.close()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_rank_layer_matches_oracle():
+@pytest.mark.parametrize("transport", ["collective", "peers"])
+def test_two_rank_layer_matches_oracle(transport):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, transport, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.terminate()
+            p.join(timeout=30)
     codes = [p.exitcode for p in procs]
     assert codes == [0] * world, codes
     errs = dict(q.get(timeout=5) for _ in range(world))
