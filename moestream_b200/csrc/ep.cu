@@ -24,6 +24,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
     const int32_t *ids, const char *x, int64_t x_nb1, int32_t top_k, int32_t n_pairs,
     int64_t K, int32_t n_local, int32_t n_rank, int32_t cap, char *send_x, int64_t send_nb1,
     char *send_e, int64_t send_e_nb, int32_t *pos) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int warp_cnt[kEpThreads / 32];
   const int p = blockIdx.x;
   const int e = ids[p];
@@ -62,6 +64,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
 // y[t, n] = sum_k w[t, k] * back[pos[t, k], n], k ascending; pos -1 adds 0.
 __global__ void ep_combine_kernel(const float *back, const int32_t *pos, const float *w,
                                   int32_t top_k, int64_t K, int64_t n_tok, float *y) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n_tok * K) return;
   const int64_t t = i / K, n = i - t * K;
@@ -97,13 +101,13 @@ extern "C" int msb_ep_dispatch(const int32_t *ids_dev, const void *x_dev, int x_
   auto *sx = static_cast<char *>(send_x_dev);
   auto *se = reinterpret_cast<char *>(send_e_dev);
   if (x_type == MSB_TYPE_BF16)
-    msb::ep_dispatch_kernel<__nv_bfloat16><<<n_pairs, msb::kEpThreads, 0, st>>>(
-        ids_dev, x, x_nb1, top_k, n_pairs, K, n_local, n_rank, cap, sx, send_nb1, se, send_e_nb,
-        pos_dev);
+    MSB_CUDA_TRY(msb::launch_pdl(msb::ep_dispatch_kernel<__nv_bfloat16>, dim3(n_pairs),
+                                 dim3(msb::kEpThreads), 0, st, ids_dev, x, x_nb1, top_k, n_pairs,
+                                 K, n_local, n_rank, cap, sx, send_nb1, se, send_e_nb, pos_dev));
   else if (x_type == MSB_TYPE_F32)
-    msb::ep_dispatch_kernel<float><<<n_pairs, msb::kEpThreads, 0, st>>>(
-        ids_dev, x, x_nb1, top_k, n_pairs, K, n_local, n_rank, cap, sx, send_nb1, se, send_e_nb,
-        pos_dev);
+    MSB_CUDA_TRY(msb::launch_pdl(msb::ep_dispatch_kernel<float>, dim3(n_pairs),
+                                 dim3(msb::kEpThreads), 0, st, ids_dev, x, x_nb1, top_k, n_pairs,
+                                 K, n_local, n_rank, cap, sx, send_nb1, se, send_e_nb, pos_dev));
   else
     return msb::fail(MSB_ERR_INVALID, "msb_ep_dispatch: activation type %d", x_type);
   msb::count_launch();
@@ -119,8 +123,9 @@ extern "C" int msb_ep_combine(const float *back_dev, const int32_t *pos_dev, con
                 "msb_ep_combine: null argument");
   const int64_t total = int64_t(n_tok) * K;
   if (total == 0) return MSB_OK;
-  msb::ep_combine_kernel<<<unsigned((total + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      back_dev, pos_dev, w_dev, top_k, K, n_tok, y_dev);
+  MSB_CUDA_TRY(msb::launch_pdl(msb::ep_combine_kernel, dim3(unsigned((total + 255) / 256)),
+                               dim3(256), 0, static_cast<cudaStream_t>(stream), back_dev, pos_dev,
+                               w_dev, top_k, K, int64_t(n_tok), y_dev));
   msb::count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;

@@ -83,6 +83,8 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(const __grid_constan
                                                             const char *x, int64_t x_nb1,
                                                             int32_t top_k, int32_t n_pairs,
                                                             int32_t n_local, int32_t *pos) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int warp_cnt[kThreads / 32];
   const int n_exp = n_local * L.n_rank;
   const bool fill = int(blockIdx.x) >= n_pairs;
@@ -140,6 +142,8 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(const __grid_constan
 // Row r of y_loc (block s = rows received from rank s) goes back to rank s,
 // block `rank`; rows whose expert id is -1 were never asked for.
 __global__ void __launch_bounds__(kThreads) return_kernel(const __grid_constant__ Layout L, const float *y_loc) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const int s = r / L.cap, i = r % L.cap;
   const char *recv_row = L.peer[L.rank] + int64_t(r) * L.row_bytes;
@@ -154,6 +158,8 @@ __global__ void __launch_bounds__(kThreads) return_kernel(const __grid_constant_
 
 // Waits until every rank published phase `ph`'s next sequence number here.
 __global__ void wait_kernel(const __grid_constant__ Layout L, int ph, int *status) {
+  pdl_wait();
+  pdl_trigger();
   uint32_t *own = ctrl_of(L, L.rank);
   const uint32_t seq = own[kWaited + ph] + 1;
   bool ok = true;
@@ -256,11 +262,11 @@ extern "C" int msb_ep_dispatch_peers(const msb_ep_peers_t *peers, const int32_t 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const char *x = static_cast<const char *>(x_dev);
   if (x_type == MSB_TYPE_BF16)
-    ep::dispatch_kernel<__nv_bfloat16><<<grid, ep::kThreads, 0, st>>>(L, ids_dev, x, x_nb1, top_k,
-                                                                     n_pairs, n_local, pos_dev);
+    MSB_CUDA_TRY(launch_pdl(ep::dispatch_kernel<__nv_bfloat16>, dim3(grid), dim3(ep::kThreads), 0, st,
+                            L, ids_dev, x, x_nb1, top_k, n_pairs, n_local, pos_dev));
   else if (x_type == MSB_TYPE_F32)
-    ep::dispatch_kernel<float><<<grid, ep::kThreads, 0, st>>>(L, ids_dev, x, x_nb1, top_k,
-                                                             n_pairs, n_local, pos_dev);
+    MSB_CUDA_TRY(launch_pdl(ep::dispatch_kernel<float>, dim3(grid), dim3(ep::kThreads), 0, st, L,
+                            ids_dev, x, x_nb1, top_k, n_pairs, n_local, pos_dev));
   else
     return fail(MSB_ERR_INVALID, "msb_ep_dispatch_peers: activation type %d", x_type);
   count_launch();
@@ -274,8 +280,8 @@ extern "C" int msb_ep_return_peers(const msb_ep_peers_t *peers, const float *y_l
   if (int rc = make_layout(peers, &L)) return rc;
   MSB_CHECK_ARG(y_loc_dev && (reinterpret_cast<uintptr_t>(y_loc_dev) & 15) == 0,
                 "msb_ep_return_peers: y_loc must be 16-byte aligned");
-  ep::return_kernel<<<unsigned(L.n_rank * L.cap), ep::kThreads, 0,
-                      static_cast<cudaStream_t>(stream)>>>(L, y_loc_dev);
+  MSB_CUDA_TRY(launch_pdl(ep::return_kernel, dim3(unsigned(L.n_rank * L.cap)), dim3(ep::kThreads),
+                          0, static_cast<cudaStream_t>(stream), L, y_loc_dev));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;
@@ -287,7 +293,8 @@ extern "C" int msb_ep_wait(const msb_ep_peers_t *peers, int32_t phase, void *str
   MSB_CHECK_ARG(phase == 0 || phase == 1, "msb_ep_wait: phase must be 0 or 1");
   int *status = nullptr;
   if (int rc = status_word(&status)) return rc;
-  ep::wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(L, phase, status);
+  MSB_CUDA_TRY(launch_pdl(ep::wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
+                          L, int(phase), status));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;

@@ -82,6 +82,8 @@ __device__ __forceinline__ void store_q8_block(ActQ8 out, int64_t row, int64_t b
 template <typename T>
 __global__ void __launch_bounds__(kThreads) quantize_act_kernel(
     const char *b, int64_t nb1, int64_t nb2, int64_t ne1, int64_t n_rows, ActQ8 out) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t item = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5);
   if (item >= n_rows * out.nb) return;
@@ -224,6 +226,8 @@ __device__ __forceinline__ void k_loop(const GemvArgs &a, int slot, int64_t n, b
 template <int WT, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
   constexpr int NV = SWIGLU ? 2 : 1;  // weight views per lane
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem[];
   const int nb = int(a.w.nb);
   int8_t *s_q = reinterpret_cast<int8_t *>(smem);                           // [kMaxPairs][nb][32]
@@ -317,6 +321,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
 // y[t, n] = sum_k w[k, t] * r[n, k, t], k in increasing order.
 __global__ void combine_kernel(const float *r, const float *w, int32_t top_k, int64_t N,
                                int64_t n_tok, float *y) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= N * n_tok) return;
   const int64_t t = i / N, n = i - t * N;
@@ -348,9 +354,11 @@ static int quantize_act(const void *b, int b_type, int64_t b_ne1, int64_t b_nb1,
   const int64_t grid = (items + kWarps - 1) / kWarps;
   const char *p = static_cast<const char *>(b);
   if (b_type == MSB_TYPE_F32)
-    quantize_act_kernel<float><<<unsigned(grid), kThreads, 0, st>>>(p, b_nb1, b_nb2, b_ne1, n_rows, out);
+    MSB_CUDA_TRY(launch_pdl(quantize_act_kernel<float>, dim3(unsigned(grid)), dim3(kThreads), 0, st,
+                            p, b_nb1, b_nb2, b_ne1, n_rows, out));
   else if (b_type == MSB_TYPE_BF16)
-    quantize_act_kernel<__nv_bfloat16><<<unsigned(grid), kThreads, 0, st>>>(p, b_nb1, b_nb2, b_ne1, n_rows, out);
+    MSB_CUDA_TRY(launch_pdl(quantize_act_kernel<__nv_bfloat16>, dim3(unsigned(grid)), dim3(kThreads),
+                            0, st, p, b_nb1, b_nb2, b_ne1, n_rows, out));
   else
     return fail(MSB_ERR_INVALID, "activation type %d is not F32 or BF16", b_type);
   count_launch();
@@ -380,7 +388,8 @@ static int launch_gemv_t(const GemvArgs &a, int max_active, cudaStream_t st) {
   if (grid == 0) return MSB_OK;
   const bool timed = SWIGLU && g_gate_up_start && g_gate_up_stop;
   if (timed) MSB_CUDA_TRY(record_timing_event(g_gate_up_start, st));
-  gemv_kernel<WT, SWIGLU><<<unsigned(grid), kThreads, smem, st>>>(a); count_launch();
+  MSB_CUDA_TRY(launch_pdl(gemv_kernel<WT, SWIGLU>, dim3(unsigned(grid)), dim3(kThreads), smem, st, a));
+  count_launch();
   if (timed) {
     MSB_CUDA_TRY(record_timing_event(g_gate_up_stop, st));
     g_gate_up_start = g_gate_up_stop = nullptr;
@@ -551,8 +560,8 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
                                max_active_tc, st))
       return rc;
     const int64_t total = down->N * n_tok;
-    combine_kernel<<<unsigned((total + 255) / 256), 256, 0, st>>>(rd, w_dev, top_k, down->N, n_tok,
-                                                                  y_dev);
+    MSB_CUDA_TRY(launch_pdl(combine_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, st,
+                            rd, w_dev, top_k, down->N, int64_t(n_tok), y_dev));
     count_launch();
     MSB_CUDA_TRY(cudaGetLastError());
     return MSB_OK;
@@ -594,7 +603,9 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
   if (int rc = launch_gemv(down->wtype, false, d, max_active, st)) return rc;
 
   const int64_t total = down->N * n_tok;
-  combine_kernel<<<unsigned((total + 255) / 256), 256, 0, st>>>(rdown, w_dev, top_k, down->N, n_tok, y_dev); count_launch();
+  MSB_CUDA_TRY(launch_pdl(combine_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, st,
+                          rdown, w_dev, top_k, down->N, int64_t(n_tok), y_dev));
+  count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;
 }

@@ -195,6 +195,8 @@ __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t n
                                                         int32_t ne1, int32_t top_k,
                                                         const int32_t *rows, int64_t n_pairs,
                                                         int64_t nb, uint8_t *q, uint8_t *sf) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31, grp = lane >> 3, l = lane & 7;
   const int64_t nc = (nb + 3) / 4;
   const int64_t item = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
@@ -222,7 +224,6 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_chunks = (a.nb + kChunk - 1) / kChunk;
-  const int64_t n_items = int64_t(a.active[0]) * a.tiles;
 
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
   uint64_t *empty = full + kStages;
@@ -253,6 +254,11 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   volatile int *abort_v = abort_flag;
+  // The prologue above overlaps the previous kernel; the route and the
+  // activation terms are read only after it completed.
+  pdl_wait();
+  pdl_trigger();
+  const int64_t n_items = int64_t(a.active[0]) * a.tiles;
 
   if (warp == 0) {
     // ---- producer ----
@@ -464,11 +470,11 @@ int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb
   const int64_t grid = (n_pairs * ((nb + 3) / 4) + 7) / 8;
   const char *p = static_cast<const char *>(b);
   if (b_type == MSB_TYPE_F32)
-    tc::act_terms_kernel<float><<<unsigned(grid), 256, 0, st>>>(p, nb1, nb2, int32_t(ne1), top_k,
-                                                                rows, n_pairs, nb, q, sf);
+    MSB_CUDA_TRY(launch_pdl(tc::act_terms_kernel<float>, dim3(unsigned(grid)), dim3(256), 0, st, p,
+                            nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, sf));
   else if (b_type == MSB_TYPE_BF16)
-    tc::act_terms_kernel<__nv_bfloat16><<<unsigned(grid), 256, 0, st>>>(
-        p, nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, sf);
+    MSB_CUDA_TRY(launch_pdl(tc::act_terms_kernel<__nv_bfloat16>, dim3(unsigned(grid)), dim3(256), 0,
+                            st, p, nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, sf));
   else
     return fail(MSB_ERR_INVALID, "activation type %d is not F32 or BF16", b_type);
   count_launch();
@@ -492,7 +498,8 @@ static int launch_tc_t(const tc::Args &a, int max_active, cudaStream_t st) {
   int64_t grid = int64_t(max_active) * a.tiles;
   if (grid > 2 * n_sm) grid = 2 * n_sm;
   if (grid == 0) return MSB_OK;
-  tc::tc_kernel<NV><<<unsigned(grid), tc::kThreads, C::kSmem, st>>>(a);
+  MSB_CUDA_TRY(launch_pdl(tc::tc_kernel<NV>, dim3(unsigned(grid)), dim3(tc::kThreads), C::kSmem, st,
+                          a));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;

@@ -3,6 +3,11 @@
 
 #include <cstdarg>
 #include <cstdint>
+#include <utility>
+
+#ifdef __CUDACC__
+#include <cuda_runtime.h>
+#endif
 
 #include "../../include/msb.h"
 
@@ -30,6 +35,35 @@ inline bool block_format(int wtype, BlockFormat *f) {
   if (wtype == MSB_TYPE_MXFP4)  { *f = {17, 1}; return true; }
   return false;
 }
+
+#ifdef __CUDACC__
+// Programmatic dependent launch. Hot-path kernels are launched with
+// launch_pdl, which lets a kernel start (and run its prologue) while the
+// previous kernel in the stream finishes; every such kernel calls pdl_wait()
+// before it reads or writes memory that earlier work uses (the wait returns
+// once the previous grid has completed and its writes are visible; without
+// the launch attribute it returns at once), and pdl_trigger() once its own
+// CTAs are all running, so the next kernel can be scheduled early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+#endif
 
 }  // namespace msb
 

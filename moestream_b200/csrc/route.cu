@@ -68,6 +68,8 @@ __device__ int block_exclusive_scan(int *v, int n, int *warp_sums) {
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sm[];
   const int S = a.n_slot + 1;
   int *cnt = sm;             // [S]
@@ -156,7 +158,8 @@ extern "C" int msb_remap_group(const int32_t *ids_dev, int64_t nb0, int64_t nb1,
                    route->offsets, route->rows, route->active};
   if (smem > 48 * 1024)
     MSB_CUDA_TRY(cudaFuncSetAttribute(msb::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  msb::route_kernel<<<1, msb::kRouteThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  MSB_CUDA_TRY(msb::launch_pdl(msb::route_kernel, dim3(1), dim3(msb::kRouteThreads), smem,
+                               static_cast<cudaStream_t>(stream), a));
   msb::count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;
