@@ -208,9 +208,8 @@ def run_layer(ctx, layer, x, ids, w, y, timed_events=None):
         return
     ep = ctx["ep"]
 
-    def local_ffn(rows, local_ids, ones, out):
-        r = ops.remap_group(local_ids, ga.n_slot, route=ctx["route"])
-        ops.moe_ffn(ga, up, dn, rows, r, ones, 1, ws=ctx["ws"], out=out)
+    def local_ffn(rows, local_ids, route, out):
+        ops.moe_ffn(ga, up, dn, rows, route, None, 1, ws=ctx["ws"], out=out)
 
     ep.layer(x, ids, w, local_ffn, y)
 

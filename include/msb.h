@@ -223,7 +223,9 @@ int msb_device_status(int32_t *status, int32_t clear);
  * gate and up may be the same pool with up_row0 = N_ff (a fused gate_up
  * tensor whose first N_ff rows are the gate); otherwise up_row0 = 0.
  * x: f32 or bf16 [K, 1, n_tok] (byte stride x_nb1 between tokens);
- * w: f32 [top_k, n_tok] router weights (contiguous); y: f32 [K, n_tok].
+ * w: f32 [top_k, n_tok] router weights (contiguous), or NULL when top_k is
+ * 1, in which case y = r (the expert outputs, no weighting);
+ * y: f32 [K, n_tok].
  * act_dev (optional, may be NULL): f32 [N_ff, top_k, n_tok] receives a.
  * Composition restated from research/spikes/s1_real_expert_stream/main.c:
  * 186-209 and research/spikes/s4_sweep_math/main.c:89-92. */
@@ -274,16 +276,19 @@ int msb_ep_combine(const float *back_dev, const int32_t *pos_dev,
  *                          their buffers (block `rank`, msb_ep_dispatch's
  *                          row order; K bf16 then the int32 local expert id,
  *                          rows msb_ep_row_bytes(K) apart; unused rows -1)
- *   msb_ep_wait(0)         until every rank's rows for this rank arrived
+ *   msb_ep_remap_group     waits until every rank's rows for this rank
+ *                          arrived, then msb_remap_group of the received
+ *                          ids (top_k 1, no table; -1 -> zero slot)
  *   ... local FFN over the received rows (buffer offset 0) ...
  *   msb_ep_return_peers    results back into the sources' buffers
- *   msb_ep_wait(1)         until every result for this rank arrived; they
- *                          are f32 rows at offset msb_ep_yback_offset, in the
- *                          row order msb_ep_combine's pos refers to
- * All ranks must make the same calls in the same order. A wait gives up
- * after about a second and sets status bit 32 (phase 0) or 64 (phase 1)
- * (msb_device_status). The sequence counters live in the buffers, so the
- * calls may be captured in a CUDA graph and replayed. */
+ *   msb_ep_combine_peers   waits until every result for this rank arrived
+ *                          (f32 rows at offset msb_ep_yback_offset), then
+ *                          msb_ep_combine
+ * msb_ep_wait(phase) is the wait alone (0: rows, 1: results). All ranks
+ * must make the same calls in the same order. A wait gives up after about a
+ * second and sets status bit 32 (rows) or 64 (results) (msb_device_status).
+ * The sequence counters live in the buffers, so the calls may be captured
+ * in a CUDA graph and replayed. */
 #define MSB_EP_MAX_RANKS 8
 #define MSB_EP_HANDLE_BYTES 64
 
@@ -307,6 +312,11 @@ int msb_ep_dispatch_peers(const msb_ep_peers_t *peers, const int32_t *ids_dev,
 int msb_ep_return_peers(const msb_ep_peers_t *peers, const float *y_loc_dev,
                         void *stream);
 int msb_ep_wait(const msb_ep_peers_t *peers, int32_t phase, void *stream);
+int msb_ep_remap_group(const msb_ep_peers_t *peers, int32_t n_slot,
+                       const msb_route_t *route, void *stream);
+int msb_ep_combine_peers(const msb_ep_peers_t *peers, const int32_t *pos_dev,
+                         const float *w_dev, int32_t top_k, int32_t n_tok,
+                         float *y_dev, void *stream);
 
 /* ======================================================================== */
 /* Measurement hooks                                                          */

@@ -117,6 +117,10 @@ SIGNATURES = {
                                              ctypes.c_int32, c_vp, c_vp]),
     "msb_ep_return_peers": (ctypes.c_int, [ctypes.POINTER(EpPeers), c_vp, c_vp]),
     "msb_ep_wait": (ctypes.c_int, [ctypes.POINTER(EpPeers), ctypes.c_int32, c_vp]),
+    "msb_ep_remap_group": (ctypes.c_int, [ctypes.POINTER(EpPeers), ctypes.c_int32,
+                                          ctypes.POINTER(Route), c_vp]),
+    "msb_ep_combine_peers": (ctypes.c_int, [ctypes.POINTER(EpPeers), c_vp, c_vp, ctypes.c_int32,
+                                            ctypes.c_int32, c_vp, c_vp]),
     "msb_ep_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.c_int64, c_vp, c_vp]),
     "msb_kernel_launches": (ctypes.c_uint64, []),

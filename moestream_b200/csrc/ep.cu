@@ -63,9 +63,11 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(
 
 // y[t, n] = sum_k w[t, k] * back[pos[t, k], n], k ascending; pos -1 adds 0.
 __global__ void ep_combine_kernel(const float *back, const int32_t *pos, const float *w,
-                                  int32_t top_k, int64_t K, int64_t n_tok, float *y) {
+                                  int32_t top_k, int64_t K, int64_t n_tok, float *y,
+                                  FlagWait wait) {
   pdl_wait();
   pdl_trigger();
+  flag_wait_block(wait);
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n_tok * K) return;
   const int64_t t = i / K, n = i - t * K;
@@ -118,6 +120,13 @@ extern "C" int msb_ep_dispatch(const int32_t *ids_dev, const void *x_dev, int x_
 extern "C" int msb_ep_combine(const float *back_dev, const int32_t *pos_dev, const float *w_dev,
                               int32_t top_k, int32_t n_tok, int64_t K, float *y_dev,
                               void *stream) {
+  return msb::ep_combine_wait(back_dev, pos_dev, w_dev, top_k, n_tok, K, y_dev, msb::FlagWait{},
+                              stream);
+}
+
+int msb::ep_combine_wait(const float *back_dev, const int32_t *pos_dev, const float *w_dev,
+                         int32_t top_k, int32_t n_tok, int64_t K, float *y_dev,
+                         const FlagWait &wait, void *stream) {
   MSB_CHECK_ARG(top_k > 0 && n_tok >= 0 && K > 0, "msb_ep_combine: bad shape");
   MSB_CHECK_ARG(n_tok == 0 || (back_dev && pos_dev && w_dev && y_dev),
                 "msb_ep_combine: null argument");
@@ -125,7 +134,7 @@ extern "C" int msb_ep_combine(const float *back_dev, const int32_t *pos_dev, con
   if (total == 0) return MSB_OK;
   MSB_CUDA_TRY(msb::launch_pdl(msb::ep_combine_kernel, dim3(unsigned((total + 255) / 256)),
                                dim3(256), 0, static_cast<cudaStream_t>(stream), back_dev, pos_dev,
-                               w_dev, top_k, K, int64_t(n_tok), y_dev));
+                               w_dev, top_k, K, int64_t(n_tok), y_dev, wait));
   msb::count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;

@@ -10,14 +10,15 @@
 //                                               the int32 local expert id
 //   [y_back: n_rank*cap rows of K f32]          block d = results from rank d
 //   [control: 32 u32]                           flags[2][8] (written by the
-//                                               peers), sent[2], waited[2],
-//                                               done[2] (this rank's own)
+//                                               peers), sent[2], done[2]
+//                                               (this rank's own)
 //
 // A sending kernel stores its rows into the destinations' buffers, and its
 // last CTA to finish (a done counter) raises this rank's flag in every
 // destination to the next sequence number. A waiting kernel spins, bounded
-// (about a second), until every peer's flag reached its own next sequence
-// number. The counters live in device memory, so a captured CUDA graph
+// (about a second), until every peer's flag reached the number of layers
+// this rank has dispatched (its own sent[0]: every rank runs the same
+// layers, so a rank waiting for layer L's rows or results expects L). The counters live in device memory, so a captured CUDA graph
 // replays the protocol correctly. Ordering: each CTA's stores are followed by
 // a system-scope fence before it counts itself done; the last CTA fences
 // again and publishes the flags with release stores; waiters load them with
@@ -33,7 +34,7 @@ namespace msb {
 namespace ep {
 
 constexpr int kThreads = 256;
-constexpr int kFlags = 0, kSent = 16, kWaited = 18, kDone = 20;   // control u32 offsets
+constexpr int kFlags = 0, kSent = 16, kDone = 20;   // control u32 offsets
 
 struct Layout {
   char *peer[MSB_EP_MAX_RANKS];
@@ -156,23 +157,22 @@ __global__ void __launch_bounds__(kThreads) return_kernel(const __grid_constant_
   publish(L, 1);
 }
 
-// Waits until every rank published phase `ph`'s next sequence number here.
-__global__ void wait_kernel(const __grid_constant__ Layout L, int ph, int *status) {
+// Waits until every rank published phase `ph` of the current layer here.
+__global__ void wait_kernel(FlagWait w) {
   pdl_wait();
   pdl_trigger();
-  uint32_t *own = ctrl_of(L, L.rank);
-  const uint32_t seq = own[kWaited + ph] + 1;
-  bool ok = true;
-  if (int(threadIdx.x) < L.n_rank) {
-    const uint32_t *flag = own + kFlags + ph * 8 + threadIdx.x;
-    const long long t0 = clock64();
-    while (int32_t(load_acquire_sys(flag) - seq) < 0) {
-      if (clock64() - t0 > (1ll << 31)) { ok = false; break; }
-    }
-  }
-  if (!ok) atomicOr(status, 32 << ph);
-  __syncthreads();
-  if (threadIdx.x == 0) own[kWaited + ph] = seq;
+  flag_wait_block(w);
+}
+
+inline FlagWait phase_wait(const Layout &L, int ph, int *status) {
+  FlagWait w;
+  const uint32_t *own = reinterpret_cast<const uint32_t *>(L.peer[L.rank] + L.ctrl_off);
+  w.flags = own + kFlags + ph * 8;
+  w.seq = own + kSent;
+  w.n = L.n_rank;
+  w.status = status;
+  w.bit = 32 << ph;
+  return w;
 }
 
 }  // namespace ep
@@ -253,7 +253,7 @@ extern "C" int msb_ep_dispatch_peers(const msb_ep_peers_t *peers, const int32_t 
                                      const void *x_dev, int x_type, int64_t x_nb1, int32_t top_k,
                                      int32_t n_tok, int32_t n_local, int32_t *pos_dev,
                                      void *stream) {
-  ep::Layout L;
+  ep::Layout L{};
   if (int rc = make_layout(peers, &L)) return rc;
   MSB_CHECK_ARG(top_k > 0 && n_tok >= 0 && n_local > 0, "msb_ep_dispatch_peers: bad shape");
   MSB_CHECK_ARG(n_tok == 0 || (ids_dev && x_dev && pos_dev), "msb_ep_dispatch_peers: null");
@@ -276,7 +276,7 @@ extern "C" int msb_ep_dispatch_peers(const msb_ep_peers_t *peers, const int32_t 
 
 extern "C" int msb_ep_return_peers(const msb_ep_peers_t *peers, const float *y_loc_dev,
                                    void *stream) {
-  ep::Layout L;
+  ep::Layout L{};
   if (int rc = make_layout(peers, &L)) return rc;
   MSB_CHECK_ARG(y_loc_dev && (reinterpret_cast<uintptr_t>(y_loc_dev) & 15) == 0,
                 "msb_ep_return_peers: y_loc must be 16-byte aligned");
@@ -288,14 +288,37 @@ extern "C" int msb_ep_return_peers(const msb_ep_peers_t *peers, const float *y_l
 }
 
 extern "C" int msb_ep_wait(const msb_ep_peers_t *peers, int32_t phase, void *stream) {
-  ep::Layout L;
+  ep::Layout L{};
   if (int rc = make_layout(peers, &L)) return rc;
   MSB_CHECK_ARG(phase == 0 || phase == 1, "msb_ep_wait: phase must be 0 or 1");
   int *status = nullptr;
   if (int rc = status_word(&status)) return rc;
   MSB_CUDA_TRY(launch_pdl(ep::wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
-                          L, int(phase), status));
+                          ep::phase_wait(L, phase, status)));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;
+}
+
+extern "C" int msb_ep_remap_group(const msb_ep_peers_t *peers, int32_t n_slot,
+                                  const msb_route_t *route, void *stream) {
+  ep::Layout L{};
+  if (int rc = make_layout(peers, &L)) return rc;
+  int *status = nullptr;
+  if (int rc = status_word(&status)) return rc;
+  const int32_t *ids = reinterpret_cast<const int32_t *>(L.peer[L.rank] + 2 * L.K);
+  return remap_group_wait(ids, 4, L.row_bytes, 1, L.n_rank * L.cap, nullptr, 0, n_slot, route,
+                          ep::phase_wait(L, 0, status), stream);
+}
+
+extern "C" int msb_ep_combine_peers(const msb_ep_peers_t *peers, const int32_t *pos_dev,
+                                    const float *w_dev, int32_t top_k, int32_t n_tok,
+                                    float *y_dev, void *stream) {
+  ep::Layout L{};
+  if (int rc = make_layout(peers, &L)) return rc;
+  int *status = nullptr;
+  if (int rc = status_word(&status)) return rc;
+  const float *back = reinterpret_cast<const float *>(L.peer[L.rank] + L.yback_off);
+  return ep_combine_wait(back, pos_dev, w_dev, top_k, n_tok, L.K, y_dev,
+                         ep::phase_wait(L, 1, status), stream);
 }

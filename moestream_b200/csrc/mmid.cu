@@ -506,7 +506,8 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
                            const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
                            const float *w_dev, int32_t top_k, int32_t n_tok, float *y_dev,
                            float *act_dev, void *workspace, int64_t workspace_bytes, void *stream) {
-  MSB_CHECK_ARG(gate && up && down && route && w_dev && y_dev && workspace, "msb_moe_ffn: null argument");
+  MSB_CHECK_ARG(gate && up && down && route && y_dev && workspace, "msb_moe_ffn: null argument");
+  MSB_CHECK_ARG(w_dev || top_k == 1, "msb_moe_ffn: router weights may be omitted only for top_k 1");
   MSB_CHECK_ARG(x_dev || n_tok == 0, "msb_moe_ffn: null x");
   MSB_CHECK_ARG(top_k > 0 && n_tok >= 0, "msb_moe_ffn: bad shape");
   const int64_t n_ff = down->K;
@@ -538,7 +539,8 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
     o = align_up(o + tc_act_bytes(gate->nb, pairs), 256);
     uint8_t *ha = ws + o;
     o = align_up(o + tc_act_bytes(n_ff / 32, pairs), 256);
-    float *rd = reinterpret_cast<float *>(ws + o);
+    // Without router weights (top_k 1) the down projection writes y itself.
+    float *rd = w_dev ? reinterpret_cast<float *>(ws + o) : y_dev;
     o = align_up(o + pairs * down->N * 4, 256);
     if (int rc = tc_act_terms(x_dev, x_type, 1, x_nb1, x_nb1, top_k, route->rows, pairs, gate->nb,
                               xa, st))
@@ -559,6 +561,7 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
     if (int rc = tc_projection(dn_pools, 1, rows_dn, down->N, route, pairs, ha, rd, nullptr, nullptr,
                                max_active_tc, st))
       return rc;
+    if (!w_dev) return MSB_OK;
     const int64_t total = down->N * n_tok;
     MSB_CUDA_TRY(launch_pdl(combine_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, st,
                             rd, w_dev, top_k, down->N, int64_t(n_tok), y_dev));
@@ -569,7 +572,7 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
   int64_t off = 0;
   ActQ8 xq = carve_act(ws, &off, n_tok, gate->nb);
   ActQ8 hq = carve_act(ws, &off, pairs, n_ff / 32);
-  float *rdown = reinterpret_cast<float *>(ws + off);
+  float *rdown = w_dev ? reinterpret_cast<float *>(ws + off) : y_dev;
   const int elt = x_type == MSB_TYPE_BF16 ? 2 : 4;
   if (int rc = quantize_act(x_dev, x_type, 1, x_nb1, x_nb1, n_tok, xq, st)) return rc;
   (void)elt;
@@ -601,6 +604,7 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
   d.in = hq;
   d.res = rdown;
   if (int rc = launch_gemv(down->wtype, false, d, max_active, st)) return rc;
+  if (!w_dev) return MSB_OK;
 
   const int64_t total = down->N * n_tok;
   MSB_CUDA_TRY(launch_pdl(combine_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, st,

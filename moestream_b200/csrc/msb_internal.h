@@ -25,6 +25,27 @@ void count_launch(int n = 1);
 // set by kernels whose bounded waits gave up; msb_device_status reads it).
 int status_word(int **out);
 
+// An optional wait at the start of a kernel for flags that other GPUs raise
+// (expert-parallel exchange): threads 0..n-1 of every CTA spin, bounded
+// (~1 s), until flags[t] reached *seq, then the CTA synchronizes. A wait
+// that gives up sets `bit` in *status. n == 0: no wait.
+struct FlagWait {
+  const uint32_t *flags = nullptr;
+  const uint32_t *seq = nullptr;
+  int n = 0;
+  int *status = nullptr;
+  int bit = 0;
+};
+
+// msb_remap_group whose kernel first waits on `wait` (route.cu), and
+// msb_ep_combine likewise (ep.cu).
+int remap_group_wait(const int32_t *ids_dev, int64_t nb0, int64_t nb1, int32_t top_k,
+                     int32_t n_tok, const int32_t *table_dev, int32_t n_expert, int32_t n_slot,
+                     const msb_route_t *route, const FlagWait &wait, void *stream);
+int ep_combine_wait(const float *back_dev, const int32_t *pos_dev, const float *w_dev,
+                    int32_t top_k, int32_t n_tok, int64_t K, float *y_dev, const FlagWait &wait,
+                    void *stream);
+
 // ggml block geometry of the two weight types.
 struct BlockFormat {
   int block_bytes;  // bytes per 32-element block in ggml layout
@@ -48,6 +69,24 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+__device__ __forceinline__ void flag_wait_block(const FlagWait &w) {
+  if (w.n == 0) return;
+  bool ok = true;
+  if (int(threadIdx.x) < w.n) {
+    const uint32_t seq = *reinterpret_cast<const volatile uint32_t *>(w.seq);
+    const uint32_t *f = w.flags + threadIdx.x;
+    const long long t0 = clock64();
+    for (;;) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if (int32_t(v - seq) >= 0) break;
+      if (clock64() - t0 > (1ll << 31)) { ok = false; break; }
+    }
+  }
+  if (!ok) atomicOr(w.status, w.bit);
+  __syncthreads();
+}
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                               cudaStream_t st, Args &&...args) {

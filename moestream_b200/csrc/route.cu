@@ -25,6 +25,7 @@ struct RouteArgs {
   const int32_t *table;
   int32_t n_expert, n_slot;
   int32_t *slot_ids, *counts, *offsets, *rows, *active;
+  FlagWait wait;   // ids arriving from other GPUs (expert parallelism)
 };
 
 static constexpr int kRouteThreads = 1024;
@@ -70,6 +71,7 @@ __device__ int block_exclusive_scan(int *v, int n, int *warp_sums) {
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   pdl_wait();
   pdl_trigger();
+  flag_wait_block(a.wait);
   extern __shared__ int sm[];
   const int S = a.n_slot + 1;
   int *cnt = sm;             // [S]
@@ -143,6 +145,14 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
 extern "C" int msb_remap_group(const int32_t *ids_dev, int64_t nb0, int64_t nb1, int32_t top_k,
                                int32_t n_tok, const int32_t *table_dev, int32_t n_expert,
                                int32_t n_slot, const msb_route_t *route, void *stream) {
+  return msb::remap_group_wait(ids_dev, nb0, nb1, top_k, n_tok, table_dev, n_expert, n_slot,
+                               route, msb::FlagWait{}, stream);
+}
+
+int msb::remap_group_wait(const int32_t *ids_dev, int64_t nb0, int64_t nb1, int32_t top_k,
+                          int32_t n_tok, const int32_t *table_dev, int32_t n_expert,
+                          int32_t n_slot, const msb_route_t *route, const FlagWait &wait,
+                          void *stream) {
   MSB_CHECK_ARG(route && route->slot_ids && route->counts && route->offsets && route->rows &&
                     route->active,
                 "msb_remap_group: route arrays must all be set");
@@ -155,7 +165,7 @@ extern "C" int msb_remap_group(const int32_t *ids_dev, int64_t nb0, int64_t nb1,
   MSB_CHECK_ARG(smem <= 200 * 1024, "msb_remap_group: n_slot %d too large", n_slot);
   msb::RouteArgs a{reinterpret_cast<const char *>(ids_dev), nb0, nb1, top_k, n_tok,
                    table_dev, n_expert, n_slot, route->slot_ids, route->counts,
-                   route->offsets, route->rows, route->active};
+                   route->offsets, route->rows, route->active, wait};
   if (smem > 48 * 1024)
     MSB_CUDA_TRY(cudaFuncSetAttribute(msb::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   MSB_CUDA_TRY(msb::launch_pdl(msb::route_kernel, dim3(1), dim3(msb::kRouteThreads), smem,

@@ -12,7 +12,7 @@ rank routing its own tokens. Per layer:
   2. one equal-split all-to-all of those rows (no count exchange and no
      host round trip: a destination block holds every row a source can
      send it);
-  3. the local FFN over the received rows with top_k = 1 and weight 1
+  3. the local FFN over the received rows with top_k = 1 and no weighting
      (unused rows land in the zero slot and give exact zeros);
   4. one equal-split all-to-all of the f32 results back to the source ranks;
   5. combine: y[t] = sum_k w[t, k] * (row of pair (t, k)), k ascending.
@@ -61,7 +61,6 @@ class ExpertParallel:
         self.transport = transport
         self.y_loc = torch.empty(R, K, dtype=torch.float32, device=device)
         self.pos = torch.empty(self.t_loc * top_k, dtype=torch.int32, device=device)
-        self.ones = torch.ones(R, 1, dtype=torch.float32, device=device)
         self._buf, self._opened = None, []
         if transport == "peers":
             self._open_peers(device)
@@ -73,10 +72,12 @@ class ExpertParallel:
             self.y_back = torch.empty_like(self.y_loc)
         else:
             raise ValueError(f"unknown transport {transport!r}")
+        self.route = None
         if dispatch is None or combine is None:
             from . import ops
             dispatch = dispatch or ops.ep_dispatch
             combine = combine or ops.ep_combine
+            self.route = ops.RouteBuffers(R, self.n_local, device)
         self._dispatch, self._combine = dispatch, combine
 
     def _open_peers(self, device):
@@ -161,21 +162,26 @@ class ExpertParallel:
     def layer(self, x, ids, w, local_ffn, y):
         """x: [t_loc, K] f32/bf16; ids: int32 [t_loc, top_k] global expert ids;
         w: f32 [t_loc, top_k]; y: f32 [t_loc, K] (written).
-        local_ffn(x_rows, local_ids [R, 1], ones [R, 1], out [R, K]) runs this
-        rank's experts over the received rows."""
+        local_ffn(x_rows [R, K], local_ids [R, 1], route, out [R, K]) runs this
+        rank's experts over the received rows with top_k 1 and no weighting;
+        `route` is those rows grouped by local slot (RouteBuffers) on GPUs,
+        None when dispatch and combine were passed in."""
         if self.transport == "peers":
             from . import ops
             ops.ep_dispatch_peers(self.peers, ids, x, self.n_local, self.pos)
-            ops.ep_wait(self.peers, 0)
-            local_ffn(self.recv_x(), self.recv_ids(), self.ones, self.y_loc)
+            route = ops.ep_remap_group(self.peers, self.n_local, self.route)
+            local_ffn(self.recv_x(), self.recv_ids(), route, self.y_loc)
             ops.ep_return_peers(self.peers, self.y_loc)
-            ops.ep_wait(self.peers, 1)
-            self._combine(self.y_back, self.pos, w, y)
+            ops.ep_combine_peers(self.peers, self.pos, w, y)
             return y
         self._dispatch(ids, x, self.n_local, self.world, self.cap, self.send[:, :self.K],
                        self.send_ids()[:, 0], self.pos)
         self._exchange(self.recv, self.send)
-        local_ffn(self.recv_x(), self.recv_ids(), self.ones, self.y_loc)
+        route = None
+        if self.route is not None:
+            from . import ops
+            route = ops.remap_group(self.recv_ids(), self.n_local, route=self.route)
+        local_ffn(self.recv_x(), self.recv_ids(), route, self.y_loc)
         self._exchange(self.y_back, self.y_loc)
         self._combine(self.y_back, self.pos, w, y)
         return y

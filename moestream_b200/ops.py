@@ -145,9 +145,11 @@ def mul_mat_id(pool, b, route, top_k, ws=None, out=None, stream=None):
 
 def moe_ffn(gate, up, down, x, route, w, top_k, up_row0=0, ws=None, out=None, act=None,
             stream=None):
-    """x: [n_tok, K] f32/bf16; w: [n_tok, top_k] f32. Returns y [n_tok, K] f32."""
+    """x: [n_tok, K] f32/bf16; w: [n_tok, top_k] f32, or None with top_k 1 (y is
+    the expert output itself). Returns y [n_tok, K] f32."""
     n_tok, K = x.shape
-    assert x.stride(1) == 1 and w.dtype == torch.float32 and w.is_contiguous()
+    assert x.stride(1) == 1
+    assert (w is None and top_k == 1) or (w.dtype == torch.float32 and w.is_contiguous())
     kmax = max(K, down.K)
     if ws is None:
         ws = workspace(kmax, n_tok, top_k, gate.n_slot, x.device)
@@ -206,6 +208,23 @@ def ep_wait(peers, phase, stream=None):
     """Waits (on the device, bounded) for every rank's rows (phase 0) or
     results (phase 1) to arrive in this rank's exchange buffer."""
     check(lib().msb_ep_wait(ctypes.byref(peers), phase, _stream(stream)))
+
+
+def ep_remap_group(peers, n_slot, route, stream=None):
+    """Waits (on the device, bounded) for every rank's rows, then groups the
+    received rows by local slot into `route` (RouteBuffers)."""
+    check(lib().msb_ep_remap_group(ctypes.byref(peers), n_slot, ctypes.byref(route.c),
+                                   _stream(stream)))
+    return route
+
+
+def ep_combine_peers(peers, pos, w, y, stream=None):
+    """Waits (on the device, bounded) for every result, then
+    y[t] = sum_k w[t, k] * (returned row of pair (t, k))."""
+    n_tok, top_k = w.shape
+    check(lib().msb_ep_combine_peers(ctypes.byref(peers), _ptr(pos), _ptr(w), top_k, n_tok,
+                                     _ptr(y), _stream(stream)))
+    return y
 
 
 def ep_combine(back, pos, w, y, stream=None):

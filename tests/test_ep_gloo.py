@@ -50,12 +50,13 @@ def _rank_main(rank, port, n_expert, n_tok, top_k, K, seed, out_q):
         x, ids, w = x_all[lo:lo + ep.t_loc], ids_all[lo:lo + ep.t_loc], w_all[lo:lo + ep.t_loc]
         local = mats[rank * ep.n_local:(rank + 1) * ep.n_local]
 
-        def local_ffn(rows, local_ids, ones, out):
+        def local_ffn(rows, local_ids, route, out):
+            assert route is None
             out.zero_()
             for r in range(rows.shape[0]):
                 e = int(local_ids[r, 0])
                 if e >= 0:
-                    out[r] = ones[r, 0] * (rows[r].float() @ local[e])
+                    out[r] = rows[r].float() @ local[e]
 
         y = torch.empty(ep.t_loc, K)
         ep.layer(x, ids, w, local_ffn, y)

@@ -94,11 +94,8 @@ def _rank_main(rank, world, port, transport, out_q):
             pools[role] = ops.SlotPool("mxfp4", kk, nn, ep.n_local)
             pools[role].fill(list(range(ep.n_local)),
                              [torch.from_numpy(mats[e]).pin_memory() for e in mine])
-        route = ops.RouteBuffers(world * ep.cap, ep.n_local)
-
-        def local_ffn(rows, local_ids, ones, out):
-            r = ops.remap_group(local_ids, ep.n_local, route=route)
-            ops.moe_ffn(pools["gate"], pools["up"], pools["down"], rows, r, ones, 1, out=out)
+        def local_ffn(rows, local_ids, route, out):
+            ops.moe_ffn(pools["gate"], pools["up"], pools["down"], rows, route, None, 1, out=out)
 
         lo = rank * ep.t_loc
         xs = x[lo:lo + ep.t_loc].cuda()

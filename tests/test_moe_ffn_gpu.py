@@ -114,3 +114,22 @@ def test_moe_ffn_matches_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, 
     assert O.max_abs_normalized(a, h_ex) < 1e-2
     form_err = O.max_abs_normalized(y_f, y_ex)
     assert O.max_abs_normalized(y, y_ex) < max(1e-2, form_err + 5e-4)
+
+
+def test_unweighted_top1_writes_expert_output(path):
+    """w omitted with top_k 1: y is the expert output itself, identical to
+    weighting by 1.0."""
+    from moestream_b200 import ops
+    pools, slabs, slot_of = build_layer("mxfp4", 512, 256, 6, 4, False, seed=5)
+    rng = np.random.default_rng(9)
+    x = torch.from_numpy(rng.normal(0, 1, size=(12, 512)).astype(np.float32)).cuda()
+    ids = torch.from_numpy(rng.integers(-1, 6, size=(12, 1)).astype(np.int32)).cuda()
+    table = np.full(6, -1, dtype=np.int32)
+    for e, s in slot_of.items():
+        table[e] = s
+    r = ops.remap_group(ids, 4, table=torch.from_numpy(table).cuda(), n_expert=6)
+    ones = torch.ones(12, 1, dtype=torch.float32, device="cuda")
+    want = ops.moe_ffn(pools["gate"], pools["up"], pools["down"], x, r, ones, 1)
+    got = ops.moe_ffn(pools["gate"], pools["up"], pools["down"], x, r, None, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
