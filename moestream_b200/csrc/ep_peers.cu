@@ -9,20 +9,19 @@
 //                                               K bf16 activations, then
 //                                               the int32 local expert id
 //   [y_back: n_rank*cap rows of K f32]          block d = results from rank d
-//   [control: 32 u32]                           flags[2][8] (written by the
-//                                               peers), sent[2], done[2]
-//                                               (this rank's own)
+//   [control: 32 u32]                           flags[2][8] (arrival counts
+//                                               the peers add to), sent[0]
+//                                               (this rank's layer count)
 //
-// A sending kernel stores its rows into the destinations' buffers, and its
-// last CTA to finish (a done counter) raises this rank's flag in every
-// destination to the next sequence number. A waiting kernel spins, bounded
-// (about a second), until every peer's flag reached the number of layers
-// this rank has dispatched (its own sent[0]: every rank runs the same
-// layers, so a rank waiting for layer L's rows or results expects L). The counters live in device memory, so a captured CUDA graph
-// replays the protocol correctly. Ordering: each CTA's stores are followed by
-// a system-scope fence before it counts itself done; the last CTA fences
-// again and publishes the flags with release stores; waiters load them with
-// acquire loads.
+// A sending kernel runs kCtas CTAs per peer; each stores its share of the
+// rows into that peer's buffer and then adds one to the peer's flag for this
+// rank (a system-scope release reduction after an acquire-release fence). A
+// waiting kernel spins, bounded (about a second), until every peer's flag
+// reached kCtas times the number of layers this rank has dispatched (its own
+// sent[0]: every rank runs the same layers, so a rank waiting for layer L's
+// rows or results expects kCtas * L arrivals from each peer). The counters
+// live in device memory, so a captured CUDA graph replays the protocol
+// correctly. Waiters read the flags with system-scope acquire loads.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -34,7 +33,8 @@ namespace msb {
 namespace ep {
 
 constexpr int kThreads = 256;
-constexpr int kFlags = 0, kSent = 16, kDone = 20;   // control u32 offsets
+constexpr int kFlags = 0, kSent = 16;   // control u32 offsets
+constexpr int kCtas = 32;                // CTAs per (this rank, peer) block
 
 struct Layout {
   char *peer[MSB_EP_MAX_RANKS];
@@ -45,116 +45,143 @@ struct Layout {
 __host__ __device__ inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 __host__ __device__ inline int64_t row_bytes_of(int64_t K) { return (2 * K + 4 + 15) / 16 * 16; }
 
-__device__ __forceinline__ void store_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ uint32_t *ctrl_of(const Layout &L, int r) {
   return reinterpret_cast<uint32_t *>(L.peer[r] + L.ctrl_off);
 }
 
-// Called by every CTA after its stores: the last one to finish publishes
-// phase `ph`'s next sequence number in every rank's flag for this rank.
-__device__ void publish(const Layout &L, int ph) {
-  __syncthreads();
-  if (threadIdx.x != 0) return;
-  uint32_t *own = ctrl_of(L, L.rank);
-  __threadfence_system();
-  const uint32_t prev = atomicAdd(&own[kDone + ph], 1u);
-  if (prev != gridDim.x - 1) return;
-  own[kDone + ph] = 0;
-  __threadfence_system();
-  const uint32_t seq = own[kSent + ph] + 1;
-  own[kSent + ph] = seq;
-  for (int d = 0; d < L.n_rank; ++d) store_release_sys(ctrl_of(L, d) + kFlags + ph * 8 + L.rank, seq);
+__device__ __forceinline__ int32_t e_local(int32_t e, int d, int32_t n_local) {
+  return e - d * n_local;
 }
 
-// Pairs p < n_pairs: the row of pair p (token p / top_k) goes to the rank
-// owning its expert, at block `rank` row (its rank among earlier pairs with
-// that destination); pos[p] = that destination's block row here. CTA
-// n_pairs + d marks the rows this rank leaves unused in rank d's block
-// (expert id -1).
+// After a CTA's stores into rank d's buffer: one arrival on d's flag for
+// this rank in phase `ph`. The barrier orders every thread's stores before
+// thread 0's acquire-release fence at system scope, which orders them before
+// the arrival (a release reduction) for any GPU that acquires the flag.
+__device__ __forceinline__ void arrive(const Layout &L, int d, int ph) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    uint32_t *f = ctrl_of(L, d) + kFlags + ph * 8 + L.rank;
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(f) : "memory");
+  }
+}
+
+// The CTA copies n16 16-byte words, each thread issuing all of its loads
+// (up to kBatch) before its stores, so the requests overlap instead of
+// waiting one round trip per word.
+constexpr int kBatch = 4;
+__device__ __forceinline__ void cta_copy16(uint4 *__restrict__ dst, const uint4 *__restrict__ src,
+                                           int64_t n16) {
+  for (int64_t b = 0; b < n16; b += int64_t(kThreads) * kBatch) {
+    uint4 r[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t i = b + u * kThreads + threadIdx.x;
+      if (i < n16) r[u] = src[i];
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t i = b + u * kThreads + threadIdx.x;
+      if (i < n16) dst[i] = r[u];
+    }
+  }
+}
+
+// One activation row (K values) into a bf16 row, by the whole CTA.
 template <typename T>
-__global__ void __launch_bounds__(kThreads) dispatch_kernel(const __grid_constant__ Layout L, const int32_t *ids,
-                                                            const char *x, int64_t x_nb1,
-                                                            int32_t top_k, int32_t n_pairs,
-                                                            int32_t n_local, int32_t *pos) {
+__device__ __forceinline__ void cta_copy_row_bf16(__nv_bfloat16 *dst, const T *src, int64_t K) {
+  if (sizeof(T) == 2 && K % 8 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    cta_copy16(reinterpret_cast<uint4 *>(dst), reinterpret_cast<const uint4 *>(src), K / 8);
+  } else {
+    for (int64_t i = threadIdx.x; i < K; i += kThreads) {
+      if constexpr (sizeof(T) == 2) dst[i] = src[i];
+      else dst[i] = __float2bfloat16_rn(src[i]);
+    }
+  }
+}
+
+// kCtas CTAs per destination rank d. Pair p goes to d's block `rank` at
+// row = its rank among the pairs with destination d (pair order); CTA c of d
+// copies the rows whose index is c mod kCtas, writes their pos and local
+// expert ids, marks its share of the unused rows with -1, then arrives once
+// on d's flag. CTA 0 also counts the layer (sent[0]) and writes pos -1 for
+// pairs with an invalid expert.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) dispatch_kernel(const __grid_constant__ Layout L,
+                                                            const int32_t *ids, const char *x,
+                                                            int64_t x_nb1, int32_t top_k,
+                                                            int32_t n_pairs, int32_t n_local,
+                                                            int32_t *pos) {
   pdl_wait();
   pdl_trigger();
-  __shared__ int warp_cnt[kThreads / 32];
+  __shared__ int warp_tot[kThreads / 32];
+  __shared__ int s_pair[kThreads], s_row[kThreads];
+  __shared__ int s_n;
+  const int d = blockIdx.x / kCtas, c = blockIdx.x % kCtas;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_exp = n_local * L.n_rank;
-  const bool fill = int(blockIdx.x) >= n_pairs;
-  const int p = blockIdx.x;
-  int dest;
-  if (fill) {
-    dest = p - n_pairs;
-  } else {
-    const int e = ids[p];
-    dest = (e >= 0 && e < n_exp) ? e / n_local : -1;
-  }
-  // Pairs before p (all pairs for a fill CTA) with this destination.
-  int c = 0;
-  if (dest >= 0) {
-    const int end = fill ? n_pairs : p;
-    for (int q = threadIdx.x; q < end; q += kThreads) {
-      const int eq = ids[q];
-      c += (eq >= 0 && eq < n_exp && eq / n_local == dest);
+  char *recv = L.peer[d] + int64_t(L.rank) * L.cap * L.row_bytes;
+  int base = 0;
+  for (int p0 = 0; p0 < n_pairs; p0 += kThreads) {
+    const int p = p0 + threadIdx.x;
+    const int e = p < n_pairs ? ids[p] : -1;
+    const bool valid = e >= 0 && e < n_exp;
+    const bool mine = valid && e / n_local == d;
+    if (p < n_pairs && !valid && blockIdx.x == 0) pos[p] = -1;
+    const unsigned bal = __ballot_sync(0xffffffffu, mine);
+    if (lane == 0) warp_tot[warp] = __popc(bal);
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < kThreads / 32; ++w) {
+      before += w < warp ? warp_tot[w] : 0;
+      total += warp_tot[w];
     }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-  if ((threadIdx.x & 31) == 0) warp_cnt[threadIdx.x >> 5] = c;
-  __syncthreads();
-  int rank = 0;
-  for (int w = 0; w < kThreads / 32; ++w) rank += warp_cnt[w];
-  char *recv = dest >= 0 ? L.peer[dest] + int64_t(L.rank) * L.cap * L.row_bytes : nullptr;
-  if (fill) {
-    for (int r = (rank < L.cap ? rank : L.cap) + threadIdx.x; r < L.cap; r += kThreads)
-      *reinterpret_cast<int32_t *>(recv + r * L.row_bytes + 2 * L.K) = -1;
-  } else if (dest < 0 || rank >= L.cap) {
-    if (threadIdx.x == 0) pos[p] = -1;
-  } else {
-    char *row = recv + rank * L.row_bytes;
-    if (threadIdx.x == 0) {
-      pos[p] = dest * L.cap + rank;
-      *reinterpret_cast<int32_t *>(row + 2 * L.K) = ids[p] - dest * n_local;
-    }
-    const T *src = reinterpret_cast<const T *>(x + int64_t(p / top_k) * x_nb1);
-    __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(row);
-    if (sizeof(T) == 2 && L.K % 8 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-      const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
-      uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-      for (int64_t i = threadIdx.x; i < L.K / 8; i += kThreads) d4[i] = s4[i];
-    } else {
-      for (int64_t i = threadIdx.x; i < L.K; i += kThreads) {
-        if constexpr (sizeof(T) == 2) dst[i] = src[i];
-        else dst[i] = __float2bfloat16_rn(src[i]);
+    const int row = base + before + __popc(bal & ((1u << lane) - 1));
+    if (mine && row % kCtas == c) {
+      if (row < L.cap) {
+        pos[p] = d * L.cap + row;
+        const int k = atomicAdd(&s_n, 1);
+        s_pair[k] = p;
+        s_row[k] = row;
+      } else {
+        pos[p] = -1;
       }
     }
+    __syncthreads();
+    for (int k = 0; k < s_n; ++k) {
+      const int q = s_pair[k];
+      char *dst = recv + int64_t(s_row[k]) * L.row_bytes;
+      if (threadIdx.x == 0) *reinterpret_cast<int32_t *>(dst + 2 * L.K) = e_local(ids[q], d, n_local);
+      cta_copy_row_bf16(reinterpret_cast<__nv_bfloat16 *>(dst),
+                        reinterpret_cast<const T *>(x + int64_t(q / top_k) * x_nb1), L.K);
+    }
+    base += total;
+    __syncthreads();
   }
-  publish(L, 0);
+  for (int r = base + threadIdx.x; r < L.cap; r += kThreads)
+    if (r % kCtas == c) *reinterpret_cast<int32_t *>(recv + r * L.row_bytes + 2 * L.K) = -1;
+  if (blockIdx.x == 0 && threadIdx.x == 0) ctrl_of(L, L.rank)[kSent] += 1;
+  arrive(L, d, 0);
 }
 
-// Row r of y_loc (block s = rows received from rank s) goes back to rank s,
-// block `rank`; rows whose expert id is -1 were never asked for.
-__global__ void __launch_bounds__(kThreads) return_kernel(const __grid_constant__ Layout L, const float *y_loc) {
+// kCtas CTAs per source rank s: rows i = c, c + kCtas, ... of the block
+// received from s go back into s's buffer (block `rank`), by the whole CTA;
+// rows whose expert id is -1 were never asked for.
+__global__ void __launch_bounds__(kThreads) return_kernel(const __grid_constant__ Layout L,
+                                                          const float *y_loc) {
   pdl_wait();
   pdl_trigger();
-  const int r = blockIdx.x;
-  const int s = r / L.cap, i = r % L.cap;
-  const char *recv_row = L.peer[L.rank] + int64_t(r) * L.row_bytes;
-  if (*reinterpret_cast<const int32_t *>(recv_row + 2 * L.K) >= 0) {
-    const float4 *src = reinterpret_cast<const float4 *>(y_loc + int64_t(r) * L.K);
-    float4 *dst = reinterpret_cast<float4 *>(L.peer[s] + L.yback_off +
-                                             (int64_t(L.rank) * L.cap + i) * L.K * 4);
-    for (int64_t j = threadIdx.x; j < L.K / 4; j += kThreads) dst[j] = src[j];
+  const int s = blockIdx.x / kCtas, c = blockIdx.x % kCtas;
+  for (int i = c; i < L.cap; i += kCtas) {
+    const int64_t r = int64_t(s) * L.cap + i;
+    const char *recv_row = L.peer[L.rank] + r * L.row_bytes;
+    if (*reinterpret_cast<const int32_t *>(recv_row + 2 * L.K) < 0) continue;
+    cta_copy16(reinterpret_cast<uint4 *>(L.peer[s] + L.yback_off +
+                                         (int64_t(L.rank) * L.cap + i) * L.K * 4),
+               reinterpret_cast<const uint4 *>(y_loc + r * L.K), L.K / 4);
   }
-  publish(L, 1);
+  arrive(L, s, 1);
 }
 
 // Waits until every rank published phase `ph` of the current layer here.
@@ -169,6 +196,7 @@ inline FlagWait phase_wait(const Layout &L, int ph, int *status) {
   const uint32_t *own = reinterpret_cast<const uint32_t *>(L.peer[L.rank] + L.ctrl_off);
   w.flags = own + kFlags + ph * 8;
   w.seq = own + kSent;
+  w.mult = kCtas;   // every block arrives kCtas times per layer
   w.n = L.n_rank;
   w.status = status;
   w.bit = 32 << ph;
@@ -258,7 +286,7 @@ extern "C" int msb_ep_dispatch_peers(const msb_ep_peers_t *peers, const int32_t 
   MSB_CHECK_ARG(top_k > 0 && n_tok >= 0 && n_local > 0, "msb_ep_dispatch_peers: bad shape");
   MSB_CHECK_ARG(n_tok == 0 || (ids_dev && x_dev && pos_dev), "msb_ep_dispatch_peers: null");
   const int n_pairs = top_k * n_tok;
-  const unsigned grid = unsigned(n_pairs + L.n_rank);
+  const unsigned grid = unsigned(L.n_rank * ep::kCtas);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const char *x = static_cast<const char *>(x_dev);
   if (x_type == MSB_TYPE_BF16)
@@ -280,7 +308,7 @@ extern "C" int msb_ep_return_peers(const msb_ep_peers_t *peers, const float *y_l
   if (int rc = make_layout(peers, &L)) return rc;
   MSB_CHECK_ARG(y_loc_dev && (reinterpret_cast<uintptr_t>(y_loc_dev) & 15) == 0,
                 "msb_ep_return_peers: y_loc must be 16-byte aligned");
-  MSB_CUDA_TRY(launch_pdl(ep::return_kernel, dim3(unsigned(L.n_rank * L.cap)), dim3(ep::kThreads),
+  MSB_CUDA_TRY(launch_pdl(ep::return_kernel, dim3(unsigned(L.n_rank * ep::kCtas)), dim3(ep::kThreads),
                           0, static_cast<cudaStream_t>(stream), L, y_loc_dev));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());

@@ -27,11 +27,12 @@ int status_word(int **out);
 
 // An optional wait at the start of a kernel for flags that other GPUs raise
 // (expert-parallel exchange): threads 0..n-1 of every CTA spin, bounded
-// (~1 s), until flags[t] reached *seq, then the CTA synchronizes. A wait
+// (~1 s), until flags[t] reached *seq * mult, then the CTA synchronizes. A wait
 // that gives up sets `bit` in *status. n == 0: no wait.
 struct FlagWait {
   const uint32_t *flags = nullptr;
   const uint32_t *seq = nullptr;
+  uint32_t mult = 1;
   int n = 0;
   int *status = nullptr;
   int bit = 0;
@@ -73,7 +74,7 @@ __device__ __forceinline__ void flag_wait_block(const FlagWait &w) {
   if (w.n == 0) return;
   bool ok = true;
   if (int(threadIdx.x) < w.n) {
-    const uint32_t seq = *reinterpret_cast<const volatile uint32_t *>(w.seq);
+    const uint32_t seq = *reinterpret_cast<const volatile uint32_t *>(w.seq) * w.mult;
     const uint32_t *f = w.flags + threadIdx.x;
     const long long t0 = clock64();
     for (;;) {
