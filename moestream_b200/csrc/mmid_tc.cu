@@ -57,24 +57,36 @@ constexpr int kPairs = 8;        // (token, k) pairs per pass
 constexpr int kN = kTerms * kPairs;   // MMA N: the pass's terms stacked
 constexpr int kChunk = 4;        // 32-element blocks per stage (two K=64 MMAs)
 constexpr int kThreads = 192;    // producer warp, MMA warp, 4 epilogue warps
+constexpr int kMaxActive = 1024; // slots (with the zero slot) one launch can walk
 
-template <int NV>
+// Shapes of one launch: NV weight views (2: gate and up) and G passes of
+// kPairs pairs per work item; one weight tile in shared memory feeds G
+// accumulators. Only G = 1 is launched: with G = 4 (one CTA per SM for
+// gate/up, single-buffered accumulators) a 2048-token layer ran 1.4x slower
+// than one pass per item, the epilogue of four passes serializing with the
+// MMAs.
+template <int NV, int G>
 struct Cfg {
-  // Ring depth: two CTAs per SM share 228 KB of shared memory.
-  static constexpr int kStages = NV == 2 ? 5 : 8;
+  // Decode (G = 1): two CTAs per SM, double-buffered accumulators. With
+  // G = 4 gate/up takes the whole SM (all 512 TMEM columns); down two.
+  static constexpr int kCtasPerSm = (NV == 2 && G > 1) ? 1 : 2;
+  static constexpr int kStages = G == 1 ? (NV == 2 ? 5 : 8) : (NV == 2 ? 7 : 5);
   static constexpr int kA = NV * kChunk * 2048;          // 128 rows x 16 B per block
   static constexpr int kSFA = NV * 512;
-  static constexpr int kB = kChunk * kN * 16;            // [block][term][pair] 16 B rows
-  static constexpr int kSFB = 512;                       // [term][pair] 16 B rows
+  static constexpr int kBPass = kChunk * kN * 16;        // [block][term][pair] 16 B rows
+  static constexpr int kB = G * kBPass;
+  static constexpr int kSFB = G * 512;                   // per pass [term][pair] 16 B rows
   static constexpr int kStage = kA + kSFA + kB + kSFB;
   static constexpr int kBarOff = kStages * kStage;
-  static constexpr int kSmem = kBarOff + 256;
-  static constexpr int kAccCols = NV * kN;               // one accumulator buffer
-  static constexpr int kSfCols = (NV + 1) * 4;           // TMEM columns per stage
-  static constexpr int kSfBase = 2 * kAccCols;           // after both buffers
-  static constexpr int kTmemCols = 256;
+  static constexpr int kItemOff = kBarOff + 256;           // item prefix, kMaxActive + 1 ints
+  static constexpr int kSmem = kItemOff + (kMaxActive + 1) * 4;
+  static constexpr int kAccCols = G * NV * kN;           // one accumulator buffer
+  static constexpr int kSfCols = (NV + G) * 4;           // TMEM columns per stage
+  static constexpr int kTmemCols = kCtasPerSm == 1 ? 512 : 256;
+  static constexpr int kAccBufs = 2 * kAccCols + kStages * kSfCols <= kTmemCols ? 2 : 1;
+  static constexpr int kSfBase = kAccBufs * kAccCols;    // after the buffers
   static_assert(kSfBase + kStages * kSfCols <= kTmemCols, "tensor memory map");
-  static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
+  static_assert(kCtasPerSm * (kSmem + 1024) <= 228 * 1024, "shared memory per SM");
   static_assert(kStage % 128 == 0, "TMA destinations stay 128-byte aligned");
 };
 
@@ -217,10 +229,33 @@ __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t n
                    sf + a4_off(0, blk / 4, n_pairs, pos) + (blk & 3), n_pairs * 16);
 }
 
-template <int NV>
-__global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__ Args a) {
-  using C = Cfg<NV>;
+// Item w of the launch: its active-slot index (cursor, advanced
+// monotonically as w grows), slot, pass group and tile.
+struct Item {
+  int slot, group;
+  int64_t n0;
+};
+__device__ __forceinline__ Item locate(const Args &a, const int *item0, int64_t w, int &cur) {
+  while (item0[cur + 1] <= w) ++cur;
+  const int slot = a.active[1 + cur];
+  const int64_t local = w - item0[cur];
+  const int64_t groups = (item0[cur + 1] - item0[cur]) / a.tiles;
+  return Item{slot, int(local % groups), (local / groups) * 128};
+}
+
+// Passes of kPairs pairs in item group `group` of a slot with c pairs.
+template <int G>
+__device__ __forceinline__ int passes_in_group(int c, int group) {
+  const int left = (c + kPairs - 1) / kPairs - group * G;
+  return left < G ? left : G;
+}
+
+template <int NV, int G>
+__global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
+    tc_kernel(const __grid_constant__ Args a) {
+  using C = Cfg<NV, G>;
   constexpr int kStages = C::kStages;
+  constexpr int kBufs = C::kAccBufs;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_chunks = (a.nb + kChunk - 1) / kChunk;
@@ -258,103 +293,138 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
   // activation terms are read only after it completed.
   pdl_wait();
   pdl_trigger();
-  const int64_t n_items = int64_t(a.active[0]) * a.tiles;
+  // Work items: (active slot, 128-row tile, group of up to G passes of
+  // kPairs pairs), the groups of one tile adjacent so that CTAs running them
+  // at the same time share the tile's weights through L2. item0[i] = first
+  // item of active slot i (the zero slot has one item per tile: its
+  // epilogue writes every pair's zeros).
+  int *item0 = reinterpret_cast<int *>(smem + C::kItemOff);
+  const int n_active = a.active[0];
+  for (int i = threadIdx.x; i < n_active; i += kThreads) {
+    const int slot = a.active[1 + i];
+    const int passes = slot == a.zero_slot ? 1 : (a.counts[slot] + kPairs - 1) / kPairs;
+    item0[i + 1] = (passes + G - 1) / G * a.tiles;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int carry = 0;
+    if (lane == 0) item0[0] = 0;
+    for (int b = 0; b < n_active; b += 32) {
+      int v = b + lane < n_active ? item0[b + lane + 1] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      if (b + lane < n_active) item0[b + lane + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+  const int64_t n_items = item0[n_active];
 
   if (warp == 0) {
     // ---- producer ----
     if (lane == 0) {
       uint32_t it = 0;
+      int cur = 0;
       for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
-        const int slot = a.active[1 + w / a.tiles];
+        const Item item = locate(a, item0, w, cur);
+        const int slot = item.slot;
         if (slot == a.zero_slot) continue;
-        const int64_t n0 = (w % a.tiles) * 128;
-        const int c_total = a.counts[slot];
-        const int64_t pos0 = a.offsets[slot];
-        for (int g0 = 0; g0 < c_total && !*abort_v; g0 += kPairs) {
-          const int64_t pos = pos0 + g0;
-          for (int64_t i = 0; i < n_chunks; ++i, ++it) {
-            const int s = it % kStages;
-            if (!sm100::mbar_wait_bounded(&empty[s], ((it / kStages) & 1) ^ 1)) {
-              atomicOr(&g_status, kStatusProducer);
-              *abort_v = 1;
-              break;
-            }
-            uint8_t *st = smem + s * C::kStage;
-            uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
-            const int64_t b0 = i * kChunk;
-            // Full boxes are counted (rows or blocks outside the tensors
-            // arrive as zeros).
-            sm100::mbar_expect_tx(&full[s], uint32_t(C::kStage));
-            for (int v = 0; v < NV; ++v) {
-              const int64_t r0 = a.row0[v] + n0;
-              sm100::tma_3d(sA + v * kChunk * 2048, &a.tm_w[v], int(r0) * 2, int(b0), slot,
+        const int n_real = passes_in_group<G>(a.counts[slot], item.group);
+        const int64_t pos0 = a.offsets[slot] + int64_t(item.group) * G * kPairs;
+        for (int64_t i = 0; i < n_chunks; ++i, ++it) {
+          const int s = it % kStages;
+          if (!sm100::mbar_wait_bounded(&empty[s], ((it / kStages) & 1) ^ 1)) {
+            atomicOr(&g_status, kStatusProducer);
+            *abort_v = 1;
+            break;
+          }
+          uint8_t *st = smem + s * C::kStage;
+          uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
+          const int64_t b0 = i * kChunk;
+          // Full boxes are counted (rows or blocks outside the tensors
+          // arrive as zeros); passes past the slot's pairs are not loaded.
+          sm100::mbar_expect_tx(&full[s],
+                                uint32_t(C::kStage - (G - n_real) * (C::kBPass + 512)));
+          for (int v = 0; v < NV; ++v) {
+            const int64_t r0 = a.row0[v] + item.n0;
+            sm100::tma_3d(sA + v * kChunk * 2048, &a.tm_w[v], int(r0) * 2, int(b0), slot,
+                          &full[s]);
+            const uint8_t *slot_base = a.pool[v] + int64_t(slot) * a.slot_stride[v];
+            const uint8_t *sf_base = slot_base + a.nb * a.N[v] * 16;
+            const int64_t sf_tiles = (a.N[v] + 127) / 128;
+            sm100::bulk_g2s(sSFA + v * 512, sf_base + (i * sf_tiles + (r0 >> 7)) * 512, 512,
                             &full[s]);
-              const uint8_t *slot_base = a.pool[v] + int64_t(slot) * a.slot_stride[v];
-              const uint8_t *sf_base = slot_base + a.nb * a.N[v] * 16;
-              const int64_t sf_tiles = (a.N[v] + 127) / 128;
-              sm100::bulk_g2s(sSFA + v * 512, sf_base + (i * sf_tiles + (r0 >> 7)) * 512, 512,
-                              &full[s]);
-            }
-            sm100::tma_3d(sB, &a.tm_aq, int(pos) * 2, 0, int(b0), &full[s]);
-            sm100::tma_3d(sSFB, &a.tm_asf, int(pos) * 2, 0, int(i), &full[s]);
+          }
+          for (int g = 0; g < n_real; ++g) {
+            const int pos = int(pos0 + g * kPairs);
+            sm100::tma_3d(sB + g * C::kBPass, &a.tm_aq, pos * 2, 0, int(b0), &full[s]);
+            sm100::tma_3d(sSFB + g * 512, &a.tm_asf, pos * 2, 0, int(i), &full[s]);
           }
         }
       }
       // No copy may still be landing in shared memory when the CTA exits
       // (only possible after an abort): wait for the last stages issued.
       for (uint32_t k = it > uint32_t(kStages) ? it - kStages : 0; k < it; ++k)
-        if (!sm100::mbar_wait_bounded(&full[k % kStages], (k / kStages) & 1)) atomicOr(&g_status, kStatusDrain);
+        if (!sm100::mbar_wait_bounded(&full[k % kStages], (k / kStages) & 1))
+          atomicOr(&g_status, kStatusDrain);
     }
   } else if (warp == 1) {
     // ---- scale-factor copies and MMA issue ----
     if (lane == 0) {
       uint32_t it = 0, acc = 0;
+      int cur = 0;
       for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
-        const int slot = a.active[1 + w / a.tiles];
-        if (slot == a.zero_slot) continue;
-        const int c_total = a.counts[slot];
-        for (int g0 = 0; g0 < c_total && !*abort_v; g0 += kPairs, ++acc) {
-          const int buf = acc & 1;
-          if (!sm100::mbar_wait_bounded(&acc_empty[buf], ((acc >> 1) & 1) ^ 1)) {
-            atomicOr(&g_status, kStatusAccEmpty);
+        const Item item = locate(a, item0, w, cur);
+        if (item.slot == a.zero_slot) continue;
+        const int n_real = passes_in_group<G>(a.counts[item.slot], item.group);
+        const int buf = acc % kBufs;
+        if (!sm100::mbar_wait_bounded(&acc_empty[buf], ((acc / kBufs) & 1) ^ 1)) {
+          atomicOr(&g_status, kStatusAccEmpty);
+          *abort_v = 1;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t d0 = tmem + buf * C::kAccCols;
+        for (int64_t i = 0; i < n_chunks; ++i, ++it) {
+          const int s = it % kStages;
+          if (!sm100::mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
+            atomicOr(&g_status, kStatusFull);
             *abort_v = 1;
             break;
           }
-          sm100::tc_fence_after();
-          const uint32_t d0 = tmem + buf * C::kAccCols;
-          for (int64_t i = 0; i < n_chunks; ++i, ++it) {
-            const int s = it % kStages;
-            if (!sm100::mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
-              atomicOr(&g_status, kStatusFull);
-              *abort_v = 1;
-              break;
-            }
-            const uint8_t *st = smem + s * C::kStage;
-            const uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
-            const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols;
-            for (int v = 0; v < NV; ++v)
-              sm100::tmem_cp_32x128b_x4(sf_col + v * 4,
-                                        sm100::smem_desc(sm100::smem_u32(sSFA + v * 512), 0, 128));
-            sm100::tmem_cp_32x128b_x4(sf_col + NV * 4,
-                                      sm100::smem_desc(sm100::smem_u32(sSFB), 0, 128));
-            const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
-            for (int j = 0; j < kbn / 2; ++j) {
-              const uint32_t sel = uint32_t(2 * j);
+          const uint8_t *st = smem + s * C::kStage;
+          const uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
+          const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols;
+          for (int v = 0; v < NV; ++v)
+            sm100::tmem_cp_32x128b_x4(sf_col + v * 4,
+                                      sm100::smem_desc(sm100::smem_u32(sSFA + v * 512), 0, 128));
+          for (int g = 0; g < n_real; ++g)
+            sm100::tmem_cp_32x128b_x4(
+                sf_col + (NV + g) * 4, sm100::smem_desc(sm100::smem_u32(sSFB + g * 512), 0, 128));
+          const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
+          for (int j = 0; j < kbn / 2; ++j) {
+            const uint32_t sel = uint32_t(2 * j);
+            for (int g = 0; g < n_real; ++g) {
               // B: 32 stacked rows of 16 B per block; K-halves one block apart.
-              const uint64_t bdesc =
-                  sm100::smem_desc(sm100::smem_u32(sB + 2 * j * (kN * 16)), kN * 16, 128);
+              const uint64_t bdesc = sm100::smem_desc(
+                  sm100::smem_u32(sB + g * C::kBPass + 2 * j * (kN * 16)), kN * 16, 128);
               for (int v = 0; v < NV; ++v) {
-                const uint64_t adesc =
-                    sm100::smem_desc(sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
-                sm100::mma_mxf4(d0 + v * kN, adesc, bdesc, sm100::idesc_mxf4(kN, sel, sel),
-                                (sf_col + v * 4) | (sel << 30), (sf_col + NV * 4) | (sel << 30),
+                const uint64_t adesc = sm100::smem_desc(
+                    sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
+                sm100::mma_mxf4(d0 + (g * NV + v) * kN, adesc, bdesc,
+                                sm100::idesc_mxf4(kN, sel, sel), (sf_col + v * 4) | (sel << 30),
+                                (sf_col + (NV + g) * 4) | (sel << 30),
                                 (i == 0 && j == 0) ? 0u : 1u);
               }
             }
-            sm100::tc_commit(&empty[s]);
           }
-          sm100::tc_commit(&acc_full[buf]);
+          sm100::tc_commit(&empty[s]);
         }
+        sm100::tc_commit(&acc_full[buf]);
+        ++acc;
       }
       // Every MMA and scale-factor copy is complete before tensor memory is
       // released.
@@ -366,9 +436,11 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
     const int quad = warp & 3;            // TMEM lane quadrant of this warp
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     uint32_t acc = 0;
+    int cur = 0;
     for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
-      const int slot = a.active[1 + w / a.tiles];
-      const int64_t n0 = (w % a.tiles) * 128;
+      const Item item = locate(a, item0, w, cur);
+      const int slot = item.slot;
+      const int64_t n0 = item.n0;
       const int64_t n = n0 + quad * 32 + lane;
       const bool valid = n < a.n_out;
       const int64_t blk = (n0 >> 5) + quad;   // SwiGLU output block of this warp
@@ -398,38 +470,46 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
         }
         continue;
       }
-      for (int g0 = 0; g0 < c_total && !*abort_v; g0 += kPairs, ++acc) {
+      const int n_real = passes_in_group<G>(c_total, item.group);
+      const uint32_t a_i = acc++;
+      const int buf = a_i % kBufs;
+      if (!sm100::mbar_wait_bounded(&acc_full[buf], (a_i / kBufs) & 1)) {
+        atomicOr(&g_status, kStatusAccFull);
+        *abort_v = 1;
+        break;
+      }
+      sm100::tc_fence_after();
+      for (int g = 0; g < n_real; ++g) {
+        const int g0 = (item.group * G + g) * kPairs;
         const int cc = min(kPairs, c_total - g0);
         const int64_t pos = pos0 + g0;
-        const int buf = acc & 1;
-        if (!sm100::mbar_wait_bounded(&acc_full[buf], (acc >> 1) & 1)) {
-          atomicOr(&g_status, kStatusAccFull);
-          *abort_v = 1;
-          break;
-        }
-        sm100::tc_fence_after();
+        const uint32_t col = tmem + lane_addr + buf * C::kAccCols + g * NV * kN;
         uint32_t dg[32], du[32];
-        sm100::tmem_ld_32cols(tmem + lane_addr + buf * C::kAccCols, dg);
-        if constexpr (NV == 2) sm100::tmem_ld_32cols(tmem + lane_addr + buf * C::kAccCols + kN, du);
+        sm100::tmem_ld_32cols(col, dg);
+        if constexpr (NV == 2) sm100::tmem_ld_32cols(col + kN, du);
         sm100::tmem_ld_wait();
-        sm100::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
-                                        sm100::smem_u32(&acc_empty[buf]))
-                                    : "memory");
+        if (g == n_real - 1) {
+          // Every accumulator of the item is in registers: release the buffer.
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0)
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                             sm100::smem_u32(&acc_empty[buf]))
+                         : "memory");
+        }
 #pragma unroll
         for (int j = 0; j < kPairs; ++j) {
           if (j >= cc) break;
           const int64_t pair = a.rows[pos + j];
           // Column t * 8 + j holds term t of pair j.
-          const float g = (__uint_as_float(dg[j]) + __uint_as_float(dg[kPairs + j])) +
-                          (__uint_as_float(dg[2 * kPairs + j]) + __uint_as_float(dg[3 * kPairs + j]));
+          const float gv = (__uint_as_float(dg[j]) + __uint_as_float(dg[kPairs + j])) +
+                           (__uint_as_float(dg[2 * kPairs + j]) + __uint_as_float(dg[3 * kPairs + j]));
           if constexpr (NV == 1) {
-            if (valid) a.res[pair * a.n_out + n] = g;
+            if (valid) a.res[pair * a.n_out + n] = gv;
           } else {
             const float u = (__uint_as_float(du[j]) + __uint_as_float(du[kPairs + j])) +
                             (__uint_as_float(du[2 * kPairs + j]) + __uint_as_float(du[3 * kPairs + j]));
-            const float h = valid ? g / (1.f + expf(-g)) * u : 0.f;
+            const float h = valid ? gv / (1.f + expf(-gv)) * u : 0.f;
             if (a.act && valid) a.act[pair * a.n_out + n] = h;
             if (blk < a.o_nb)
               warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, pos + j), a.a_rows * 16,
@@ -482,24 +562,26 @@ int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb
   return MSB_OK;
 }
 
-template <int NV>
-static int launch_tc_t(const tc::Args &a, int max_active, cudaStream_t st) {
-  using C = tc::Cfg<NV>;
-  MSB_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    C::kSmem));
-  // Persistent grid: two CTAs per SM (shared memory allows two), never more
-  // than the work items the route can produce.
+template <int NV, int G>
+static int launch_tc_t(const tc::Args &a, int max_active, int64_t n_pairs, cudaStream_t st) {
+  using C = tc::Cfg<NV, G>;
+  MSB_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<NV, G>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+  // Persistent grid: as many CTAs as fit (shared and tensor memory), never
+  // more than the work items the route can produce (each active slot has at
+  // most ceil(pairs / (kPairs * G)) + 1 groups per tile).
   static int n_sm = 0;
   if (!n_sm) {
     int dev = 0;
     MSB_CUDA_TRY(cudaGetDevice(&dev));
     MSB_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
   }
-  int64_t grid = int64_t(max_active) * a.tiles;
-  if (grid > 2 * n_sm) grid = 2 * n_sm;
+  const int64_t groups = int64_t(max_active) + n_pairs / (int64_t(tc::kPairs) * G) + 1;
+  int64_t grid = groups * a.tiles;
+  if (grid > int64_t(C::kCtasPerSm) * n_sm) grid = int64_t(C::kCtasPerSm) * n_sm;
   if (grid == 0) return MSB_OK;
-  MSB_CUDA_TRY(launch_pdl(tc::tc_kernel<NV>, dim3(unsigned(grid)), dim3(tc::kThreads), C::kSmem, st,
-                          a));
+  MSB_CUDA_TRY(launch_pdl(tc::tc_kernel<NV, G>, dim3(unsigned(grid)), dim3(tc::kThreads), C::kSmem,
+                          st, a));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;
@@ -531,6 +613,9 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   a.rows = route->rows;
   a.active = route->active;
   a.zero_slot = pool->n_slot;
+  if (pool->n_slot + 1 > tc::kMaxActive)
+    return fail(MSB_ERR_UNSUPPORTED, "tensor-core path: %d slots exceed %d", pool->n_slot,
+                tc::kMaxActive - 1);
   a.aq = act_in;
   a.asf = act_in + int64_t(tc::kTerms) * pool->nb * n_pairs * 16;
   a.a_rows = n_pairs;
@@ -553,7 +638,8 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
         !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sq, bf))
       return fail(MSB_ERR_CUDA, "tensor-core path: activation tensor maps could not be encoded");
   }
-  return nv == 2 ? launch_tc_t<2>(a, max_active, st) : launch_tc_t<1>(a, max_active, st);
+  return nv == 2 ? launch_tc_t<2, 1>(a, max_active, n_pairs, st)
+                 : launch_tc_t<1, 1>(a, max_active, n_pairs, st);
 }
 
 }  // namespace msb

@@ -72,6 +72,7 @@ SHAPES = [
     ("mxfp4", 2880, 256, 10, 6, 4, 4, 1),     # gpt-oss K (90 blocks: uneven warp split)
     ("mxfp4", 2880, 2880, 6, 4, 3, 4, 4),     # gpt-oss down: last 128-row tile half full
     ("mxfp4", 256, 96, 8, 5, 60, 4, 4),       # many pairs per slot (> 8 and > 32: passes)
+    ("mxfp4", 2880, 384, 6, 3, 64, 4, 1),     # prompt-sized: ~8 passes per slot, 3 row tiles
     ("mxfp4", 96, 64, 6, 4, 5, 2, 1),         # K not a multiple of 64: CUDA cores
     ("iq4_nl", 96, 40, 6, 4, 5, 2, 1),        # N not a multiple of 32
 ]
