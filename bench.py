@@ -422,6 +422,10 @@ def main():
     except OSError:
         pass
     hbm = float(peaks.get("hbm_gbs", 6650.0))
+    # DRAM bytes (read + write) of one gate/up launch of this workload, from
+    # the committed ncu capture of the same layer shape
+    # (profiles/tc_kernel_moe_ffn_decode_64tok.md); other shapes: unmeasured.
+    traffic = 1.025e9 if (world == 1 and T == SHAPE["tokens"]) else None
     # Graphs holding NCCL calls must be gone before the process group is
     # destroyed.
     graphs.clear()
@@ -499,7 +503,7 @@ def main():
                                         else "NCCL all-to-all"),
                            "launch": "eager" if args.eager else "one CUDA graph per step"},
                 "roofline": {"bound": "hbm", "achieved": gate_gbs, "peak": hbm, "unit": "GB/s",
-                             "frac": gate_gbs / hbm, "traffic": None,
+                             "frac": gate_gbs / hbm, "traffic": traffic,
                              "kernel": "tc_kernel<2> (fused gate/up mul_mat_id, tcgen05 mxf4)",
                              "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
