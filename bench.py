@@ -211,7 +211,7 @@ def run_layer(ctx, layer, x, ids, w, y, timed_events=None):
     def local_ffn(rows, local_ids, route, out):
         ops.moe_ffn(ga, up, dn, rows, route, None, 1, ws=ctx["ws"], out=out)
 
-    ep.layer(x, ids, w, local_ffn, y)
+    ep.layer(x, ids, w, local_ffn, y, pools=(ga, up, dn, 0, ctx["ws"]))
 
 
 def cpu_sample(layer0, tokens, top_k, K, n_ff, n_expert, ids0, w0, x0, threads):

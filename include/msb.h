@@ -281,6 +281,7 @@ int msb_ep_combine(const float *back_dev, const int32_t *pos_dev,
  *                          ids (top_k 1, no table; -1 -> zero slot)
  *   ... local FFN over the received rows (buffer offset 0) ...
  *   msb_ep_return_peers    results back into the sources' buffers
+ *                          (or both at once: msb_ep_moe_ffn_peers)
  *   msb_ep_combine_peers   waits until every result for this rank arrived
  *                          (f32 rows at offset msb_ep_yback_offset), then
  *                          msb_ep_combine
@@ -317,6 +318,17 @@ int msb_ep_remap_group(const msb_ep_peers_t *peers, int32_t n_slot,
 int msb_ep_combine_peers(const msb_ep_peers_t *peers, const int32_t *pos_dev,
                          const float *w_dev, int32_t top_k, int32_t n_tok,
                          float *y_dev, void *stream);
+/* The local FFN over the received rows with the return fused in: the down
+ * projection's epilogue stores every result row straight into its source
+ * rank's buffer over NVLink and the kernel's last CTA raises the result
+ * flags, replacing msb_moe_ffn + msb_ep_return_peers. MXFP4 pools of
+ * tensor-core shapes only (MSB_ERR_UNSUPPORTED otherwise, nothing launched);
+ * route from msb_ep_remap_group; workspace as msb_moe_ffn with
+ * n_tok = n_rank * cap, top_k = 1. */
+int msb_ep_moe_ffn_peers(const msb_ep_peers_t *peers, msb_pool_t gate,
+                         msb_pool_t up, int64_t up_row0, msb_pool_t down,
+                         const msb_route_t *route, void *workspace,
+                         int64_t workspace_bytes, void *stream);
 
 /* ======================================================================== */
 /* Measurement hooks                                                          */

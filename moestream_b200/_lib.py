@@ -119,6 +119,9 @@ SIGNATURES = {
     "msb_ep_wait": (ctypes.c_int, [ctypes.POINTER(EpPeers), ctypes.c_int32, c_vp]),
     "msb_ep_remap_group": (ctypes.c_int, [ctypes.POINTER(EpPeers), ctypes.c_int32,
                                           ctypes.POINTER(Route), c_vp]),
+    "msb_ep_moe_ffn_peers": (ctypes.c_int, [ctypes.POINTER(EpPeers), c_vp, c_vp, ctypes.c_int64,
+                                            c_vp, ctypes.POINTER(Route), c_vp, ctypes.c_int64,
+                                            c_vp]),
     "msb_ep_combine_peers": (ctypes.c_int, [ctypes.POINTER(EpPeers), c_vp, c_vp, ctypes.c_int32,
                                             ctypes.c_int32, c_vp, c_vp]),
     "msb_ep_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, ctypes.c_int32, ctypes.c_int32,

@@ -11,15 +11,19 @@
 //   [y_back: n_rank*cap rows of K f32]          block d = results from rank d
 //   [control: 32 u32]                           flags[2][8] (arrival counts
 //                                               the peers add to), sent[0]
-//                                               (this rank's layer count)
+//                                               (this rank's layer count),
+//                                               done (results sent, per
+//                                               launch)
 //
-// A sending kernel runs kCtas CTAs per peer; each stores its share of the
+// The dispatch kernel runs kCtas CTAs per peer; each stores its share of the
 // rows into that peer's buffer and then adds one to the peer's flag for this
-// rank (a system-scope release reduction after an acquire-release fence). A
+// rank (a system-scope release reduction after an acquire-release fence).
+// Results go back either from the down projection's epilogue itself
+// (msb_ep_moe_ffn_peers) or by return_kernel; in both the last CTA to finish
+// (a done counter) adds one to each source's result flag for this rank. A
 // waiting kernel spins, bounded (about a second), until every peer's flag
-// reached kCtas times the number of layers this rank has dispatched (its own
-// sent[0]: every rank runs the same layers, so a rank waiting for layer L's
-// rows or results expects kCtas * L arrivals from each peer). The counters
+// reached kCtas (rows) or 1 (results) times the number of layers this rank
+// has dispatched (its own sent[0]: every rank runs the same layers). The counters
 // live in device memory, so a captured CUDA graph replays the protocol
 // correctly. Waiters read the flags with system-scope acquire loads.
 #include <cuda_bf16.h>
@@ -33,7 +37,7 @@ namespace msb {
 namespace ep {
 
 constexpr int kThreads = 256;
-constexpr int kFlags = 0, kSent = 16;   // control u32 offsets
+constexpr int kFlags = 0, kSent = 16, kDone = 17;   // control u32 offsets
 constexpr int kCtas = 32;                // CTAs per (this rank, peer) block
 
 struct Layout {
@@ -167,7 +171,8 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(const __grid_constan
 
 // kCtas CTAs per source rank s: rows i = c, c + kCtas, ... of the block
 // received from s go back into s's buffer (block `rank`), by the whole CTA;
-// rows whose expert id is -1 were never asked for.
+// rows whose expert id is -1 were never asked for. The last CTA to finish
+// adds one to every source's result flag for this rank.
 __global__ void __launch_bounds__(kThreads) return_kernel(const __grid_constant__ Layout L,
                                                           const float *y_loc) {
   pdl_wait();
@@ -181,7 +186,19 @@ __global__ void __launch_bounds__(kThreads) return_kernel(const __grid_constant_
                                          (int64_t(L.rank) * L.cap + i) * L.K * 4),
                reinterpret_cast<const uint4 *>(y_loc + r * L.K), L.K / 4);
   }
-  arrive(L, s, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t *own = ctrl_of(L, L.rank);
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    if (atomicAdd(own + kDone, 1u) == gridDim.x - 1) {
+      own[kDone] = 0;
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      for (int d = 0; d < L.n_rank; ++d) {
+        uint32_t *f = ctrl_of(L, d) + kFlags + 8 + L.rank;
+        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(f) : "memory");
+      }
+    }
+  }
 }
 
 // Waits until every rank published phase `ph` of the current layer here.
@@ -196,7 +213,7 @@ inline FlagWait phase_wait(const Layout &L, int ph, int *status) {
   const uint32_t *own = reinterpret_cast<const uint32_t *>(L.peer[L.rank] + L.ctrl_off);
   w.flags = own + kFlags + ph * 8;
   w.seq = own + kSent;
-  w.mult = kCtas;   // every block arrives kCtas times per layer
+  w.mult = ph == 0 ? kCtas : 1;   // rows: kCtas arrivals per peer per layer
   w.n = L.n_rank;
   w.status = status;
   w.bit = 32 << ph;
@@ -349,4 +366,23 @@ extern "C" int msb_ep_combine_peers(const msb_ep_peers_t *peers, const int32_t *
   const float *back = reinterpret_cast<const float *>(L.peer[L.rank] + L.yback_off);
   return ep_combine_wait(back, pos_dev, w_dev, top_k, n_tok, L.K, y_dev,
                          ep::phase_wait(L, 1, status), stream);
+}
+
+extern "C" int msb_ep_moe_ffn_peers(const msb_ep_peers_t *peers, msb_pool_t gate, msb_pool_t up,
+                                    int64_t up_row0, msb_pool_t down, const msb_route_t *route,
+                                    void *workspace, int64_t workspace_bytes, void *stream) {
+  ep::Layout L{};
+  if (int rc = make_layout(peers, &L)) return rc;
+  RowTarget rows;
+  for (int s = 0; s < L.n_rank; ++s) {
+    rows.blk[s] = reinterpret_cast<float *>(L.peer[s] + L.yback_off) + int64_t(L.rank) * L.cap * L.K;
+    rows.arrive[s] = reinterpret_cast<uint32_t *>(L.peer[s] + L.ctrl_off) + ep::kFlags + 8 + L.rank;
+  }
+  rows.cap = L.cap;
+  rows.ld = L.K;
+  rows.skip_zero = true;   // rows with expert -1 are padding nobody reads
+  rows.done = reinterpret_cast<uint32_t *>(L.peer[L.rank] + L.ctrl_off) + ep::kDone;
+  rows.n_arrive = L.n_rank;
+  return moe_ffn_to_rows(gate, up, up_row0, down, L.peer[L.rank], MSB_TYPE_BF16, L.row_bytes, route,
+                         L.n_rank * L.cap, rows, workspace, workspace_bytes, stream);
 }

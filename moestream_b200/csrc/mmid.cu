@@ -36,7 +36,8 @@ int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb
                  const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st);
 int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
-                  uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st);
+                  uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st,
+                  const RowTarget *res_rows = nullptr);
 
 // MXFP4 arithmetic: 0 = tensor cores where the shapes allow, 1 = CUDA cores
 // with int8 activations (ggml's q8_0 form) everywhere.
@@ -502,11 +503,16 @@ extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, in
   return launch_gemv(pool->wtype, false, g, max_active, st);
 }
 
-extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
-                           const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
-                           const float *w_dev, int32_t top_k, int32_t n_tok, float *y_dev,
-                           float *act_dev, void *workspace, int64_t workspace_bytes, void *stream) {
-  MSB_CHECK_ARG(gate && up && down && route && y_dev && workspace, "msb_moe_ffn: null argument");
+// msb_moe_ffn; with `rows` the down projection stores its result rows there
+// instead of y (top_k 1, no weights, tensor-core shapes only).
+static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
+                        const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
+                        const float *w_dev, int32_t top_k, int32_t n_tok, float *y_dev,
+                        float *act_dev, void *workspace, int64_t workspace_bytes,
+                        const RowTarget *rows, void *stream) {
+  MSB_CHECK_ARG(gate && up && down && route && (y_dev || rows) && workspace,
+                "msb_moe_ffn: null argument");
+  MSB_CHECK_ARG(!rows || (!w_dev && top_k == 1), "msb_moe_ffn: row targets need top_k 1");
   MSB_CHECK_ARG(w_dev || top_k == 1, "msb_moe_ffn: router weights may be omitted only for top_k 1");
   MSB_CHECK_ARG(x_dev || n_tok == 0, "msb_moe_ffn: null x");
   MSB_CHECK_ARG(top_k > 0 && n_tok >= 0, "msb_moe_ffn: bad shape");
@@ -530,8 +536,11 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   const int64_t pairs = int64_t(n_tok) * top_k;
   const int max_active_tc = int(pairs < gate->n_slot + 1 ? pairs : gate->n_slot + 1);
-  if (g_mxfp4_path == 0 && tc_supported(gate) && tc_supported(up) && tc_supported(down) &&
-      n_ff % 64 == 0 && up_row0 % 128 == 0) {
+  const bool tc = g_mxfp4_path == 0 && tc_supported(gate) && tc_supported(up) &&
+                  tc_supported(down) && n_ff % 64 == 0 && up_row0 % 128 == 0;
+  if (rows && !tc)
+    return fail(MSB_ERR_UNSUPPORTED, "msb_moe_ffn: row targets need the tensor-core path");
+  if (tc) {
     // Tensor cores: x terms per pair -> fused gate/up + SwiGLU writing the
     // down projection's terms -> down projection -> weighted combine.
     int64_t o = 0;
@@ -559,7 +568,7 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
     const int64_t rows_dn[2] = {0, 0};
     const msb_pool_s *dn_pools[2] = {down, down};
     if (int rc = tc_projection(dn_pools, 1, rows_dn, down->N, route, pairs, ha, rd, nullptr, nullptr,
-                               max_active_tc, st))
+                               max_active_tc, st, rows))
       return rc;
     if (!w_dev) return MSB_OK;
     const int64_t total = down->N * n_tok;
@@ -612,6 +621,22 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
   return MSB_OK;
+}
+
+extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
+                           const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
+                           const float *w_dev, int32_t top_k, int32_t n_tok, float *y_dev,
+                           float *act_dev, void *workspace, int64_t workspace_bytes, void *stream) {
+  return moe_ffn_core(gate, up, up_row0, down, x_dev, x_type, x_nb1, route, w_dev, top_k, n_tok,
+                      y_dev, act_dev, workspace, workspace_bytes, nullptr, stream);
+}
+
+int msb::moe_ffn_to_rows(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
+                         const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
+                         int32_t n_tok, const RowTarget &rows, void *workspace,
+                         int64_t workspace_bytes, void *stream) {
+  return moe_ffn_core(gate, up, up_row0, down, x_dev, x_type, x_nb1, route, nullptr, 1, n_tok,
+                      nullptr, nullptr, workspace, workspace_bytes, &rows, stream);
 }
 
 // ---- mul_mat_id without allocation ------------------------------------------

@@ -104,11 +104,16 @@ struct Args {
   int32_t zero_slot;
   const uint8_t *aq, *asf;   // activation terms (grouped pair order)
   int64_t a_rows;            // rows of the activation buffers (= pairs)
-  float *res;                // one view: res[pair * n_out + n]
+  RowTarget out;              // one view: result row of each pair
   uint8_t *oq, *osf;         // two views: terms of silu(gate) * up
   int64_t o_nb;              // n_out / 32
   float *act;                // two views, optional: f32 silu(gate) * up
 };
+
+__device__ __forceinline__ float *out_row(const RowTarget &t, int64_t r) {
+  const int64_t b = r / t.cap;
+  return t.blk[b] + (r - b * t.cap) * t.ld;
+}
 
 // Status bits of the tensor-core kernels on this device (see
 // msb_device_status): which bounded wait gave up.
@@ -453,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
         for (int j = 0; j < c_total; ++j) {
           const int64_t pair = a.rows[pos0 + j];
           if constexpr (NV == 1) {
-            if (valid) a.res[pair * a.n_out + n] = 0.f;
+            if (valid && !a.out.skip_zero) out_row(a.out, pair)[n] = 0.f;
           } else {
             if (a.act && valid) a.act[pair * a.n_out + n] = 0.f;
           }
@@ -505,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
           const float gv = (__uint_as_float(dg[j]) + __uint_as_float(dg[kPairs + j])) +
                            (__uint_as_float(dg[2 * kPairs + j]) + __uint_as_float(dg[3 * kPairs + j]));
           if constexpr (NV == 1) {
-            if (valid) a.res[pair * a.n_out + n] = gv;
+            if (valid) out_row(a.out, pair)[n] = gv;
           } else {
             const float u = (__uint_as_float(du[j]) + __uint_as_float(du[kPairs + j])) +
                             (__uint_as_float(du[2 * kPairs + j]) + __uint_as_float(du[3 * kPairs + j]));
@@ -527,6 +532,18 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
   if (warp == 0) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, C::kTmemCols);
+  }
+  if (a.out.done && threadIdx.x == 0) {
+    // This CTA's rows are stored (the barrier above); the last CTA to count
+    // itself done tells the rows' owners, once per launch.
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    if (atomicAdd(a.out.done, 1u) == gridDim.x - 1) {
+      *a.out.done = 0;
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      for (int i = 0; i < a.out.n_arrive; ++i)
+        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.out.arrive[i])
+                     : "memory");
+    }
   }
 }
 
@@ -593,7 +610,8 @@ static int launch_tc_t(const tc::Args &a, int max_active, int64_t n_pairs, cudaS
 // act_out, nv == 1 writes res.
 int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
-                  uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st) {
+                  uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st,
+                  const RowTarget *res_rows) {
   const msb_pool_s *pool = pools[0];
   tc::Args a{};
   for (int v = 0; v < 2; ++v) {
@@ -619,7 +637,13 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   a.aq = act_in;
   a.asf = act_in + int64_t(tc::kTerms) * pool->nb * n_pairs * 16;
   a.a_rows = n_pairs;
-  a.res = res;
+  if (res_rows) {
+    a.out = *res_rows;
+  } else {
+    a.out.blk[0] = res;
+    a.out.cap = n_pairs > 0 ? int32_t(n_pairs) : 1;
+    a.out.ld = n_out;
+  }
   a.oq = act_out;
   a.o_nb = n_out / 32;
   a.osf = act_out ? act_out + int64_t(tc::kTerms) * a.o_nb * n_pairs * 16 : nullptr;

@@ -38,6 +38,30 @@ struct FlagWait {
   int bit = 0;
 };
 
+// Where a projection's f32 result rows go when they are not one contiguous
+// [pairs][n_out] array: row r at blk[r / cap] + (r % cap) * ld floats (the
+// blocks may be other GPUs' memory). Rows routed to the zero slot are not
+// written when skip_zero. With done set, the kernel's last CTA to finish
+// adds one to every arrive[i] (a system-scope release) once all rows are
+// stored; done is a counter of this GPU that starts at and returns to 0.
+struct RowTarget {
+  float *blk[MSB_EP_MAX_RANKS] = {};
+  int32_t cap = 0;
+  int64_t ld = 0;
+  bool skip_zero = false;
+  uint32_t *done = nullptr;
+  uint32_t *arrive[MSB_EP_MAX_RANKS] = {};
+  int32_t n_arrive = 0;
+};
+
+// msb_moe_ffn whose down projection writes its rows to `rows` (top_k 1, no
+// router weights, tensor-core shapes only; MSB_ERR_UNSUPPORTED otherwise,
+// before any launch).
+int moe_ffn_to_rows(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
+                    const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
+                    int32_t n_tok, const RowTarget &rows, void *workspace,
+                    int64_t workspace_bytes, void *stream);
+
 // msb_remap_group whose kernel first waits on `wait` (route.cu), and
 // msb_ep_combine likewise (ep.cu).
 int remap_group_wait(const int32_t *ids_dev, int64_t nb0, int64_t nb1, int32_t top_k,

@@ -159,19 +159,28 @@ class ExpertParallel:
         import torch.distributed as dist
         dist.all_to_all_single(out, inp, group=self.group)
 
-    def layer(self, x, ids, w, local_ffn, y):
+    def layer(self, x, ids, w, local_ffn, y, pools=None):
         """x: [t_loc, K] f32/bf16; ids: int32 [t_loc, top_k] global expert ids;
         w: f32 [t_loc, top_k]; y: f32 [t_loc, K] (written).
         local_ffn(x_rows [R, K], local_ids [R, 1], route, out [R, K]) runs this
         rank's experts over the received rows with top_k 1 and no weighting;
         `route` is those rows grouped by local slot (RouteBuffers) on GPUs,
-        None when dispatch and combine were passed in."""
+        None when dispatch and combine were passed in.
+        pools (peers transport): (gate, up, down, up_row0, workspace) of this
+        rank's experts; where the tensor cores take them, the down projection
+        returns its rows to their source ranks itself and local_ffn is not
+        called."""
         if self.transport == "peers":
             from . import ops
             ops.ep_dispatch_peers(self.peers, ids, x, self.n_local, self.pos)
             route = ops.ep_remap_group(self.peers, self.n_local, self.route)
-            local_ffn(self.recv_x(), self.recv_ids(), route, self.y_loc)
-            ops.ep_return_peers(self.peers, self.y_loc)
+            fused = False
+            if pools is not None:
+                gate, up, down, up_row0, ws = pools
+                fused = ops.ep_moe_ffn_peers(self.peers, gate, up, down, route, ws, up_row0)
+            if not fused:
+                local_ffn(self.recv_x(), self.recv_ids(), route, self.y_loc)
+                ops.ep_return_peers(self.peers, self.y_loc)
             ops.ep_combine_peers(self.peers, self.pos, w, y)
             return y
         self._dispatch(ids, x, self.n_local, self.world, self.cap, self.send[:, :self.K],

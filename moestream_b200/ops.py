@@ -218,6 +218,22 @@ def ep_remap_group(peers, n_slot, route, stream=None):
     return route
 
 
+ERR_UNSUPPORTED = 4
+
+
+def ep_moe_ffn_peers(peers, gate, up, down, route, ws, up_row0=0, stream=None):
+    """The local FFN over the received rows with the results stored straight
+    into their source ranks' buffers by the down projection. Returns False
+    (nothing launched) when the pools are not tensor-core shapes."""
+    rc = lib().msb_ep_moe_ffn_peers(ctypes.byref(peers), gate.handle, up.handle, up_row0,
+                                    down.handle, ctypes.byref(route.c), _ptr(ws), ws.numel(),
+                                    _stream(stream))
+    if rc == ERR_UNSUPPORTED:
+        return False
+    check(rc)
+    return True
+
+
 def ep_combine_peers(peers, pos, w, y, stream=None):
     """Waits (on the device, bounded) for every result, then
     y[t] = sum_k w[t, k] * (returned row of pair (t, k))."""

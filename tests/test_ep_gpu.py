@@ -5,8 +5,9 @@
 - The whole expert-parallel MoE layer (moestream_b200.ep, two ranks,
   tensor-core FFN on each) against the oracle's single-process layer, with
   the rows exchanged by NCCL all-to-all and by the NVLink peer-memory
-  kernels (run twice in a row, and from a replayed CUDA graph); needs two
-  GPUs and is skipped with fewer.
+  kernels, with the return separate or fused into the down projection (run
+  twice in a row, and from a replayed CUDA graph); needs two GPUs and is
+  skipped with fewer.
 """
 import datetime
 import os
@@ -86,7 +87,9 @@ def _rank_main(rank, world, port, transport, out_q):
                             timeout=datetime.timedelta(seconds=60))
     try:
         gate, up, down, x, ids, w = _layer_inputs()
-        ep = ExpertParallel(world, rank, N_EXPERT, N_TOK, TOP_K, K, "cuda", transport=transport)
+        fused = transport == "peers_fused"
+        ep = ExpertParallel(world, rank, N_EXPERT, N_TOK, TOP_K, K, "cuda",
+                            transport="peers" if fused else transport)
         mine = range(rank * ep.n_local, (rank + 1) * ep.n_local)
         pools = {}
         for role, mats, kk, nn in (("gate", gate, K, N_FF), ("up", up, K, N_FF),
@@ -95,20 +98,26 @@ def _rank_main(rank, world, port, transport, out_q):
             pools[role].fill(list(range(ep.n_local)),
                              [torch.from_numpy(mats[e]).pin_memory() for e in mine])
         def local_ffn(rows, local_ids, route, out):
+            assert not fused, "the fused path returns rows from the down projection"
             ops.moe_ffn(pools["gate"], pools["up"], pools["down"], rows, route, None, 1, out=out)
+
+        ffn_pools = None
+        if fused:
+            ws = ops.workspace(K, world * ep.cap, 1, ep.n_local)
+            ffn_pools = (pools["gate"], pools["up"], pools["down"], 0, ws)
 
         lo = rank * ep.t_loc
         xs = x[lo:lo + ep.t_loc].cuda()
         ids_d = torch.from_numpy(ids[lo:lo + ep.t_loc]).cuda()
         w_d = torch.from_numpy(w[lo:lo + ep.t_loc]).cuda()
         ys = [torch.empty(ep.t_loc, K, device="cuda") for _ in range(3)]
-        ep.layer(xs, ids_d, w_d, local_ffn, ys[0])
-        ep.layer(xs, ids_d, w_d, local_ffn, ys[1])
+        ep.layer(xs, ids_d, w_d, local_ffn, ys[0], pools=ffn_pools)
+        ep.layer(xs, ids_d, w_d, local_ffn, ys[1], pools=ffn_pools)
         graph = None
-        if transport == "peers":
+        if transport != "collective":
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                ep.layer(xs, ids_d, w_d, local_ffn, ys[2])
+                ep.layer(xs, ids_d, w_d, local_ffn, ys[2], pools=ffn_pools)
             graph.replay()
             graph.replay()
         else:
@@ -130,7 +139,7 @@ def _rank_main(rank, world, port, transport, out_q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("transport", ["collective", "peers"])
+@pytest.mark.parametrize("transport", ["collective", "peers", "peers_fused"])
 def test_two_rank_layer_matches_oracle(transport):
     world = 2
     ctx = mp.get_context("spawn")
