@@ -11,7 +11,7 @@
 // with its own power-of-two scale (a residual expansion: term t encodes what
 // terms 0..t-1 left over). Four terms are ~30x closer to exact than ggml's
 // int8 (q8_0) activations. The terms of a pass's 8 pairs are stacked along
-// the MMA's N (row t * 8 + p of B is term t of pair p, each row with its own
+// the MMA's N (row 4p + t of B is term t of pair p, each row with its own
 // block scales), so one M=128 N=32 K=64 MMA reads each weight tile from
 // shared memory once for all four terms; the epilogue adds the four f32
 // partial sums of a pair.
@@ -24,8 +24,9 @@
 //   warp 0, lane 0 : producer -- per stage, one tiled TMA copy per weight
 //                    view (128 rows x 4 blocks, 8 KB), one 512-byte bulk
 //                    copy of each view's scale-factor chunk, one tiled TMA
-//                    copy of the pass's activation terms (4 blocks x 4
-//                    terms x 8 pairs, 2 KB) and one of their scales (512 B),
+//                    copy of the pass's activation terms (4 blocks x 8
+//                    pairs x 4 terms: four 512-byte lines) and one of their
+//                    scales (one 512-byte line),
 //                    into a shared-memory ring;
 //   warp 1, lane 0 : copies each stage's scale factors into tensor memory
 //                    (tcgen05.cp) and issues the MMAs (one per view and
@@ -73,9 +74,9 @@ struct Cfg {
   static constexpr int kStages = G == 1 ? (NV == 2 ? 5 : 8) : (NV == 2 ? 7 : 5);
   static constexpr int kA = NV * kChunk * 2048;          // 128 rows x 16 B per block
   static constexpr int kSFA = NV * 512;
-  static constexpr int kBPass = kChunk * kN * 16;        // [block][term][pair] 16 B rows
+  static constexpr int kBPass = kChunk * kN * 16;        // [block][pair][term] 16 B rows
   static constexpr int kB = G * kBPass;
-  static constexpr int kSFB = G * 512;                   // per pass [term][pair] 16 B rows
+  static constexpr int kSFB = G * 512;                   // per pass [pair][term] 16 B rows
   static constexpr int kStage = kA + kSFA + kB + kSFB;
   static constexpr int kBarOff = kStages * kStage;
   static constexpr int kItemOff = kBarOff + 256;           // item prefix, kMaxActive + 1 ints
@@ -92,8 +93,8 @@ struct Cfg {
 
 struct Args {
   CUtensorMap tm_w[2];       // each view's pool: (8 B x 2 x rows, blocks, slots)
-  CUtensorMap tm_aq;         // activation terms: (8 B x 2 x pairs, terms, blocks)
-  CUtensorMap tm_asf;        // their scales: (8 B x 2 x pairs, terms, chunks)
+  CUtensorMap tm_aq;         // activation terms: (8 B x 8 x pairs, blocks, 1)
+  CUtensorMap tm_asf;        // their scales: (8 B x 8 x pairs, chunks, 1)
   const uint8_t *pool[2];    // slot 0 of each view's pool
   int64_t slot_stride[2], N[2];
   int64_t nb;                // blocks per row (K / 32), same for both views
@@ -122,11 +123,12 @@ constexpr int kStatusProducer = 1, kStatusAccEmpty = 2, kStatusFull = 4, kStatus
               kStatusDrain = 16;
 
 // Byte offset of the 16-byte record of (term t, block or chunk b, row r) in
-// an activation-term buffer of `rows` rows: [b][t][r][16 B]. The records of
+// an activation-term buffer of `rows` rows: [b][r][t][16 B]. The records of
 // one pass (8 consecutive rows, all terms) of one block are 512 contiguous
-// bytes: the stacked B operand of one MMA K-half, or its 32 scale rows.
+// bytes -- the stacked B operand of one MMA K-half (row 4p + t), or its 32
+// scale rows -- so the pass moves as one 512-byte line per block.
 __device__ __forceinline__ int64_t a4_off(int t, int64_t b, int64_t rows, int64_t r) {
-  return ((b * kTerms + t) * rows + r) * 16;
+  return ((b * rows + r) * kTerms + t) * 16;
 }
 
 // Splits the block held by the warp (lane j = element j) into kTerms e2m1
@@ -230,8 +232,8 @@ __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t n
     if constexpr (sizeof(T) == 4) r[e] = live ? float(x[el[e]]) : 0.f;
     else r[e] = live ? __bfloat162float(x[el[e]]) : 0.f;
   }
-  group_e2m1_terms(r, l, live, q + a4_off(0, blk, n_pairs, pos), n_pairs * 16,
-                   sf + a4_off(0, blk / 4, n_pairs, pos) + (blk & 3), n_pairs * 16);
+  group_e2m1_terms(r, l, live, q + a4_off(0, blk, n_pairs, pos), 16,
+                   sf + a4_off(0, blk / 4, n_pairs, pos) + (blk & 3), 16);
 }
 
 // Item w of the launch: its active-slot index (cursor, advanced
@@ -365,8 +367,8 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
           }
           for (int g = 0; g < n_real; ++g) {
             const int pos = int(pos0 + g * kPairs);
-            sm100::tma_3d(sB + g * C::kBPass, &a.tm_aq, pos * 2, 0, int(b0), &full[s]);
-            sm100::tma_3d(sSFB + g * 512, &a.tm_asf, pos * 2, 0, int(i), &full[s]);
+            sm100::tma_3d(sB + g * C::kBPass, &a.tm_aq, pos * 8, int(b0), 0, &full[s]);
+            sm100::tma_3d(sSFB + g * 512, &a.tm_asf, pos * 8, int(i), 0, &full[s]);
           }
         }
       }
@@ -506,20 +508,19 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
         for (int j = 0; j < kPairs; ++j) {
           if (j >= cc) break;
           const int64_t pair = a.rows[pos + j];
-          // Column t * 8 + j holds term t of pair j.
-          const float gv = (__uint_as_float(dg[j]) + __uint_as_float(dg[kPairs + j])) +
-                           (__uint_as_float(dg[2 * kPairs + j]) + __uint_as_float(dg[3 * kPairs + j]));
+          // Column 4j + t holds term t of pair j.
+          const float gv = (__uint_as_float(dg[4 * j]) + __uint_as_float(dg[4 * j + 1])) +
+                           (__uint_as_float(dg[4 * j + 2]) + __uint_as_float(dg[4 * j + 3]));
           if constexpr (NV == 1) {
             if (valid) out_row(a.out, pair)[n] = gv;
           } else {
-            const float u = (__uint_as_float(du[j]) + __uint_as_float(du[kPairs + j])) +
-                            (__uint_as_float(du[2 * kPairs + j]) + __uint_as_float(du[3 * kPairs + j]));
+            const float u = (__uint_as_float(du[4 * j]) + __uint_as_float(du[4 * j + 1])) +
+                            (__uint_as_float(du[4 * j + 2]) + __uint_as_float(du[4 * j + 3]));
             const float h = valid ? gv / (1.f + expf(-gv)) * u : 0.f;
             if (a.act && valid) a.act[pair * a.n_out + n] = h;
             if (blk < a.o_nb)
-              warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, pos + j), a.a_rows * 16,
-                              a.osf + a4_off(0, blk / 4, a.a_rows, pos + j) + (blk & 3),
-                              a.a_rows * 16);
+              warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, pos + j), 16,
+                              a.osf + a4_off(0, blk / 4, a.a_rows, pos + j) + (blk & 3), 16);
           }
         }
       }
@@ -649,17 +650,20 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   a.osf = act_out ? act_out + int64_t(tc::kTerms) * a.o_nb * n_pairs * 16 : nullptr;
   a.act = act_f32;
   {
-    // One 16-byte row per pair = two 8-byte elements; a box line is the 8
-    // pairs of one (block, term) -- 128 contiguous bytes. Boxes land as
-    // [block][term][pair] (terms) and [term][pair] (scales).
+    // A pair's four 16-byte term records of one block are 64 contiguous
+    // bytes (8 elements of 8 bytes); a box line is the 8 pairs of one pass
+    // and block -- 512 contiguous bytes. Boxes land as [block][pair][term]
+    // (terms) and [pair][term] (scales): B rows 4p + t.
     const uint64_t nc = uint64_t((pool->nb + 3) / 4);
-    const uint64_t dq[3] = {uint64_t(n_pairs) * 2, uint64_t(tc::kTerms), uint64_t(pool->nb)};
-    const uint64_t sq[2] = {uint64_t(n_pairs) * 16, uint64_t(tc::kTerms * n_pairs) * 16};
-    const uint32_t bq[3] = {uint32_t(tc::kPairs) * 2, uint32_t(tc::kTerms), uint32_t(tc::kChunk)};
-    const uint64_t df[3] = {uint64_t(n_pairs) * 2, uint64_t(tc::kTerms), nc};
-    const uint32_t bf[3] = {uint32_t(tc::kPairs) * 2, uint32_t(tc::kTerms), 1};
+    const uint64_t row_u64 = uint64_t(n_pairs) * tc::kTerms * 2;
+    const uint64_t dq[3] = {row_u64, uint64_t(pool->nb), 1};
+    const uint64_t sq[2] = {row_u64 * 8, row_u64 * 8 * uint64_t(pool->nb)};
+    const uint32_t bq[3] = {uint32_t(tc::kPairs * tc::kTerms * 2), uint32_t(tc::kChunk), 1};
+    const uint64_t df[3] = {row_u64, nc, 1};
+    const uint64_t sf[2] = {row_u64 * 8, row_u64 * 8 * nc};
+    const uint32_t bf[3] = {uint32_t(tc::kPairs * tc::kTerms * 2), 1, 1};
     if (!encode_tmap_u64_3d(&a.tm_aq, a.aq, dq, sq, bq) ||
-        !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sq, bf))
+        !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sf, bf))
       return fail(MSB_ERR_CUDA, "tensor-core path: activation tensor maps could not be encoded");
   }
   return nv == 2 ? launch_tc_t<2, 1>(a, max_active, n_pairs, st)
