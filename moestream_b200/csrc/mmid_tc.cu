@@ -16,7 +16,7 @@
 // shared memory once for all four terms; the epilogue adds the four f32
 // partial sums of a pair.
 //
-// Persistent CTAs (two per SM, 192 threads) walk the work items (active
+// Persistent CTAs (two per SM, 224 threads) walk the work items (active
 // slot x 128-row tile) with a stride of the grid; each item runs in passes of
 // 8 of the slot's (token, k) pairs. The pipeline never drains between
 // items: the producer streams the next item's tiles while the accumulators
@@ -28,11 +28,13 @@
 //                    pairs x 4 terms: four 512-byte lines) and one of their
 //                    scales (one 512-byte line),
 //                    into a shared-memory ring;
-//   warp 1, lane 0 : copies each stage's scale factors into tensor memory
-//                    (tcgen05.cp) and issues the MMAs (one per view and
-//                    K=64 step) into one of two accumulator buffers;
-//                    tcgen05.commit frees the stage / hands over a buffer;
-//   warps 2-5      : epilogue -- warp w reads TMEM lanes 32*(w%4)..+31
+//   warps 1-2, lane 0 : copy the stage's scale factors into tensor memory
+//                    (tcgen05.cp) and issue the MMAs (one per K=64 step)
+//                    into one of two accumulator buffers -- with two views
+//                    each warp takes one, with one view they take alternate
+//                    stages into two accumulators; tcgen05.commit frees the
+//                    stage / hands over a buffer;
+//   warps 3-6      : epilogue -- warp w reads TMEM lanes 32*(w%4)..+31
 //                    (rows), releases the buffer, then stores.
 // With two views (gate and up) the epilogue applies SwiGLU and writes the
 // down projection's activation terms directly.
@@ -57,7 +59,7 @@ constexpr int kTerms = 4;        // e2m1 terms per activation block
 constexpr int kPairs = 8;        // (token, k) pairs per pass
 constexpr int kN = kTerms * kPairs;   // MMA N: the pass's terms stacked
 constexpr int kChunk = 4;        // 32-element blocks per stage (two K=64 MMAs)
-constexpr int kThreads = 192;    // producer warp, MMA warp, 4 epilogue warps
+constexpr int kThreads = 224;    // producer warp, 2 MMA warps, 4 epilogue warps
 constexpr int kMaxActive = 1024; // slots (with the zero slot) one launch can walk
 
 // Shapes of one launch: NV weight views (2: gate and up) and G passes of
@@ -81,8 +83,11 @@ struct Cfg {
   static constexpr int kBarOff = kStages * kStage;
   static constexpr int kItemOff = kBarOff + 256;           // item prefix, kMaxActive + 1 ints
   static constexpr int kSmem = kItemOff + (kMaxActive + 1) * 4;
-  static constexpr int kAccCols = G * NV * kN;           // one accumulator buffer
-  static constexpr int kSfCols = (NV + G) * 4;           // TMEM columns per stage
+  // One accumulator buffer: two N=32 accumulators, one per MMA warp (gate
+  // and up, or the down projection's even and odd stages).
+  static constexpr int kAccCols = 2 * kN;
+  // TMEM columns per stage: each MMA warp's scale factors (A then B).
+  static constexpr int kSfCols = NV == 2 ? 16 : 8;
   static constexpr int kTmemCols = kCtasPerSm == 1 ? 512 : 256;
   static constexpr int kAccBufs = 2 * kAccCols + kStages * kSfCols <= kTmemCols ? 2 : 1;
   static constexpr int kSfBase = kAccBufs * kAccCols;    // after the buffers
@@ -277,13 +282,13 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       sm100::mbar_init(&full[s], 1);
-      sm100::mbar_init(&empty[s], 1);
+      sm100::mbar_init(&empty[s], NV == 2 ? 2 : 1);   // the stage's MMA warps
     }
     for (int b = 0; b < 2; ++b) {
-      sm100::mbar_init(&acc_full[b], 1);
+      sm100::mbar_init(&acc_full[b], 2);
       sm100::mbar_init(&acc_empty[b], 4);
     }
-    sm100::mbar_init(drained, 1);
+    sm100::mbar_init(drained, 2);
     *abort_flag = 0;
     sm100::fence_mbar_init();
   }
@@ -378,15 +383,20 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
         if (!sm100::mbar_wait_bounded(&full[k % kStages], (k / kStages) & 1))
           atomicOr(&g_status, kStatusDrain);
     }
-  } else if (warp == 1) {
-    // ---- scale-factor copies and MMA issue ----
+  } else if (warp <= 2) {
+    // ---- scale-factor copies and MMA issue (warps 1 and 2) ----
+    // One thread issuing every tcgen05 copy and MMA caps a CTA at ~26 GB/s
+    // (about 0.4 us per stage), so two warps issue: with two views each
+    // takes one (gate, up); with one view they take alternate stages into
+    // two accumulators that the epilogue adds.
+    static_assert(G == 1, "one pass per work item");
+    const int m = warp - 1;
     if (lane == 0) {
       uint32_t it = 0, acc = 0;
       int cur = 0;
       for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
         const Item item = locate(a, item0, w, cur);
         if (item.slot == a.zero_slot) continue;
-        const int n_real = passes_in_group<G>(a.counts[item.slot], item.group);
         const int buf = acc % kBufs;
         if (!sm100::mbar_wait_bounded(&acc_empty[buf], ((acc / kBufs) & 1) ^ 1)) {
           atomicOr(&g_status, kStatusAccEmpty);
@@ -394,8 +404,11 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
           break;
         }
         sm100::tc_fence_after();
-        const uint32_t d0 = tmem + buf * C::kAccCols;
+        const uint32_t d0 = tmem + buf * C::kAccCols + m * kN;
+        const int v = NV == 2 ? m : 0;
+        bool first = true;
         for (int64_t i = 0; i < n_chunks; ++i, ++it) {
+          if (NV == 1 && (i & 1) != m) continue;   // the other warp's stage
           const int s = it % kStages;
           if (!sm100::mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
             atomicOr(&g_status, kStatusFull);
@@ -404,30 +417,24 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
           }
           const uint8_t *st = smem + s * C::kStage;
           const uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
-          const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols;
-          for (int v = 0; v < NV; ++v)
-            sm100::tmem_cp_32x128b_x4(sf_col + v * 4,
-                                      sm100::smem_desc(sm100::smem_u32(sSFA + v * 512), 0, 128));
-          for (int g = 0; g < n_real; ++g)
-            sm100::tmem_cp_32x128b_x4(
-                sf_col + (NV + g) * 4, sm100::smem_desc(sm100::smem_u32(sSFB + g * 512), 0, 128));
+          const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols + (NV == 2 ? m * 8 : 0);
+          sm100::tmem_cp_32x128b_x4(sf_col,
+                                    sm100::smem_desc(sm100::smem_u32(sSFA + v * 512), 0, 128));
+          sm100::tmem_cp_32x128b_x4(sf_col + 4,
+                                    sm100::smem_desc(sm100::smem_u32(sSFB), 0, 128));
           const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
           for (int j = 0; j < kbn / 2; ++j) {
             const uint32_t sel = uint32_t(2 * j);
-            for (int g = 0; g < n_real; ++g) {
-              // B: 32 stacked rows of 16 B per block; K-halves one block apart.
-              const uint64_t bdesc = sm100::smem_desc(
-                  sm100::smem_u32(sB + g * C::kBPass + 2 * j * (kN * 16)), kN * 16, 128);
-              for (int v = 0; v < NV; ++v) {
-                const uint64_t adesc = sm100::smem_desc(
-                    sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
-                sm100::mma_mxf4(d0 + (g * NV + v) * kN, adesc, bdesc,
-                                sm100::idesc_mxf4(kN, sel, sel), (sf_col + v * 4) | (sel << 30),
-                                (sf_col + (NV + g) * 4) | (sel << 30),
-                                (i == 0 && j == 0) ? 0u : 1u);
-              }
-            }
+            // B: 32 stacked rows of 16 B per block; K-halves one block apart.
+            const uint64_t bdesc =
+                sm100::smem_desc(sm100::smem_u32(sB + 2 * j * (kN * 16)), kN * 16, 128);
+            const uint64_t adesc =
+                sm100::smem_desc(sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
+            sm100::mma_mxf4(d0, adesc, bdesc, sm100::idesc_mxf4(kN, sel, sel),
+                            sf_col | (sel << 30), (sf_col + 4) | (sel << 30),
+                            (first && j == 0) ? 0u : 1u);
           }
+          first = false;
           sm100::tc_commit(&empty[s]);
         }
         sm100::tc_commit(&acc_full[buf]);
@@ -439,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
       if (!sm100::mbar_wait_bounded(drained, 0)) atomicOr(&g_status, kStatusDrain);
     }
   } else {
-    // ---- epilogue (warps 2-5) ----
+    // ---- epilogue (warps 3-6) ----
     const int quad = warp & 3;            // TMEM lane quadrant of this warp
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     uint32_t acc = 0;
@@ -490,11 +497,19 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
         const int g0 = (item.group * G + g) * kPairs;
         const int cc = min(kPairs, c_total - g0);
         const int64_t pos = pos0 + g0;
-        const uint32_t col = tmem + lane_addr + buf * C::kAccCols + g * NV * kN;
+        const uint32_t col = tmem + lane_addr + buf * C::kAccCols;
         uint32_t dg[32], du[32];
         sm100::tmem_ld_32cols(col, dg);
-        if constexpr (NV == 2) sm100::tmem_ld_32cols(col + kN, du);
+        if (NV == 2 || n_chunks > 1) sm100::tmem_ld_32cols(col + kN, du);
         sm100::tmem_ld_wait();
+        if constexpr (NV == 1) {
+          // Even and odd stages' accumulators, added in that order.
+          if (n_chunks > 1) {
+#pragma unroll
+            for (int c = 0; c < kN; ++c)
+              dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
+          }
+        }
         if (g == n_real - 1) {
           // Every accumulator of the item is in registers: release the buffer.
           sm100::tc_fence_before();
