@@ -16,7 +16,7 @@
 // shared memory once for all four terms; the epilogue adds the four f32
 // partial sums of a pair.
 //
-// Persistent CTAs (two per SM, 224 threads) walk the work items (active
+// Persistent CTAs (two per SM, 256 threads) walk the work items (active
 // slot x 128-row tile) with a stride of the grid; each item runs in passes of
 // 8 of the slot's (token, k) pairs. The pipeline never drains between
 // items: the producer streams the next item's tiles while the accumulators
@@ -28,13 +28,13 @@
 //                    pairs x 4 terms: four 512-byte lines) and one of their
 //                    scales (one 512-byte line),
 //                    into a shared-memory ring;
-//   warps 1-2, lane 0 : copy the stage's scale factors into tensor memory
+//   warps 1-3, lane 0 : copy the stage's scale factors into tensor memory
 //                    (tcgen05.cp) and issue the MMAs (one per K=64 step)
 //                    into one of two accumulator buffers -- with two views
-//                    each warp takes one, with one view they take alternate
-//                    stages into two accumulators; tcgen05.commit frees the
-//                    stage / hands over a buffer;
-//   warps 3-6      : epilogue -- warp w reads TMEM lanes 32*(w%4)..+31
+//                    warps 1-2 take one each, with one view warps 1-3 take
+//                    the stages in turn, each into its own accumulator;
+//                    tcgen05.commit frees the stage / hands over a buffer;
+//   warps 4-7      : epilogue -- warp w reads TMEM lanes 32*(w%4)..+31
 //                    (rows), releases the buffer, then stores.
 // With two views (gate and up) the epilogue applies SwiGLU and writes the
 // down projection's activation terms directly.
@@ -59,7 +59,7 @@ constexpr int kTerms = 4;        // e2m1 terms per activation block
 constexpr int kPairs = 8;        // (token, k) pairs per pass
 constexpr int kN = kTerms * kPairs;   // MMA N: the pass's terms stacked
 constexpr int kChunk = 4;        // 32-element blocks per stage (two K=64 MMAs)
-constexpr int kThreads = 224;    // producer warp, 2 MMA warps, 4 epilogue warps
+constexpr int kThreads = 256;    // producer warp, 3 MMA warps, 4 epilogue warps
 constexpr int kMaxActive = 1024; // slots (with the zero slot) one launch can walk
 
 // Shapes of one launch: NV weight views (2: gate and up) and G passes of
@@ -83,9 +83,11 @@ struct Cfg {
   static constexpr int kBarOff = kStages * kStage;
   static constexpr int kItemOff = kBarOff + 256;           // item prefix, kMaxActive + 1 ints
   static constexpr int kSmem = kItemOff + (kMaxActive + 1) * 4;
-  // One accumulator buffer: two N=32 accumulators, one per MMA warp (gate
-  // and up, or the down projection's even and odd stages).
-  static constexpr int kAccCols = 2 * kN;
+  // MMA-issuing warps: one per view (gate and up), or three taking turns
+  // over the stages of a single view. One accumulator buffer holds one N=32
+  // accumulator per MMA warp.
+  static constexpr int kMma = NV == 2 ? 2 : 3;
+  static constexpr int kAccCols = kMma * kN;
   // TMEM columns per stage: each MMA warp's scale factors (A then B).
   static constexpr int kSfCols = NV == 2 ? 16 : 8;
   static constexpr int kTmemCols = kCtasPerSm == 1 ? 512 : 256;
@@ -285,10 +287,10 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
       sm100::mbar_init(&empty[s], NV == 2 ? 2 : 1);   // the stage's MMA warps
     }
     for (int b = 0; b < 2; ++b) {
-      sm100::mbar_init(&acc_full[b], 2);
+      sm100::mbar_init(&acc_full[b], C::kMma);
       sm100::mbar_init(&acc_empty[b], 4);
     }
-    sm100::mbar_init(drained, 2);
+    sm100::mbar_init(drained, C::kMma);
     *abort_flag = 0;
     sm100::fence_mbar_init();
   }
@@ -383,15 +385,15 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
         if (!sm100::mbar_wait_bounded(&full[k % kStages], (k / kStages) & 1))
           atomicOr(&g_status, kStatusDrain);
     }
-  } else if (warp <= 2) {
-    // ---- scale-factor copies and MMA issue (warps 1 and 2) ----
+  } else if (warp <= 3) {
+    // ---- scale-factor copies and MMA issue (warps 1-3) ----
     // One thread issuing every tcgen05 copy and MMA caps a CTA at ~26 GB/s
-    // (about 0.4 us per stage), so two warps issue: with two views each
-    // takes one (gate, up); with one view they take alternate stages into
-    // two accumulators that the epilogue adds.
+    // (about 0.4 us per stage), so several warps issue: with two views each
+    // of warps 1-2 takes one (gate, up); with one view warps 1-3 take the
+    // stages in turn, each into its own accumulator, added by the epilogue.
     static_assert(G == 1, "one pass per work item");
     const int m = warp - 1;
-    if (lane == 0) {
+    if (lane == 0 && m < C::kMma) {
       uint32_t it = 0, acc = 0;
       int cur = 0;
       for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
@@ -408,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
         const int v = NV == 2 ? m : 0;
         bool first = true;
         for (int64_t i = 0; i < n_chunks; ++i, ++it) {
-          if (NV == 1 && (i & 1) != m) continue;   // the other warp's stage
+          if (NV == 1 && i % C::kMma != m) continue;   // another warp's stage
           const int s = it % kStages;
           if (!sm100::mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
             atomicOr(&g_status, kStatusFull);
@@ -446,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
       if (!sm100::mbar_wait_bounded(drained, 0)) atomicOr(&g_status, kStatusDrain);
     }
   } else {
-    // ---- epilogue (warps 3-6) ----
+    // ---- epilogue (warps 4-7) ----
     const int quad = warp & 3;            // TMEM lane quadrant of this warp
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     uint32_t acc = 0;
@@ -503,8 +505,16 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
         if (NV == 2 || n_chunks > 1) sm100::tmem_ld_32cols(col + kN, du);
         sm100::tmem_ld_wait();
         if constexpr (NV == 1) {
-          // Even and odd stages' accumulators, added in that order.
+          // The MMA warps' accumulators (stages i % 3 = 0, 1, 2), added in
+          // that order; a warp that had no stage holds nothing.
           if (n_chunks > 1) {
+#pragma unroll
+            for (int c = 0; c < kN; ++c)
+              dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
+          }
+          if (n_chunks > 2) {
+            sm100::tmem_ld_32cols(col + 2 * kN, du);
+            sm100::tmem_ld_wait();
 #pragma unroll
             for (int c = 0; c < kN; ++c)
               dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
