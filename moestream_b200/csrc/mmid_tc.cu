@@ -62,23 +62,21 @@ constexpr int kChunk = 4;        // 32-element blocks per stage (two K=64 MMAs)
 constexpr int kThreads = 256;    // producer warp, 3 MMA warps, 4 epilogue warps
 constexpr int kMaxActive = 1024; // slots (with the zero slot) one launch can walk
 
-// Shapes of one launch: NV weight views (2: gate and up) and G passes of
-// kPairs pairs per work item; one weight tile in shared memory feeds G
-// accumulators. Only G = 1 is launched: with G = 4 (one CTA per SM for
-// gate/up, single-buffered accumulators) a 2048-token layer ran 1.4x slower
-// than one pass per item, the epilogue of four passes serializing with the
-// MMAs.
-template <int NV, int G>
+// Shapes of one launch with NV weight views (2: gate and up); a work item
+// is one pass of up to kPairs pairs over one 128-row weight tile. (Feeding
+// four passes' accumulators from one staged tile -- one CTA per SM,
+// single-buffered tensor memory -- ran a 2048-token layer 1.4x slower: the
+// four passes' epilogue serialized with the MMAs.)
+template <int NV>
 struct Cfg {
-  // Decode (G = 1): two CTAs per SM, double-buffered accumulators. With
-  // G = 4 gate/up takes the whole SM (all 512 TMEM columns); down two.
-  static constexpr int kCtasPerSm = (NV == 2 && G > 1) ? 1 : 2;
-  static constexpr int kStages = G == 1 ? (NV == 2 ? 5 : 8) : (NV == 2 ? 7 : 5);
+  // Two CTAs per SM, double-buffered accumulators.
+  static constexpr int kCtasPerSm = 2;
+  static constexpr int kStages = NV == 2 ? 5 : 8;
   static constexpr int kA = NV * kChunk * 2048;          // 128 rows x 16 B per block
   static constexpr int kSFA = NV * 512;
   static constexpr int kBPass = kChunk * kN * 16;        // [block][pair][term] 16 B rows
-  static constexpr int kB = G * kBPass;
-  static constexpr int kSFB = G * 512;                   // per pass [pair][term] 16 B rows
+  static constexpr int kB = kBPass;
+  static constexpr int kSFB = 512;                       // [pair][term] 16 B rows
   static constexpr int kStage = kA + kSFA + kB + kSFB;
   static constexpr int kBarOff = kStages * kStage;
   static constexpr int kItemOff = kBarOff + 256;           // item prefix, kMaxActive + 1 ints
@@ -90,7 +88,7 @@ struct Cfg {
   static constexpr int kAccCols = kMma * kN;
   // TMEM columns per stage: each MMA warp's scale factors (A then B).
   static constexpr int kSfCols = NV == 2 ? 16 : 8;
-  static constexpr int kTmemCols = kCtasPerSm == 1 ? 512 : 256;
+  static constexpr int kTmemCols = 256;
   static constexpr int kAccBufs = 2 * kAccCols + kStages * kSfCols <= kTmemCols ? 2 : 1;
   static constexpr int kSfBase = kAccBufs * kAccCols;    // after the buffers
   static_assert(kSfBase + kStages * kSfCols <= kTmemCols, "tensor memory map");
@@ -244,30 +242,22 @@ __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t n
 }
 
 // Item w of the launch: its active-slot index (cursor, advanced
-// monotonically as w grows), slot, pass group and tile.
+// monotonically as w grows), slot, pass and tile.
 struct Item {
-  int slot, group;
+  int slot, pass;
   int64_t n0;
 };
 __device__ __forceinline__ Item locate(const Args &a, const int *item0, int64_t w, int &cur) {
   while (item0[cur + 1] <= w) ++cur;
   const int slot = a.active[1 + cur];
   const int64_t local = w - item0[cur];
-  const int64_t groups = (item0[cur + 1] - item0[cur]) / a.tiles;
-  return Item{slot, int(local % groups), (local / groups) * 128};
+  const int64_t passes = (item0[cur + 1] - item0[cur]) / a.tiles;
+  return Item{slot, int(local % passes), (local / passes) * 128};
 }
 
-// Passes of kPairs pairs in item group `group` of a slot with c pairs.
-template <int G>
-__device__ __forceinline__ int passes_in_group(int c, int group) {
-  const int left = (c + kPairs - 1) / kPairs - group * G;
-  return left < G ? left : G;
-}
-
-template <int NV, int G>
-__global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
-    tc_kernel(const __grid_constant__ Args a) {
-  using C = Cfg<NV, G>;
+template <int NV>
+__global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__ Args a) {
+  using C = Cfg<NV>;
   constexpr int kStages = C::kStages;
   constexpr int kBufs = C::kAccBufs;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -307,17 +297,17 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
   // activation terms are read only after it completed.
   pdl_wait();
   pdl_trigger();
-  // Work items: (active slot, 128-row tile, group of up to G passes of
-  // kPairs pairs), the groups of one tile adjacent so that CTAs running them
-  // at the same time share the tile's weights through L2. item0[i] = first
-  // item of active slot i (the zero slot has one item per tile: its
-  // epilogue writes every pair's zeros).
+  // Work items: (active slot, 128-row tile, pass of up to kPairs pairs), the
+  // passes of one tile adjacent so that CTAs running them at the same time
+  // share the tile's weights through L2. item0[i] = first item of active
+  // slot i (the zero slot has one item per tile: its epilogue writes every
+  // pair's zeros).
   int *item0 = reinterpret_cast<int *>(smem + C::kItemOff);
   const int n_active = a.active[0];
   for (int i = threadIdx.x; i < n_active; i += kThreads) {
     const int slot = a.active[1 + i];
     const int passes = slot == a.zero_slot ? 1 : (a.counts[slot] + kPairs - 1) / kPairs;
-    item0[i + 1] = (passes + G - 1) / G * a.tiles;
+    item0[i + 1] = passes * a.tiles;
   }
   __syncthreads();
   if (warp == 0) {
@@ -346,8 +336,7 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
         const Item item = locate(a, item0, w, cur);
         const int slot = item.slot;
         if (slot == a.zero_slot) continue;
-        const int n_real = passes_in_group<G>(a.counts[slot], item.group);
-        const int64_t pos0 = a.offsets[slot] + int64_t(item.group) * G * kPairs;
+        const int pos = int(a.offsets[slot] + int64_t(item.pass) * kPairs);
         for (int64_t i = 0; i < n_chunks; ++i, ++it) {
           const int s = it % kStages;
           if (!sm100::mbar_wait_bounded(&empty[s], ((it / kStages) & 1) ^ 1)) {
@@ -359,9 +348,8 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
           uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
           const int64_t b0 = i * kChunk;
           // Full boxes are counted (rows or blocks outside the tensors
-          // arrive as zeros); passes past the slot's pairs are not loaded.
-          sm100::mbar_expect_tx(&full[s],
-                                uint32_t(C::kStage - (G - n_real) * (C::kBPass + 512)));
+          // arrive as zeros).
+          sm100::mbar_expect_tx(&full[s], uint32_t(C::kStage));
           for (int v = 0; v < NV; ++v) {
             const int64_t r0 = a.row0[v] + item.n0;
             sm100::tma_3d(sA + v * kChunk * 2048, &a.tm_w[v], int(r0) * 2, int(b0), slot,
@@ -372,11 +360,8 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
             sm100::bulk_g2s(sSFA + v * 512, sf_base + (i * sf_tiles + (r0 >> 7)) * 512, 512,
                             &full[s]);
           }
-          for (int g = 0; g < n_real; ++g) {
-            const int pos = int(pos0 + g * kPairs);
-            sm100::tma_3d(sB + g * C::kBPass, &a.tm_aq, pos * 8, int(b0), 0, &full[s]);
-            sm100::tma_3d(sSFB + g * 512, &a.tm_asf, pos * 8, int(i), 0, &full[s]);
-          }
+          sm100::tma_3d(sB, &a.tm_aq, pos * 8, int(b0), 0, &full[s]);
+          sm100::tma_3d(sSFB, &a.tm_asf, pos * 8, int(i), 0, &full[s]);
         }
       }
       // No copy may still be landing in shared memory when the CTA exits
@@ -391,7 +376,6 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
     // (about 0.4 us per stage), so several warps issue: with two views each
     // of warps 1-2 takes one (gate, up); with one view warps 1-3 take the
     // stages in turn, each into its own accumulator, added by the epilogue.
-    static_assert(G == 1, "one pass per work item");
     const int m = warp - 1;
     if (lane == 0 && m < C::kMma) {
       uint32_t it = 0, acc = 0;
@@ -486,7 +470,6 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
         }
         continue;
       }
-      const int n_real = passes_in_group<G>(c_total, item.group);
       const uint32_t a_i = acc++;
       const int buf = a_i % kBufs;
       if (!sm100::mbar_wait_bounded(&acc_full[buf], (a_i / kBufs) & 1)) {
@@ -495,8 +478,8 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
         break;
       }
       sm100::tc_fence_after();
-      for (int g = 0; g < n_real; ++g) {
-        const int g0 = (item.group * G + g) * kPairs;
+      {
+        const int g0 = item.pass * kPairs;
         const int cc = min(kPairs, c_total - g0);
         const int64_t pos = pos0 + g0;
         const uint32_t col = tmem + lane_addr + buf * C::kAccCols;
@@ -520,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, (Cfg<NV, G>::kCtasPerSm))
               dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
           }
         }
-        if (g == n_real - 1) {
+        {
           // Every accumulator of the item is in registers: release the buffer.
           sm100::tc_fence_before();
           __syncwarp();
@@ -605,25 +588,25 @@ int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb
   return MSB_OK;
 }
 
-template <int NV, int G>
+template <int NV>
 static int launch_tc_t(const tc::Args &a, int max_active, int64_t n_pairs, cudaStream_t st) {
-  using C = tc::Cfg<NV, G>;
-  MSB_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<NV, G>,
+  using C = tc::Cfg<NV>;
+  MSB_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<NV>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
   // Persistent grid: as many CTAs as fit (shared and tensor memory), never
   // more than the work items the route can produce (each active slot has at
-  // most ceil(pairs / (kPairs * G)) + 1 groups per tile).
+  // most ceil(pairs / kPairs) + 1 passes per tile).
   static int n_sm = 0;
   if (!n_sm) {
     int dev = 0;
     MSB_CUDA_TRY(cudaGetDevice(&dev));
     MSB_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
   }
-  const int64_t groups = int64_t(max_active) + n_pairs / (int64_t(tc::kPairs) * G) + 1;
-  int64_t grid = groups * a.tiles;
+  const int64_t passes = int64_t(max_active) + n_pairs / tc::kPairs + 1;
+  int64_t grid = passes * a.tiles;
   if (grid > int64_t(C::kCtasPerSm) * n_sm) grid = int64_t(C::kCtasPerSm) * n_sm;
   if (grid == 0) return MSB_OK;
-  MSB_CUDA_TRY(launch_pdl(tc::tc_kernel<NV, G>, dim3(unsigned(grid)), dim3(tc::kThreads), C::kSmem,
+  MSB_CUDA_TRY(launch_pdl(tc::tc_kernel<NV>, dim3(unsigned(grid)), dim3(tc::kThreads), C::kSmem,
                           st, a));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
@@ -691,8 +674,8 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
         !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sf, bf))
       return fail(MSB_ERR_CUDA, "tensor-core path: activation tensor maps could not be encoded");
   }
-  return nv == 2 ? launch_tc_t<2, 1>(a, max_active, n_pairs, st)
-                 : launch_tc_t<1, 1>(a, max_active, n_pairs, st);
+  return nv == 2 ? launch_tc_t<2>(a, max_active, n_pairs, st)
+                 : launch_tc_t<1>(a, max_active, n_pairs, st);
 }
 
 }  // namespace msb
