@@ -41,6 +41,7 @@ extern "C" {
 #define MSB_ERR_NOMEM        3   /* device or pinned host allocation failed    */
 #define MSB_ERR_UNSUPPORTED  4   /* valid request this build does not handle   */
 #define MSB_ERR_TIMEOUT      5   /* a bounded device wait gave up              */
+#define MSB_ERR_IO           6   /* a file could not be opened or read         */
 
 /* ---- element types (values are ggml's enum ggml_type) ------------------ */
 #define MSB_TYPE_F32     0
@@ -450,6 +451,71 @@ int msb_streamer_remap(msb_streamer_t s, uint32_t layer, const int32_t *ids,
 /* Summed stats over the layers plus the exhaustion count. */
 int msb_streamer_stats(msb_streamer_t s, msb_cache_stats_t *out,
                        uint64_t *n_exhausted);
+
+/* ======================================================================== */
+/* GGUF expert source: slot fills read straight from the model file          */
+/* ======================================================================== */
+
+/* The reference reads expert bytes out of the GGUF the model came from
+ * (src/llama-moestream.cpp:1230-1263 do_read / run_reads_parallel), opening
+ * every shard of a split file "<base>-NNNNN-of-MMMMM.gguf" (:571-598,
+ * :1455-1466), reading metadata integers by key suffix (:601-693) and
+ * checking every expert tensor against its shard's size (:1478-1506). This
+ * library parses the GGUF itself (format versions 2 and 3, little-endian). */
+typedef struct msb_gguf_s *msb_gguf_t;
+
+typedef struct {
+  const char *name;     /* owned by the handle                               */
+  int      type;        /* ggml type id                                      */
+  int      n_dims;      /* 1..4                                              */
+  int64_t  ne[4];       /* ne[0] fastest; unused dimensions are 1            */
+  int32_t  shard;       /* file of a split GGUF (0-based)                    */
+  uint64_t offset;      /* absolute byte offset of the data in that file     */
+  int64_t  nbytes;      /* bytes of the whole tensor                         */
+} msb_gguf_tensor_t;
+
+/* Opens a GGUF (any shard's name of a split one opens all shards), parses
+ * every header and checks that each tensor lies inside its file. Fails with
+ * MSB_ERR_IO when a shard is missing, MSB_ERR_INVALID on a malformed header
+ * or a tensor past the end of its file, MSB_ERR_UNSUPPORTED on another
+ * format version or an unknown tensor type. A handle is not thread-safe. */
+int msb_gguf_open(const char *path, msb_gguf_t *out);
+/* Waits for the handle's staged copies, closes the files, frees it. */
+int msb_gguf_close(msb_gguf_t g);
+int32_t msb_gguf_shard_count(msb_gguf_t g);
+int64_t msb_gguf_tensor_count(msb_gguf_t g);
+int msb_gguf_tensor_info(msb_gguf_t g, int64_t index, msb_gguf_tensor_t *out);
+/* Index of the tensor with this name, -1 if absent. */
+int64_t msb_gguf_find_tensor(msb_gguf_t g, const char *name);
+/* Index of "blk.<layer>.ffn_{gate,up,down}_exps.weight" (role MSB_ROLE_*),
+ * a 3-D tensor [K, N, n_expert]; -1 if absent. The reference's expert
+ * tensor naming (src/llama-moestream.cpp:434-445 parse_name). */
+int64_t msb_gguf_expert_tensor(msb_gguf_t g, int32_t layer, int role);
+/* First integer key of the first shard whose name ends in key_suffix (e.g.
+ * ".expert_used_count", ".block_count", ".expert_count"); MSB_ERR_INVALID
+ * when there is none. Replaces gguf_kv_int (src/llama-moestream.cpp:610-693). */
+int msb_gguf_kv_int(msb_gguf_t g, const char *key_suffix, int64_t *value);
+/* Bytes of one expert per layer and role summed over every expert tensor
+ * with more than one expert: the cost of one slot across the model
+ * (gguf_bytes_per_slot, src/llama-moestream.cpp:771-830). */
+uint64_t msb_gguf_bytes_per_slot(msb_gguf_t g);
+/* Reads experts[i] (ggml block layout, nbytes / ne[2] bytes each) of 3-D
+ * tensor `tensor` into host memory dst_host[i], with up to n_threads
+ * threads taking experts in turn. Synchronous; MSB_ERR_IO on a short read. */
+int msb_gguf_read_experts(msb_gguf_t g, int64_t tensor, int32_t n,
+                          const int32_t *experts, void *const *dst_host,
+                          int32_t n_threads);
+/* Reads experts[i] into pinned host memory owned by the handle and fills
+ * slots[i] of `pool` from it (msb_fill_slots_async), stream-ordered on
+ * `stream`. The tensor's type, K and N must be the pool's. The reads are
+ * synchronous; the copies are not. Two staging halves are used in turn:
+ * a call waits only for the copies of the call before the previous one.
+ * Replaces the read-and-upload of ms_remap_fn
+ * (src/llama-moestream.cpp:1954-2028). */
+int msb_gguf_fill_slots_async(msb_gguf_t g, int64_t tensor, msb_pool_t pool,
+                              int32_t n, const int32_t *experts,
+                              const int32_t *slots, int32_t n_threads,
+                              void *stream);
 
 #ifdef __cplusplus
 }

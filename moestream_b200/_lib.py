@@ -45,6 +45,12 @@ class EpPeers(ctypes.Structure):
                 ("K", ctypes.c_int64), ("peer", c_vp * EP_MAX_RANKS)]
 
 
+class GgufTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_int), ("n_dims", ctypes.c_int),
+                ("ne", ctypes.c_int64 * 4), ("shard", ctypes.c_int32), ("offset", ctypes.c_uint64),
+                ("nbytes", ctypes.c_int64)]
+
+
 class Route(ctypes.Structure):
     _fields_ = [("slot_ids", c_vp), ("counts", c_vp), ("offsets", c_vp),
                 ("rows", c_vp), ("active", c_vp)]
@@ -150,6 +156,19 @@ SIGNATURES = {
                                           ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, c_i32p,
                                           c_i32p, c_i32p, c_i32p, c_i32p]),
     "msb_streamer_stats": (ctypes.c_int, [c_vp, ctypes.POINTER(CacheStats), c_u64p]),
+    "msb_gguf_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(c_vp)]),
+    "msb_gguf_close": (ctypes.c_int, [c_vp]),
+    "msb_gguf_shard_count": (ctypes.c_int32, [c_vp]),
+    "msb_gguf_tensor_count": (ctypes.c_int64, [c_vp]),
+    "msb_gguf_tensor_info": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.POINTER(GgufTensor)]),
+    "msb_gguf_find_tensor": (ctypes.c_int64, [c_vp, ctypes.c_char_p]),
+    "msb_gguf_expert_tensor": (ctypes.c_int64, [c_vp, ctypes.c_int32, ctypes.c_int]),
+    "msb_gguf_kv_int": (ctypes.c_int, [c_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]),
+    "msb_gguf_bytes_per_slot": (ctypes.c_uint64, [c_vp]),
+    "msb_gguf_read_experts": (ctypes.c_int, [c_vp, ctypes.c_int64, ctypes.c_int32, c_i32p,
+                                             ctypes.POINTER(c_vp), ctypes.c_int32]),
+    "msb_gguf_fill_slots_async": (ctypes.c_int, [c_vp, ctypes.c_int64, c_vp, ctypes.c_int32,
+                                                 c_i32p, c_i32p, ctypes.c_int32, c_vp]),
 }
 
 _lib = None

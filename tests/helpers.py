@@ -28,3 +28,30 @@ def zipf_bias(rng, n_expert, s=1.1):
     ranks = rng.permutation(n_expert) + 1
     p = ranks.astype(np.float64) ** (-s)
     return np.log(p / p.sum())
+
+
+def write_gguf(path, tensors, kvs=(), arch="gpt-oss", split_max_tensors=0, alignment=None):
+    """Writes a GGUF with the gguf package's writer (an implementation
+    independent of the library's parser). tensors: [(name, array, ggml type
+    or None)]; quantized arrays are uint8 [..., row bytes]. kvs: [(method of
+    GGUFWriter, args...)]. Returns the paths written, shard order."""
+    import os
+
+    from gguf import GGUFWriter
+    w = GGUFWriter(str(path), arch, split_max_tensors=split_max_tensors)
+    if alignment is not None:
+        w.add_custom_alignment(alignment)
+    for method, *args in kvs:
+        getattr(w, method)(*args)
+    for name, arr, raw in tensors:
+        w.add_tensor(name, arr, raw_dtype=raw)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    d, base = os.path.split(str(path))
+    stem = base[:-5] if base.endswith(".gguf") else base
+    if split_max_tensors:
+        return sorted(os.path.join(d, f) for f in os.listdir(d)
+                      if f.startswith(stem + "-") and f.endswith(".gguf"))
+    return [str(path)]
