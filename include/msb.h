@@ -517,6 +517,65 @@ int msb_gguf_fill_slots_async(msb_gguf_t g, int64_t tensor, msb_pool_t pool,
                               const int32_t *slots, int32_t n_threads,
                               void *stream);
 
+/* ======================================================================== */
+/* Prefill arena on the device                                              */
+/* ======================================================================== */
+
+/* When a micro-batch's expert union exceeds the slots (msb_arena_threshold),
+ * the reference runs mul_mat_id against a per-layer arena holding every
+ * expert (prefill_exps, src/llama-moestream.cpp:2147-2155), loads into arena
+ * il % n_buf only the experts the batch needs that it does not hold yet
+ * (load_layer_arena :2167-2283), and loads the next layer in the background
+ * with the previous pass's union of that layer as the hint (pf_kick
+ * :2285-2317); what the hint missed is read once the ids are known.
+ * Here each arena buffer is three pools (gate, up, down) with one slot per
+ * expert (slot e holds expert e; slot n_expert is the zero slot), filled
+ * from the GGUF; route the batch with msb_remap_group(ids, ..., table NULL,
+ * n_slot = n_expert) and run the FFN over the pools msb_arena_ready gives.
+ * All calls come from one thread; the background load is the library's. */
+typedef struct msb_arena_s *msb_arena_t;
+
+typedef struct {
+  uint64_t loads;          /* loads that read something                     */
+  uint64_t hits;           /* loads with nothing left to read               */
+  uint64_t experts_asked;  /* n_expert per load (what a full read would be) */
+  uint64_t experts_read;   /* experts actually read                         */
+  uint64_t bytes_read;     /* expert bytes read, all roles                  */
+} msb_arena_stats_t;
+
+/* Opens the GGUF (its own handle) and sets up n_buf arena buffers on the
+ * current device. Layers: <arch>.block_count, else the highest layer with
+ * expert tensors. Pools are allocated on a buffer's first load, and again
+ * when a layer's type or shape differs from the buffer's. */
+int msb_arena_create(const char *gguf_path, int32_t n_buf, int32_t n_threads,
+                     msb_arena_t *out);
+/* Waits for the background load and every recorded use, frees it all. */
+int msb_arena_destroy(msb_arena_t a);
+int msb_arena_info(msb_arena_t a, int32_t *n_layer, int32_t *n_expert,
+                   int32_t *n_buf);
+/* Loads into buffer layer % n_buf the experts with need[e] != 0 (need NULL:
+ * all) that it does not hold for this layer; forgets what it held when it
+ * held another layer. Reads are synchronous, uploads ordered on `stream`
+ * after the last use of the buffer (msb_arena_release). Joins a background
+ * load first. */
+int msb_arena_load(msb_arena_t a, int32_t layer, const uint8_t *need,
+                   void *stream);
+/* msb_arena_load on a background thread (hint as `need`), uploads on
+ * `stream`; one in flight at a time; needs n_buf >= 2. */
+int msb_arena_prefetch(msb_arena_t a, int32_t layer, const uint8_t *hint,
+                       void *stream);
+/* Joins the background load; returns its status. */
+int msb_arena_wait(msb_arena_t a);
+/* The pools holding `layer`, with compute_stream made to wait for their
+ * uploads. Fails when the buffer holds another layer. */
+int msb_arena_ready(msb_arena_t a, int32_t layer, void *compute_stream,
+                    msb_pool_t *gate, msb_pool_t *up, msb_pool_t *down);
+/* Marks the end of this layer's reads on compute_stream (the next load
+ * into its buffer waits for it). */
+int msb_arena_release(msb_arena_t a, int32_t layer, void *compute_stream);
+/* Counters (joins the background load first). */
+int msb_arena_stats(msb_arena_t a, msb_arena_stats_t *out);
+
 #ifdef __cplusplus
 }
 #endif

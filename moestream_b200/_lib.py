@@ -51,6 +51,14 @@ class GgufTensor(ctypes.Structure):
                 ("nbytes", ctypes.c_int64)]
 
 
+class ArenaStats(ctypes.Structure):
+    _fields_ = [(f, ctypes.c_uint64) for f in ("loads", "hits", "experts_asked", "experts_read",
+                                                "bytes_read")]
+
+    def as_dict(self):
+        return {f: int(getattr(self, f)) for f, _ in self._fields_}
+
+
 class Route(ctypes.Structure):
     _fields_ = [("slot_ids", c_vp), ("counts", c_vp), ("offsets", c_vp),
                 ("rows", c_vp), ("active", c_vp)]
@@ -169,6 +177,17 @@ SIGNATURES = {
                                              ctypes.POINTER(c_vp), ctypes.c_int32]),
     "msb_gguf_fill_slots_async": (ctypes.c_int, [c_vp, ctypes.c_int64, c_vp, ctypes.c_int32,
                                                  c_i32p, c_i32p, ctypes.c_int32, c_vp]),
+    "msb_arena_create": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int32, ctypes.c_int32,
+                                        ctypes.POINTER(c_vp)]),
+    "msb_arena_destroy": (ctypes.c_int, [c_vp]),
+    "msb_arena_info": (ctypes.c_int, [c_vp, c_i32p, c_i32p, c_i32p]),
+    "msb_arena_load": (ctypes.c_int, [c_vp, ctypes.c_int32, c_vp, c_vp]),
+    "msb_arena_prefetch": (ctypes.c_int, [c_vp, ctypes.c_int32, c_vp, c_vp]),
+    "msb_arena_wait": (ctypes.c_int, [c_vp]),
+    "msb_arena_ready": (ctypes.c_int, [c_vp, ctypes.c_int32, c_vp, ctypes.POINTER(c_vp),
+                                       ctypes.POINTER(c_vp), ctypes.POINTER(c_vp)]),
+    "msb_arena_release": (ctypes.c_int, [c_vp, ctypes.c_int32, c_vp]),
+    "msb_arena_stats": (ctypes.c_int, [c_vp, ctypes.POINTER(ArenaStats)]),
 }
 
 _lib = None

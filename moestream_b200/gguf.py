@@ -102,3 +102,78 @@ class GGUFFile:
         sl = (ctypes.c_int32 * max(n, 1))(*slots)
         check(lib().msb_gguf_fill_slots_async(self.handle, tensor, pool.handle, n, ids, sl,
                                               n_threads, _stream(stream)))
+
+
+class ExpertArena:
+    """Per-layer device arenas holding every expert of a layer, loaded from a
+    GGUF (msb_arena_*): the prefill path for micro-batches whose expert union
+    exceeds the slots. Route a batch with ops.remap_group(ids, n_expert)
+    (no table: slot e is expert e) and run the FFN over the pools of
+    ready(). One thread drives it; the background load is the library's."""
+
+    def __init__(self, path, n_buf=2, n_threads=4):
+        h = c_vp()
+        check(lib().msb_arena_create(str(path).encode(), n_buf, n_threads, ctypes.byref(h)))
+        self.handle = h
+        nl, ne, nb = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        check(lib().msb_arena_info(h, ctypes.byref(nl), ctypes.byref(ne), ctypes.byref(nb)))
+        self.n_layer, self.n_expert, self.n_buf = nl.value, ne.value, nb.value
+
+    def close(self):
+        if self.handle:
+            check(lib().msb_arena_destroy(self.handle))
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _mask(self, need):
+        """uint8 mask over experts from expert ids or a boolean mask; None stays None."""
+        if need is None:
+            return None, None
+        need = np.asarray(need)
+        if need.dtype == bool:
+            m = need.astype(np.uint8)
+            assert m.shape == (self.n_expert,)
+        else:
+            m = np.zeros(self.n_expert, dtype=np.uint8)
+            m[need.astype(np.int64).ravel()] = 1
+        return m, c_vp(m.ctypes.data)
+
+    def load(self, layer, need=None, stream=None):
+        """need: experts to hold (ids or a boolean mask over experts); None = all."""
+        m, p = self._mask(need)
+        check(lib().msb_arena_load(self.handle, layer, p, _stream(stream)))
+
+    def prefetch(self, layer, hint=None, stream=None):
+        m, p = self._mask(hint)
+        check(lib().msb_arena_prefetch(self.handle, layer, p, _stream(stream)))
+
+    def wait(self):
+        check(lib().msb_arena_wait(self.handle))
+
+    def ready(self, layer, stream=None):
+        """(gate, up, down) pools of the layer, the stream made to wait for them."""
+        from .ops import SlotPool
+        g, u, d = c_vp(), c_vp(), c_vp()
+        check(lib().msb_arena_ready(self.handle, layer, _stream(stream), ctypes.byref(g),
+                                    ctypes.byref(u), ctypes.byref(d)))
+        return SlotPool.borrowed(g), SlotPool.borrowed(u), SlotPool.borrowed(d)
+
+    def release(self, layer, stream=None):
+        check(lib().msb_arena_release(self.handle, layer, _stream(stream)))
+
+    def stats(self):
+        from ._lib import ArenaStats
+        st = ArenaStats()
+        check(lib().msb_arena_stats(self.handle, ctypes.byref(st)))
+        return st.as_dict()

@@ -61,10 +61,24 @@ class SlotPool:
         self.slot_stride = info.slot_stride
         self.zero_slot = n_slot
 
+    @classmethod
+    def borrowed(cls, handle):
+        """A view of a pool the library owns (an arena's): not destroyed here."""
+        self = cls.__new__(cls)
+        self.handle = handle if isinstance(handle, c_vp) else c_vp(handle)
+        self._owned = False
+        info = PoolInfo()
+        check(lib().msb_pool_get_info(handle, ctypes.byref(info)))
+        self.wtype, self.K, self.N, self.n_slot = info.wtype, info.K, info.N, info.n_slot
+        self.expert_bytes = info.expert_bytes
+        self.slot_stride = info.slot_stride
+        self.zero_slot = info.n_slot
+        return self
+
     def close(self):
-        if self.handle:
+        if self.handle and getattr(self, "_owned", True):
             check(lib().msb_pool_destroy(self.handle))
-            self.handle = None
+        self.handle = None
 
     def __del__(self):
         try:

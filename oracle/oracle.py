@@ -359,3 +359,36 @@ def ep_combine(back, pos, w, y):
         acc = torch.where(ok, fused, acc)
     y.copy_(acc)
     return y
+
+
+# --------------------------------------------------------------------------
+# Prefill arena bookkeeping: which experts each load reads.
+# --------------------------------------------------------------------------
+class ArenaPlan:
+    """Restates load_layer_arena's choice of reads
+    (src/llama-moestream.cpp:2167-2283): arena il % n_buf; when it switches
+    layers it forgets what it held (:2235-2239); it reads the experts that
+    `need` marks (all when need is None, :2249) and it does not hold
+    (:2250); a load with nothing to read is a hit (:2269-2276)."""
+
+    def __init__(self, n_expert, n_buf):
+        self.n_expert, self.n_buf = n_expert, n_buf
+        self.layer = [-1] * n_buf
+        self.have = [set() for _ in range(n_buf)]
+        self.loads = self.hits = self.asked = self.read = 0
+
+    def load(self, layer, need=None):
+        b = layer % self.n_buf
+        if self.layer[b] != layer:
+            self.have[b] = set()
+            self.layer[b] = layer
+        want = set(range(self.n_expert)) if need is None else {int(e) for e in need}
+        todo = sorted(want - self.have[b])
+        self.asked += self.n_expert
+        if not todo:
+            self.hits += 1
+        else:
+            self.loads += 1
+            self.read += len(todo)
+            self.have[b] |= set(todo)
+        return todo

@@ -229,3 +229,33 @@ def test_missing_file(tmp_path):
     from moestream_b200.gguf import GGUFFile
     with pytest.raises(MsbError, match="cannot open"):
         GGUFFile(tmp_path / "nope.gguf")
+
+
+def test_arena_bookkeeping_restatement():
+    """The oracle's restatement of the reference's arena reads on a small
+    schedule worked out by hand."""
+    from oracle.oracle import ArenaPlan
+    p = ArenaPlan(n_expert=4, n_buf=2)
+    assert p.load(0, [1, 2]) == [1, 2]
+    assert p.load(1) == [0, 1, 2, 3]                # no hint: every expert
+    assert p.load(0, [2, 3]) == [3]                 # 2 is held already
+    assert p.load(0, [1]) == [] and p.hits == 1
+    assert p.load(2, [0]) == [0]                    # arena 0 switches layers: forgets
+    assert p.load(0, [1]) == [1]
+    assert (p.loads, p.read, p.asked) == (5, 9, 24)
+
+
+def test_arena_refuses_files_without_experts(tmp_path):
+    from moestream_b200 import MsbError
+    from moestream_b200._lib import lib
+    import ctypes
+    path = write_gguf(tmp_path / "dense.gguf",
+                      [("blk.0.ffn_up.weight", np.zeros((4, 32), np.float32), None)])[0]
+    h = ctypes.c_void_p()
+    assert lib().msb_arena_create(path.encode(), 2, 1, ctypes.byref(h)) != 0
+    assert b"no expert tensors" in lib().msb_last_error()
+    assert lib().msb_arena_create(str(tmp_path / "none.gguf").encode(), 2, 1,
+                                  ctypes.byref(h)) != 0
+    with pytest.raises(MsbError):
+        from moestream_b200.gguf import ExpertArena
+        ExpertArena(tmp_path / "none.gguf")
