@@ -167,6 +167,26 @@ int msb_remap_group(const int32_t *ids_dev, int64_t nb0, int64_t nb1,
                     const msb_route_t *route, void *stream);
 
 /* ======================================================================== */
+/* Router: top-k experts and weights per token (device)                      */
+/* ======================================================================== */
+
+#define MSB_ROUTER_SOFTMAX_TOPK 0  /* softmax over the k selected logits (gpt-oss;
+                                      = softmax over all, renormalised)      */
+#define MSB_ROUTER_SOFTMAX_ALL  1  /* softmax over all experts, the selected
+                                      probabilities as they are             */
+
+/* For each token t (row t of `logits`, n_expert values of type F32, F16 or
+ * BF16, rows nb1 bytes apart): ids[t*top_k + j] = the expert with the j-th
+ * largest logit (lower index first among equal logits; NaN counts as -inf)
+ * and w[t*top_k + j] its weight. 1 <= top_k <= min(32, n_expert),
+ * n_expert <= 1024. The ids feed msb_remap_group with nb0 = 4,
+ * nb1 = 4 * top_k. The router of llama.cpp's MoE graph that produces the
+ * ids the reference remaps (build_remap, src/llama-moestream.cpp:2555). */
+int msb_router_topk(const void *logits_dev, int logits_type, int64_t nb1,
+                    int32_t n_tok, int32_t n_expert, int32_t top_k, int mode,
+                    int32_t *ids_dev, float *w_dev, void *stream);
+
+/* ======================================================================== */
 /* mul_mat_id                                                                 */
 /* ======================================================================== */
 

@@ -18,6 +18,7 @@ TYPE_MXFP4 = 39
 ORIGIN_DEMAND, ORIGIN_PREFETCH_HIGH, ORIGIN_PREFETCH_LOW, ORIGIN_SWEEP = 0, 1, 2, 3
 NO_SLOT = 0xFFFFFFFF
 OPT_MXFP4_PATH = 1
+ROUTER_SOFTMAX_TOPK, ROUTER_SOFTMAX_ALL = 0, 1
 
 c_i32p = ctypes.POINTER(ctypes.c_int32)
 c_u32p = ctypes.POINTER(ctypes.c_uint32)
@@ -177,6 +178,9 @@ SIGNATURES = {
                                              ctypes.POINTER(c_vp), ctypes.c_int32]),
     "msb_gguf_fill_slots_async": (ctypes.c_int, [c_vp, ctypes.c_int64, c_vp, ctypes.c_int32,
                                                  c_i32p, c_i32p, ctypes.c_int32, c_vp]),
+    "msb_router_topk": (ctypes.c_int, [c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int32,
+                                       ctypes.c_int32, ctypes.c_int32, ctypes.c_int, c_vp, c_vp,
+                                       c_vp]),
     "msb_arena_create": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int32, ctypes.c_int32,
                                         ctypes.POINTER(c_vp)]),
     "msb_arena_destroy": (ctypes.c_int, [c_vp]),

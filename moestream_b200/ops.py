@@ -136,6 +136,23 @@ def remap_group(ids, n_slot, table=None, n_expert=None, route=None, stream=None)
     return route
 
 
+def router_topk(logits, top_k, mode="topk", ids=None, w=None, stream=None):
+    """logits: [n_tok, n_expert] f32/f16/bf16 device tensor (row stride free).
+    Returns (ids int32 [n_tok, top_k], w f32 [n_tok, top_k]); mode "topk":
+    softmax over the selected logits, "all": softmax over all experts."""
+    n_tok, n_expert = logits.shape
+    assert logits.stride(1) == 1
+    if ids is None:
+        ids = torch.empty(n_tok, top_k, dtype=torch.int32, device=logits.device)
+    if w is None:
+        w = torch.empty(n_tok, top_k, dtype=torch.float32, device=logits.device)
+    types = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 30}
+    check(lib().msb_router_topk(_ptr(logits), types[logits.dtype],
+                                logits.stride(0) * logits.element_size(), n_tok, n_expert, top_k,
+                                {"topk": 0, "all": 1}[mode], _ptr(ids), _ptr(w), _stream(stream)))
+    return ids, w
+
+
 def workspace(K_max, n_tok, top_k, n_slot, device="cuda"):
     nbytes = int(lib().msb_workspace_bytes(K_max, n_tok, top_k, n_slot))
     return torch.empty(nbytes, dtype=torch.uint8, device=device)
