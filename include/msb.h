@@ -596,6 +596,55 @@ int msb_arena_release(msb_arena_t a, int32_t layer, void *compute_stream);
 /* Counters (joins the background load first). */
 int msb_arena_stats(msb_arena_t a, msb_arena_stats_t *out);
 
+/* ======================================================================== */
+/* Device slot streamer: the decode remap without a host round trip          */
+/* ======================================================================== */
+
+/* The same decisions as msb_streamer_remap (one ExpertCache per layer as
+ * the reference's finalize builds them, src/llama-moestream.cpp:1438-1447;
+ * decode loop :1900-1952), made by a kernel from cache state kept in device
+ * memory, with the miss queue (experts and slots, first-seen order) in
+ * mapped pinned memory: the reference's stated fix for its per-layer
+ * GPU<->CPU synchronisation. A fill kernel then copies the missed experts
+ * from pinned host memory into their slots, so remap, fills, grouping and
+ * the FFN are all stream-ordered launches that a CUDA graph can hold.
+ * on_host != 0 keeps the state in host memory and runs the same decision
+ * code on the calling thread (ids and slots are host pointers, no fills):
+ * for checking on machines without a GPU. */
+typedef struct msb_dstreamer_s *msb_dstreamer_t;
+
+/* n_layer caches of n_expert experts over n_slot slots (slot n_slot is the
+ * zero slot); at most max_pairs (token, k) pairs per call. */
+int msb_dstreamer_create(uint32_t n_layer, uint32_t n_expert, uint32_t n_slot,
+                         int32_t max_pairs, uint64_t expert_bytes_total,
+                         int on_host, msb_dstreamer_t *out);
+/* Synchronizes the device, frees everything. */
+int msb_dstreamer_destroy(msb_dstreamer_t s);
+/* One layer's remap: releases the layer's previous references, acquires
+ * every (t, k) in order; out_slots[t*top_k + k] = slot, or n_slot for an
+ * invalid id or on exhaustion (device memory; ids read with byte strides
+ * nb0 between k, nb1 between tokens). The layer's miss queue is replaced. */
+int msb_dstreamer_remap(msb_dstreamer_t s, uint32_t layer, const int32_t *ids,
+                        int64_t nb0, int64_t nb1, int32_t top_k, int32_t n_tok,
+                        int32_t *out_slots, void *stream);
+/* Fills the slots of the layer's last misses in `pool` (n_slot slots, as
+ * the streamer's) from `src`: expert e in ggml layout at
+ * src + e * src_expert_stride, pinned host memory or device memory. Call
+ * once per role (gate, up, down) with that role's pool and source. */
+int msb_dstreamer_fill(msb_dstreamer_t s, uint32_t layer, msb_pool_t pool,
+                       const void *src, int64_t src_expert_stride,
+                       void *stream);
+/* The layer's last miss queue, read from the mapped memory: valid once the
+ * remap has completed (after a stream or event synchronize). experts and
+ * slots may be NULL; otherwise they hold max_pairs entries. */
+int msb_dstreamer_misses(msb_dstreamer_t s, uint32_t layer, int32_t *n_miss,
+                         int32_t *experts, int32_t *slots);
+/* expert -> slot of a layer (-1 without one), n_expert entries; synchronous. */
+int msb_dstreamer_table(msb_dstreamer_t s, uint32_t layer, int32_t *table);
+/* Counters summed over layers plus the exhaustion count; synchronous. */
+int msb_dstreamer_stats(msb_dstreamer_t s, msb_cache_stats_t *out,
+                        uint64_t *n_exhausted);
+
 #ifdef __cplusplus
 }
 #endif

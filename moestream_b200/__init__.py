@@ -6,7 +6,7 @@ runs in libmsb.so (hand-written sm_100a CUDA); this package binds its C ABI.
 """
 from ._lib import (LIB_PATH, NO_SLOT, TYPE_BF16, TYPE_F32, TYPE_IQ4_NL, TYPE_MXFP4, MsbError,
                    lib)
-from .cache import ExpertCache, SlotStreamer
+from .cache import DeviceSlotStreamer, ExpertCache, SlotStreamer
 
 __all__ = ["LIB_PATH", "NO_SLOT", "TYPE_BF16", "TYPE_F32", "TYPE_IQ4_NL", "TYPE_MXFP4",
-           "MsbError", "lib", "ExpertCache", "SlotStreamer"]
+           "MsbError", "lib", "ExpertCache", "SlotStreamer", "DeviceSlotStreamer"]

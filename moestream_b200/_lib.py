@@ -181,6 +181,18 @@ SIGNATURES = {
     "msb_router_topk": (ctypes.c_int, [c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_int, c_vp, c_vp,
                                        c_vp]),
+    "msb_dstreamer_create": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                            ctypes.c_int32, ctypes.c_uint64, ctypes.c_int,
+                                            ctypes.POINTER(c_vp)]),
+    "msb_dstreamer_destroy": (ctypes.c_int, [c_vp]),
+    "msb_dstreamer_remap": (ctypes.c_int, [c_vp, ctypes.c_uint32, c_vp, ctypes.c_int64,
+                                           ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, c_vp,
+                                           c_vp]),
+    "msb_dstreamer_fill": (ctypes.c_int, [c_vp, ctypes.c_uint32, c_vp, c_vp, ctypes.c_int64,
+                                          c_vp]),
+    "msb_dstreamer_misses": (ctypes.c_int, [c_vp, ctypes.c_uint32, c_i32p, c_i32p, c_i32p]),
+    "msb_dstreamer_table": (ctypes.c_int, [c_vp, ctypes.c_uint32, c_i32p]),
+    "msb_dstreamer_stats": (ctypes.c_int, [c_vp, ctypes.POINTER(CacheStats), c_u64p]),
     "msb_arena_create": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int32, ctypes.c_int32,
                                         ctypes.POINTER(c_vp)]),
     "msb_arena_destroy": (ctypes.c_int, [c_vp]),

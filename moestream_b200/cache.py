@@ -112,4 +112,91 @@ class SlotStreamer:
         return d
 
 
-__all__ = ["ExpertCache", "SlotStreamer", "NO_SLOT"]
+class DeviceSlotStreamer:
+    """The SlotStreamer's decisions made on the device (msb_dstreamer_*):
+    cache state in device memory, the miss queue in mapped pinned memory,
+    and a fill kernel that copies missed experts from pinned host memory, so
+    a decode step needs no host round trip. on_host=True runs the same
+    decision code on the host (numpy ids and slots; no fills)."""
+
+    def __init__(self, n_layer, n_expert, n_slot, max_pairs, expert_bytes_total=0,
+                 on_host=False):
+        h = c_vp()
+        check(lib().msb_dstreamer_create(n_layer, n_expert, n_slot, max_pairs,
+                                         expert_bytes_total, 1 if on_host else 0,
+                                         ctypes.byref(h)))
+        self.h = h
+        self.n_layer, self.n_expert, self.n_slot = n_layer, n_expert, n_slot
+        self.max_pairs, self.on_host = max_pairs, on_host
+
+    def close(self):
+        if getattr(self, "h", None):
+            check(lib().msb_dstreamer_destroy(self.h))
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def remap(self, layer, ids, out=None, stream=None):
+        """ids: int32 [n_tok, top_k] (numpy on a host streamer, a device tensor
+        otherwise; any strides). Returns the slots [n_tok, top_k]."""
+        if self.on_host:
+            ids = np.asarray(ids)
+            assert ids.dtype == np.int32 and ids.ndim == 2
+            n_tok, top_k = ids.shape
+            if out is None:
+                out = np.empty((n_tok, top_k), dtype=np.int32)
+            nb0, nb1 = ids.strides[1], ids.strides[0]
+            base, dst, st = ids.__array_interface__["data"][0], out.ctypes.data, None
+        else:
+            import torch
+            assert ids.dtype == torch.int32 and ids.is_cuda and ids.dim() == 2
+            n_tok, top_k = ids.shape
+            if out is None:
+                out = torch.empty(n_tok, top_k, dtype=torch.int32, device=ids.device)
+            nb0, nb1 = ids.stride(1) * 4, ids.stride(0) * 4
+            base, dst = ids.data_ptr(), out.data_ptr()
+            st = stream if stream is not None else torch.cuda.current_stream()
+            st = st.cuda_stream
+        check(lib().msb_dstreamer_remap(self.h, layer, c_vp(base), nb0, nb1, top_k, n_tok,
+                                        c_vp(dst), c_vp(st)))
+        return out
+
+    def fill(self, layer, pool, src, stream=None):
+        """src: uint8 [n_expert, stride] tensor of ggml-layout experts, pinned
+        host memory or device memory."""
+        import torch
+        assert src.dtype == torch.uint8 and src.dim() == 2 and src.stride(1) == 1
+        assert src.shape[0] >= self.n_expert and src.shape[1] >= pool.expert_bytes
+        assert src.is_cuda or src.is_pinned()
+        st = stream if stream is not None else torch.cuda.current_stream()
+        check(lib().msb_dstreamer_fill(self.h, layer, pool.handle, c_vp(src.data_ptr()),
+                                       src.stride(0), c_vp(st.cuda_stream)))
+
+    def misses(self, layer):
+        """[(expert, slot)] of the layer's last remap (after it completed)."""
+        me = np.empty(self.max_pairs, dtype=np.int32)
+        ms = np.empty(self.max_pairs, dtype=np.int32)
+        n = ctypes.c_int32(0)
+        check(lib().msb_dstreamer_misses(self.h, layer, ctypes.byref(n),
+                                         me.ctypes.data_as(c_i32p), ms.ctypes.data_as(c_i32p)))
+        return list(zip(me[:n.value].tolist(), ms[:n.value].tolist()))
+
+    def table(self, layer):
+        t = np.empty(self.n_expert, dtype=np.int32)
+        check(lib().msb_dstreamer_table(self.h, layer, t.ctypes.data_as(c_i32p)))
+        return t
+
+    def stats(self):
+        st = CacheStats()
+        ex = ctypes.c_uint64(0)
+        check(lib().msb_dstreamer_stats(self.h, ctypes.byref(st), ctypes.byref(ex)))
+        d = st.as_dict()
+        d["exhausted"] = int(ex.value)
+        return d
+
+
+__all__ = ["ExpertCache", "SlotStreamer", "DeviceSlotStreamer", "NO_SLOT"]

@@ -12,8 +12,8 @@ PKG = os.path.dirname(HERE)
 OUT = os.path.join(PKG, "libmsb.so")
 BUILD = os.path.join(PKG, "_build")
 
-SOURCES = ["host_api.cpp", "expert_cache.cpp", "pool.cu", "route.cu", "mmid.cu", "mmid_tc.cu", "ep.cu", "ep_peers.cu", "gguf.cpp", "arena.cpp", "router.cu"]
-HEADERS = ["msb_internal.h", "expert_cache.hpp", "pool.cuh", "quant.cuh", "sm100.cuh",
+SOURCES = ["host_api.cpp", "expert_cache.cpp", "pool.cu", "route.cu", "mmid.cu", "mmid_tc.cu", "ep.cu", "ep_peers.cu", "gguf.cpp", "arena.cpp", "router.cu", "dstreamer.cu"]
+HEADERS = ["msb_internal.h", "dcache.cuh", "expert_cache.hpp", "pool.cuh", "quant.cuh", "sm100.cuh",
            os.path.join("..", "..", "include", "msb.h")]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

@@ -19,12 +19,8 @@
 
 namespace msb {
 
-static constexpr int kRepackRows = 32;  // rows per repack CTA
-
 // ggml-layout expert (rows of `nb` blocks) -> device layout, one CTA per
-// (expert, 32-row tile). The tile's bytes are contiguous in the source, so
-// they are staged in shared memory with coalesced loads and written out one
-// block column at a time (32 rows x 16 bytes contiguous).
+// (expert, 32-row tile) (repack_tile in pool.cuh).
 __global__ void __launch_bounds__(256) repack_to_device_kernel(
     const uint8_t *const *srcs, const int32_t *slots, uint8_t *pool_base,
     int64_t slot_stride, int64_t N, int64_t nb, int block_bytes,
@@ -32,35 +28,8 @@ __global__ void __launch_bounds__(256) repack_to_device_kernel(
   extern __shared__ uint8_t tile[];
   const int ex = blockIdx.x / tiles_per_expert;
   const int64_t n0 = int64_t(blockIdx.x % tiles_per_expert) * kRepackRows;
-  const int rows = int(N - n0 < kRepackRows ? N - n0 : kRepackRows);
-  const int64_t row_bytes = nb * block_bytes;
-  const uint8_t *src = srcs[ex] + n0 * row_bytes;
-  const int64_t tile_bytes = rows * row_bytes;
-  if ((reinterpret_cast<uintptr_t>(src) & 3) == 0 && (tile_bytes & 3) == 0) {
-    const uint32_t *s4 = reinterpret_cast<const uint32_t *>(src);
-    uint32_t *t4 = reinterpret_cast<uint32_t *>(tile);
-    for (int64_t i = threadIdx.x; i < tile_bytes / 4; i += blockDim.x) t4[i] = s4[i];
-  } else {
-    for (int64_t i = threadIdx.x; i < tile_bytes; i += blockDim.x) tile[i] = src[i];
-  }
-  __syncthreads();
-  uint8_t *dst = pool_base + int64_t(slots[ex]) * slot_stride;
-  uint8_t *dst_scale = dst + nb * N * 16;
-  const bool mx = scale_bytes == 1;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane >= rows) return;
-  const int64_t n = n0 + lane;
-  for (int64_t b = warp; b < nb; b += blockDim.x / 32) {
-    const uint8_t *blk = tile + lane * row_bytes + b * block_bytes;
-    uint8_t q[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) q[j] = blk[scale_bytes + j];
-    uint4 v;
-    memcpy(&v, q, 16);
-    *reinterpret_cast<uint4 *>(dst + (b * N + n) * 16) = v;
-    uint8_t *sd = dst_scale + scale_offset(mx, b, n, N);
-    for (int j = 0; j < scale_bytes; ++j) sd[j] = blk[j];
-  }
+  repack_tile(tile, srcs[ex], pool_base + int64_t(slots[ex]) * slot_stride, n0, N, nb,
+              block_bytes, scale_bytes);
 }
 
 // Device layout -> ggml layout for one slot (used to check fills).
