@@ -13,12 +13,15 @@
 //                     streamer's decisions (the same code the host path
 //                     compiles), the CTA writes back the state, the slot ids
 //                     and the miss queue (experts and slots, first-seen
-//                     order) into mapped pinned memory the host can read;
+//                     order), into device memory for the fills and into
+//                     mapped pinned memory for the host;
 //   dfill_kernel      copies each missed expert, in ggml layout, from pinned
 //                     host memory (read by the kernel over the bus) or device
 //                     memory into its slot, repacking into the pool layout;
-//                     it reads the miss count from the queue, so the launch
-//                     does not depend on it;
+//                     it reads the miss count from the device copy of the
+//                     queue, so the launch does not depend on it (reading it
+//                     from the mapped copy in every CTA serialises on the
+//                     bus: 1.8 ms per launch with nothing to fill);
 // after which msb_remap_group groups the slot ids (no table) and the FFN
 // runs. Every launch is stream-ordered with no host decision between them,
 // so a whole decode step, misses and fills included, can be captured in a
@@ -45,6 +48,7 @@ struct msb_dstreamer_s {
   int32_t *state = nullptr;     // n_layer blocks of L.words (device, or host when on_host)
   int32_t *queue = nullptr;     // pinned, mapped: per layer [n_miss, 3 pad, experts, slots]
   int32_t *queue_dev = nullptr; // device address of `queue`
+  int32_t *dqueue = nullptr;    // device-memory copy the fill kernels read
   int64_t queue_words = 0;      // per layer
   size_t remap_smem = 0;
 
@@ -55,6 +59,7 @@ struct msb_dstreamer_s {
       return;
     }
     if (state) cudaFree(state);
+    if (dqueue) cudaFree(dqueue);
     if (queue) cudaFreeHost(queue);
   }
   int32_t *layer_queue(uint32_t l) const { return queue + int64_t(l) * queue_words; }
@@ -67,7 +72,7 @@ constexpr int kRemapThreads = 256;
 
 __global__ void __launch_bounds__(kRemapThreads) dc_remap_kernel(
     int32_t *state, DcLayout L, const char *ids, int64_t nb0, int64_t nb1, int32_t top_k,
-    int32_t n_tok, uint64_t expert_bytes, int32_t *out_slots, int32_t *queue) {
+    int32_t n_tok, uint64_t expert_bytes, int32_t *out_slots, int32_t *dqueue, int32_t *queue) {
   extern __shared__ int4 smem4[];
   int32_t *sm = reinterpret_cast<int32_t *>(smem4);
   const int32_t n_pairs = top_k * n_tok;
@@ -91,11 +96,14 @@ __global__ void __launch_bounds__(kRemapThreads) dc_remap_kernel(
   for (int32_t p = threadIdx.x; p < n_pairs; p += blockDim.x) out_slots[p] = sout[p];
   const int32_t cap = L.max_pairs;
   for (int32_t i = threadIdx.x; i < n_miss; i += blockDim.x) {
+    dqueue[4 + i] = sme[i];
+    dqueue[4 + cap + i] = sms[i];
     queue[4 + i] = sme[i];
     queue[4 + cap + i] = sms[i];
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    dqueue[0] = n_miss;
     __threadfence_system();  // the queue entries before the count
     queue[0] = n_miss;
   }
@@ -109,7 +117,7 @@ __global__ void __launch_bounds__(256) dfill_kernel(
     int scale_bytes, int tiles) {
   extern __shared__ uint8_t tile[];
   pdl_wait();
-  const int32_t n_miss = *reinterpret_cast<const volatile int32_t *>(queue);
+  const int32_t n_miss = queue[0];
   const int64_t items = int64_t(n_miss) * tiles;
   for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
     const int32_t m = int32_t(w / tiles);
@@ -167,6 +175,8 @@ int msb_dstreamer_create(uint32_t n_layer, uint32_t n_expert, uint32_t n_slot, i
   cudaError_t e = cudaMalloc(&s->state, init.size() * sizeof(int32_t));
   if (e == cudaSuccess)
     e = cudaMemcpy(s->state, init.data(), init.size() * sizeof(int32_t), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&s->dqueue, qbytes);
+  if (e == cudaSuccess) e = cudaMemset(s->dqueue, 0, qbytes);
   if (e == cudaSuccess)
     e = cudaHostAlloc(reinterpret_cast<void **>(&s->queue), qbytes,
                       cudaHostAllocMapped | cudaHostAllocPortable);
@@ -174,6 +184,7 @@ int msb_dstreamer_create(uint32_t n_layer, uint32_t n_expert, uint32_t n_slot, i
     std::memset(s->queue, 0, qbytes);
     e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&s->queue_dev), s->queue, 0);
   }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // the memset and copies above
   if (e == cudaSuccess && s->remap_smem > 48 * 1024)
     e = cudaFuncSetAttribute(msb::dc_remap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(s->remap_smem));
@@ -223,6 +234,7 @@ int msb_dstreamer_remap(msb_dstreamer_t s, uint32_t layer, const int32_t *ids, i
                                static_cast<cudaStream_t>(stream), st, s->L,
                                reinterpret_cast<const char *>(ids), nb0, nb1, top_k, n_tok,
                                s->expert_bytes, out_slots,
+                               s->dqueue + int64_t(layer) * s->queue_words,
                                s->queue_dev + int64_t(layer) * s->queue_words));
   msb::count_launch();
   return MSB_OK;
@@ -249,7 +261,7 @@ int msb_dstreamer_fill(msb_dstreamer_t s, uint32_t layer, msb_pool_t pool, const
   const int grid = int(most < 2 * n_sm ? most : 2 * n_sm);
   MSB_CUDA_TRY(msb::launch_pdl(msb::dfill_kernel, dim3(grid), dim3(256), smem,
                                static_cast<cudaStream_t>(stream),
-                               s->queue_dev + int64_t(layer) * s->queue_words, s->L.max_pairs,
+                               s->dqueue + int64_t(layer) * s->queue_words, s->L.max_pairs,
                                static_cast<const uint8_t *>(src), src_expert_stride, pool->data,
                                pool->slot_stride, pool->N, pool->nb, pool->block_bytes,
                                pool->scale_bytes, tiles));
