@@ -256,6 +256,29 @@ int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0,
                 int32_t n_tok, float *y_dev, float *act_dev, void *workspace,
                 int64_t workspace_bytes, void *stream);
 
+/* The activation between the gate/up and down projections of
+ * msb_moe_ffn_act. MSB_ACT_SILU: silu(g) * u (what msb_moe_ffn applies).
+ * MSB_ACT_SWIGLU_OAI: gpt-oss's clamped form, x = min(g, limit),
+ * y = clamp(u, -limit, limit), h = x * sigmoid(alpha * x) * (y + 1)
+ * (llama.cpp's swiglu_oai, alpha 1.702 and limit 7 for gpt-oss; the
+ * reference's spikes use plain SwiGLU and the reference itself leaves the
+ * activation to llama.cpp). Expert biases are not applied. */
+#define MSB_ACT_SILU        0
+#define MSB_ACT_SWIGLU_OAI  1
+typedef struct {
+  int   kind;
+  float alpha;
+  float limit;   /* > 0 for MSB_ACT_SWIGLU_OAI */
+} msb_ffn_act_t;
+
+/* msb_moe_ffn with the activation chosen by `act` (NULL: MSB_ACT_SILU). */
+int msb_moe_ffn_act(msb_pool_t gate, msb_pool_t up, int64_t up_row0,
+                    msb_pool_t down, const void *x_dev, int x_type,
+                    int64_t x_nb1, const msb_route_t *route, const float *w_dev,
+                    int32_t top_k, int32_t n_tok, float *y_dev, float *act_dev,
+                    const msb_ffn_act_t *act, void *workspace,
+                    int64_t workspace_bytes, void *stream);
+
 /* ======================================================================== */
 /* Expert parallelism (packing around the all-to-all exchanges)               */
 /* ======================================================================== */

@@ -60,6 +60,13 @@ class ArenaStats(ctypes.Structure):
         return {f: int(getattr(self, f)) for f, _ in self._fields_}
 
 
+ACT_SILU, ACT_SWIGLU_OAI = 0, 1
+
+
+class FfnActCfg(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int), ("alpha", ctypes.c_float), ("limit", ctypes.c_float)]
+
+
 class Route(ctypes.Structure):
     _fields_ = [("slot_ids", c_vp), ("counts", c_vp), ("offsets", c_vp),
                 ("rows", c_vp), ("active", c_vp)]
@@ -116,6 +123,10 @@ SIGNATURES = {
     "msb_moe_ffn": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, c_vp, c_vp, ctypes.c_int,
                                    ctypes.c_int64, ctypes.POINTER(Route), c_vp, ctypes.c_int32,
                                    ctypes.c_int32, c_vp, c_vp, c_vp, ctypes.c_int64, c_vp]),
+    "msb_moe_ffn_act": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, c_vp, c_vp, ctypes.c_int,
+                                       ctypes.c_int64, ctypes.POINTER(Route), c_vp,
+                                       ctypes.c_int32, ctypes.c_int32, c_vp, c_vp,
+                                       ctypes.POINTER(FfnActCfg), c_vp, ctypes.c_int64, c_vp]),
     "msb_ep_dispatch": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_int32, c_vp, ctypes.c_int64,

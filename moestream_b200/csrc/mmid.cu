@@ -37,7 +37,7 @@ int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb
 int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
                   uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st,
-                  const RowTarget *res_rows = nullptr);
+                  const RowTarget *res_rows = nullptr, const FfnAct *fa = nullptr);
 
 // MXFP4 arithmetic: 0 = tensor cores where the shapes allow, 1 = CUDA cores
 // with int8 activations (ggml's q8_0 form) everywhere.
@@ -109,6 +109,7 @@ struct GemvArgs {
   float *res;        // plain: res[pair * n_out + n]
   ActQ8 out;         // SWIGLU: quantized silu(g) * u, nb = n_out / 32
   float *act;        // SWIGLU, optional: f32 silu(g) * u [pair * n_out + n]
+  FfnAct fa;         // SWIGLU: the activation
 };
 
 template <int WT>
@@ -309,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
       const int64_t pair = prs[c0 + r];
       if constexpr (SWIGLU) {
         const float g = tot[0], up = tot[1];
-        float h = valid ? g / (1.f + expf(-g)) * up : 0.f;
+        float h = valid ? ffn_act(a.fa, g, up) : 0.f;
         if (a.act && valid) a.act[pair * a.n_out + n] = h;
         store_q8_block(a.out, pair, tile, h, lane);
       } else if (valid) {
@@ -509,7 +510,9 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
                         const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
                         const float *w_dev, int32_t top_k, int32_t n_tok, float *y_dev,
                         float *act_dev, void *workspace, int64_t workspace_bytes,
-                        const RowTarget *rows, void *stream) {
+                        const RowTarget *rows, void *stream, const FfnAct &fa) {
+  MSB_CHECK_ARG(fa.kind == 0 || (fa.kind == 1 && fa.limit > 0.f),
+                "msb_moe_ffn: unknown activation %d (or limit <= 0)", fa.kind);
   MSB_CHECK_ARG(gate && up && down && route && (y_dev || rows) && workspace,
                 "msb_moe_ffn: null argument");
   MSB_CHECK_ARG(!rows || (!w_dev && top_k == 1), "msb_moe_ffn: row targets need top_k 1");
@@ -559,7 +562,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
     const bool timed = g_gate_up_start && g_gate_up_stop;
     if (timed) MSB_CUDA_TRY(record_timing_event(g_gate_up_start, st));
     if (int rc = tc_projection(gu_pools, 2, rows_gu, n_ff, route, pairs, xa, nullptr, ha, act_dev,
-                               max_active_tc, st))
+                               max_active_tc, st, nullptr, &fa))
       return rc;
     if (timed) {
       MSB_CUDA_TRY(record_timing_event(g_gate_up_stop, st));
@@ -596,6 +599,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
   g.zero_slot = gate->n_slot;
   g.top_k = top_k;
   g.b_ne1 = 1;
+  g.fa = fa;
   g.in = xq;
   g.out = hq;
   g.act = act_dev;
@@ -628,15 +632,31 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
                            const float *w_dev, int32_t top_k, int32_t n_tok, float *y_dev,
                            float *act_dev, void *workspace, int64_t workspace_bytes, void *stream) {
   return moe_ffn_core(gate, up, up_row0, down, x_dev, x_type, x_nb1, route, w_dev, top_k, n_tok,
-                      y_dev, act_dev, workspace, workspace_bytes, nullptr, stream);
+                      y_dev, act_dev, workspace, workspace_bytes, nullptr, stream, FfnAct{});
+}
+
+extern "C" int msb_moe_ffn_act(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
+                               const void *x_dev, int x_type, int64_t x_nb1,
+                               const msb_route_t *route, const float *w_dev, int32_t top_k,
+                               int32_t n_tok, float *y_dev, float *act_dev,
+                               const msb_ffn_act_t *act, void *workspace,
+                               int64_t workspace_bytes, void *stream) {
+  FfnAct fa;
+  if (act) {
+    fa.kind = act->kind;
+    fa.alpha = act->alpha;
+    fa.limit = act->limit;
+  }
+  return moe_ffn_core(gate, up, up_row0, down, x_dev, x_type, x_nb1, route, w_dev, top_k, n_tok,
+                      y_dev, act_dev, workspace, workspace_bytes, nullptr, stream, fa);
 }
 
 int msb::moe_ffn_to_rows(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
                          const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
                          int32_t n_tok, const RowTarget &rows, void *workspace,
-                         int64_t workspace_bytes, void *stream) {
+                         int64_t workspace_bytes, void *stream, const FfnAct &fa) {
   return moe_ffn_core(gate, up, up_row0, down, x_dev, x_type, x_nb1, route, nullptr, 1, n_tok,
-                      nullptr, nullptr, workspace, workspace_bytes, &rows, stream);
+                      nullptr, nullptr, workspace, workspace_bytes, &rows, stream, fa);
 }
 
 // ---- mul_mat_id without allocation ------------------------------------------

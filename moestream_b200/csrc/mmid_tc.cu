@@ -114,6 +114,7 @@ struct Args {
   uint8_t *oq, *osf;         // two views: terms of silu(gate) * up
   int64_t o_nb;              // n_out / 32
   float *act;                // two views, optional: f32 silu(gate) * up
+  FfnAct fa;                 // two views: the activation
 };
 
 __device__ __forceinline__ float *out_row(const RowTarget &t, int64_t r) {
@@ -524,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
           } else {
             const float u = (__uint_as_float(du[4 * j]) + __uint_as_float(du[4 * j + 1])) +
                             (__uint_as_float(du[4 * j + 2]) + __uint_as_float(du[4 * j + 3]));
-            const float h = valid ? gv / (1.f + expf(-gv)) * u : 0.f;
+            const float h = valid ? ffn_act(a.fa, gv, u) : 0.f;
             if (a.act && valid) a.act[pair * a.n_out + n] = h;
             if (blk < a.o_nb)
               warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, pos + j), 16,
@@ -620,7 +621,7 @@ static int launch_tc_t(const tc::Args &a, int max_active, int64_t n_pairs, cudaS
 int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
                   uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st,
-                  const RowTarget *res_rows) {
+                  const RowTarget *res_rows, const FfnAct *fa) {
   const msb_pool_s *pool = pools[0];
   tc::Args a{};
   for (int v = 0; v < 2; ++v) {
@@ -657,6 +658,7 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   a.o_nb = n_out / 32;
   a.osf = act_out ? act_out + int64_t(tc::kTerms) * a.o_nb * n_pairs * 16 : nullptr;
   a.act = act_f32;
+  a.fa = fa ? *fa : FfnAct{};
   {
     // A pair's four 16-byte term records of one block are 64 contiguous
     // bytes (8 elements of 8 bytes); a box line is the 8 pairs of one pass

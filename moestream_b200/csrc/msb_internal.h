@@ -54,13 +54,22 @@ struct RowTarget {
   int32_t n_arrive = 0;
 };
 
+// The activation between the gate/up and down projections: kind 0 is
+// silu(g) * u; kind 1 (MSB_ACT_SWIGLU_OAI) is gpt-oss's clamped form
+// min(g, limit) * sigmoid(alpha * min(g, limit)) * (clamp(u, -limit, limit) + 1).
+struct FfnAct {
+  int kind = 0;
+  float alpha = 1.f;
+  float limit = 0.f;
+};
+
 // msb_moe_ffn whose down projection writes its rows to `rows` (top_k 1, no
 // router weights, tensor-core shapes only; MSB_ERR_UNSUPPORTED otherwise,
 // before any launch).
 int moe_ffn_to_rows(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
                     const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
                     int32_t n_tok, const RowTarget &rows, void *workspace,
-                    int64_t workspace_bytes, void *stream);
+                    int64_t workspace_bytes, void *stream, const FfnAct &fa = FfnAct{});
 
 // msb_remap_group whose kernel first waits on `wait` (route.cu), and
 // msb_ep_combine likewise (ep.cu).
@@ -126,6 +135,15 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+// h = act(g, u) of FfnAct, in f32 with expf.
+__device__ __forceinline__ float ffn_act(const FfnAct &f, float g, float u) {
+  if (f.kind == 1) {
+    const float x = g < f.limit ? g : f.limit;
+    const float y = u < -f.limit ? -f.limit : (u > f.limit ? f.limit : u);
+    return x / (1.f + expf(-f.alpha * x)) * (y + 1.f);
+  }
+  return g / (1.f + expf(-g)) * u;
 }
 #endif
 

@@ -7,8 +7,8 @@ import ctypes
 
 import torch
 
-from ._lib import (OPT_MXFP4_PATH, TYPE_BF16, TYPE_F32, TYPE_IQ4_NL, TYPE_MXFP4, PoolInfo,
-                   Route, c_vp, check, lib)
+from ._lib import (OPT_MXFP4_PATH, TYPE_BF16, TYPE_F32, TYPE_IQ4_NL, TYPE_MXFP4, FfnActCfg,
+                   PoolInfo, Route, c_vp, check, lib)
 
 WEIGHT_TYPES = {"iq4_nl": TYPE_IQ4_NL, "mxfp4": TYPE_MXFP4}
 _ACT_TYPES = {torch.float32: TYPE_F32, torch.bfloat16: TYPE_BF16}
@@ -175,9 +175,11 @@ def mul_mat_id(pool, b, route, top_k, ws=None, out=None, stream=None):
 
 
 def moe_ffn(gate, up, down, x, route, w, top_k, up_row0=0, ws=None, out=None, act=None,
-            stream=None):
+            stream=None, activation=None):
     """x: [n_tok, K] f32/bf16; w: [n_tok, top_k] f32, or None with top_k 1 (y is
-    the expert output itself). Returns y [n_tok, K] f32."""
+    the expert output itself). activation: None for silu(g) * u, or
+    ("swiglu_oai", alpha, limit) for gpt-oss's clamped form. Returns y
+    [n_tok, K] f32."""
     n_tok, K = x.shape
     assert x.stride(1) == 1
     assert (w is None and top_k == 1) or (w.dtype == torch.float32 and w.is_contiguous())
@@ -186,10 +188,19 @@ def moe_ffn(gate, up, down, x, route, w, top_k, up_row0=0, ws=None, out=None, ac
         ws = workspace(kmax, n_tok, top_k, gate.n_slot, x.device)
     if out is None:
         out = torch.empty(n_tok, K, dtype=torch.float32, device=x.device)
-    check(lib().msb_moe_ffn(gate.handle, up.handle, up_row0, down.handle, _ptr(x),
-                            _ACT_TYPES[x.dtype], x.stride(0) * x.element_size(),
-                            ctypes.byref(route.c), _ptr(w), top_k, n_tok, _ptr(out), _ptr(act),
-                            _ptr(ws), ws.numel(), _stream(stream)))
+    if activation is None:
+        check(lib().msb_moe_ffn(gate.handle, up.handle, up_row0, down.handle, _ptr(x),
+                                _ACT_TYPES[x.dtype], x.stride(0) * x.element_size(),
+                                ctypes.byref(route.c), _ptr(w), top_k, n_tok, _ptr(out),
+                                _ptr(act), _ptr(ws), ws.numel(), _stream(stream)))
+        return out
+    kind, alpha, limit = activation
+    cfg = FfnActCfg({"silu": 0, "swiglu_oai": 1}[kind], alpha, limit)
+    check(lib().msb_moe_ffn_act(gate.handle, up.handle, up_row0, down.handle, _ptr(x),
+                                _ACT_TYPES[x.dtype], x.stride(0) * x.element_size(),
+                                ctypes.byref(route.c), _ptr(w), top_k, n_tok, _ptr(out),
+                                _ptr(act), ctypes.byref(cfg), _ptr(ws), ws.numel(),
+                                _stream(stream)))
     return out
 
 

@@ -402,7 +402,8 @@ int orc_mul_mat_id(int type, const uint8_t *as, int64_t K, int64_t N, int64_t n_
   return 0;
 }
 
-/* MoE FFN over slot ids: h = silu(gate(x)) * up(x) per (t, k), r = down(h),
+/* MoE FFN over slot ids: h = silu(gate(x)) * up(x) per (t, k) (act 1: the
+ * gpt-oss clamped form with alpha and limit), r = down(h),
  * y[t] = sum_k w[t][k] * r[t][k]. gate/up/down: [n_slots][rows][K/32] ggml
  * bytes; up rows start at up_row0 within up (fused gate_up tensors).
  * In q8 mode h is re-quantized before the down projection, as the device
@@ -410,7 +411,8 @@ int orc_mul_mat_id(int type, const uint8_t *as, int64_t K, int64_t N, int64_t n_
 int orc_moe_ffn(int type, const uint8_t *gate, int64_t gate_rows, const uint8_t *up,
                 int64_t up_rows, int64_t up_row0, const uint8_t *down, int64_t K, int64_t n_ff,
                 int64_t n_slots, const float *x, const int32_t *ids, const float *w, int top_k,
-                int T, int mode, float *y, float *h_out, int nthreads) {
+                int T, int mode, int act, float alpha, float limit, float *y, float *h_out,
+                int nthreads) {
   const int64_t pairs = (int64_t)T * top_k;
   const int64_t bb = block_bytes(type);
   if (bb < 0 || K % 32 || n_ff % 32) return -1;
@@ -432,7 +434,17 @@ int orc_moe_ffn(int type, const uint8_t *gate, int64_t gate_rows, const uint8_t 
   free(uv);
   if (!rc) {
     float *h = (float *)malloc(sizeof(float) * (size_t)(pairs * n_ff));
-    for (int64_t i = 0; i < pairs * n_ff; ++i) h[i] = g[i] / (1.f + expf(-g[i])) * u[i];
+    for (int64_t i = 0; i < pairs * n_ff; ++i) {
+      if (act == 1) {
+        /* gpt-oss: gate clamped above, up clamped both ways and shifted by
+         * one, sigmoid with slope alpha (llama.cpp's swiglu_oai). */
+        const float xg = g[i] < limit ? g[i] : limit;
+        const float yu = u[i] < -limit ? -limit : (u[i] > limit ? limit : u[i]);
+        h[i] = xg / (1.f + expf(-alpha * xg)) * (yu + 1.f);
+      } else {
+        h[i] = g[i] / (1.f + expf(-g[i])) * u[i];
+      }
+    }
     if (h_out) memcpy(h_out, h, sizeof(float) * (size_t)(pairs * n_ff));
     rc = orc_mul_mat_id(type, down, n_ff, K, n_slots, h, top_k, ids, top_k, T, mode, r, nthreads);
     free(h);

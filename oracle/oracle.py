@@ -58,7 +58,8 @@ def orc():
         L.orc_moe_ffn.argtypes = [ctypes.c_int, _u8p, ctypes.c_int64, _u8p, ctypes.c_int64,
                                   ctypes.c_int64, _u8p, ctypes.c_int64, ctypes.c_int64,
                                   ctypes.c_int64, _f32p, _i32p, _f32p, ctypes.c_int, ctypes.c_int,
-                                  ctypes.c_int, _f32p, _f32p, ctypes.c_int]
+                                  ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                  _f32p, _f32p, ctypes.c_int]
         L.orc_e2m1_split.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, _f32p, _u8p, _u8p]
         L.orc_quantize_q8.argtypes = [_f32p, ctypes.c_int64, ctypes.POINTER(ctypes.c_int8), _f32p]
         L.orc_f32_to_f16.argtypes = [ctypes.c_float]
@@ -261,11 +262,13 @@ def mul_mat_id(wtype, slab, K, N, b, ids, mode="exact", nthreads=None):
 
 
 def moe_ffn(wtype, gate, up, down, K, n_ff, x, ids, w, mode="exact", up_row0=0, up_rows=None,
-            nthreads=None):
+            nthreads=None, act=None):
     """gate/up/down: uint8 [n_slots, bytes]; x: f32 [T, K]; ids: [T, top_k] slot
     ids; w: f32 [T, top_k]. The gate is rows [0, n_ff) and the up projection
     rows [up_row0, up_row0 + n_ff) of their slots (the same array for a fused
-    gate_up tensor). Returns (y [T, K], h [T, top_k, n_ff])."""
+    gate_up tensor). act: None for silu(gate) * up, or (alpha, limit) for the
+    gpt-oss form min(g, limit) * sigmoid(alpha * min(g, limit)) *
+    (clamp(u, -limit, limit) + 1). Returns (y [T, K], h [T, top_k, n_ff])."""
     t = TYPES.get(wtype, wtype)
     gate, up, down = (np.ascontiguousarray(a, dtype=np.uint8) for a in (gate, up, down))
     row_bytes = (K // 32) * BLOCK_BYTES[t]
@@ -279,7 +282,8 @@ def moe_ffn(wtype, gate, up, down, K, n_ff, x, ids, w, mode="exact", up_row0=0, 
     h = np.empty((T, top_k, n_ff), dtype=np.float32)
     rc = orc().orc_moe_ffn(t, _p(gate, _u8p), gate_rows, _p(up, _u8p), up_rows, up_row0,
                            _p(down, _u8p), K, n_ff, gate.shape[0], _p(x, _f32p), _p(ids, _i32p),
-                           _p(w, _f32p), top_k, T, MODES[mode], _p(y, _f32p),
+                           _p(w, _f32p), top_k, T, MODES[mode], 1 if act else 0,
+                           act[0] if act else 1.0, act[1] if act else 0.0, _p(y, _f32p),
                            _p(h, _f32p), nthreads or os.cpu_count() or 1)
     assert rc == 0, rc
     return y, h

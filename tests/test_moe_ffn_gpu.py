@@ -133,3 +133,51 @@ def test_unweighted_top1_writes_expert_output(path):
     got = ops.moe_ffn(pools["gate"], pools["up"], pools["down"], x, r, None, 1)
     torch.cuda.synchronize()
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("wtype,K,n_ff,n_expert,n_slot,n_tok,top_k,fused", [
+    ("mxfp4", 2880, 2880, 6, 4, 3, 4, False),    # tensor cores
+    ("mxfp4", 512, 256, 8, 8, 40, 4, True),      # tensor cores, fused gate_up, several passes
+    ("iq4_nl", 2048, 512, 10, 8, 8, 8, False),   # CUDA cores
+])
+def test_gpt_oss_activation_matches_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, fused):
+    """gpt-oss's clamped SwiGLU (alpha 1.702, limit 7) in both paths. The
+    activations are scaled by 8 so that many gate and up values pass the
+    clamp; tolerances as for plain SwiGLU."""
+    from moestream_b200 import ops
+    pools, slabs, slot_of = build_layer(wtype, K, n_ff, n_expert, n_slot, fused, seed=K + 7)
+    rng = np.random.default_rng(3)
+    x = (8 * rng.normal(0, 1, size=(n_tok, K))).astype(np.float32)
+    ids_e, w = topk_ids(rng, n_tok, n_expert, top_k)
+    table = np.full(n_expert, -1, dtype=np.int32)
+    for e, s in slot_of.items():
+        table[e] = s
+    slots = O.remap_table(ids_e, table, n_slot)
+    r = ops.remap_group(torch.from_numpy(ids_e).cuda(), n_slot,
+                        table=torch.from_numpy(table).cuda(), n_expert=n_expert)
+    act = torch.empty(n_tok, top_k, n_ff, dtype=torch.float32, device="cuda")
+    y = ops.moe_ffn(pools["gate"], pools["up"], pools["down"], torch.from_numpy(x).cuda(), r,
+                    torch.from_numpy(w).cuda(), top_k, up_row0=n_ff if fused else 0, act=act,
+                    activation=("swiglu_oai", 1.702, 7.0))
+    torch.cuda.synchronize()
+    tc = wtype == "mxfp4"
+    up = slabs["gate"] if fused else slabs["up"]
+    y_f, h_f = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
+                         mode="e2m1x4" if tc else "q8", up_row0=n_ff if fused else 0,
+                         act=(1.702, 7.0))
+    _, h_silu = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
+                          mode="e2m1x4" if tc else "q8", up_row0=n_ff if fused else 0)
+    assert np.abs(h_f).max() > 0 and not np.allclose(h_f, h_silu)  # not plain SwiGLU
+    assert O.max_abs_normalized(act.cpu().numpy(), h_f) < (1e-4 if tc else 1e-5)
+    assert O.max_abs_normalized(y.cpu().numpy(), y_f) < (1e-3 if tc else 2e-3)
+
+
+def test_unknown_activation_is_refused():
+    from moestream_b200 import MsbError, ops
+    pools, _, _ = build_layer("iq4_nl", 256, 128, 4, 2, False, seed=1)
+    r = ops.remap_group(torch.zeros(1, 1, dtype=torch.int32, device="cuda"), 2)
+    x = torch.zeros(1, 256, device="cuda")
+    for bad in (("swiglu_oai", 1.702, 0.0),):
+        with pytest.raises(MsbError, match="activation"):
+            ops.moe_ffn(pools["gate"], pools["up"], pools["down"], x, r, None, 1,
+                        activation=bad)
