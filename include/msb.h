@@ -662,9 +662,11 @@ int msb_dstreamer_fill(msb_dstreamer_t s, uint32_t layer, msb_pool_t pool,
  * slots may be NULL; otherwise they hold max_pairs entries. */
 int msb_dstreamer_misses(msb_dstreamer_t s, uint32_t layer, int32_t *n_miss,
                          int32_t *experts, int32_t *slots);
-/* expert -> slot of a layer (-1 without one), n_expert entries; synchronous. */
+/* expert -> slot of a layer (-1 without one), n_expert entries; waits for
+ * the device (every stream) first. */
 int msb_dstreamer_table(msb_dstreamer_t s, uint32_t layer, int32_t *table);
-/* Counters summed over layers plus the exhaustion count; synchronous. */
+/* Counters summed over layers plus the exhaustion count; waits for the
+ * device first. */
 int msb_dstreamer_stats(msb_dstreamer_t s, msb_cache_stats_t *out,
                         uint64_t *n_exhausted);
 

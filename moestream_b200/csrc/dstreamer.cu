@@ -287,6 +287,8 @@ int msb_dstreamer_table(msb_dstreamer_t s, uint32_t layer, int32_t *table) {
     std::memcpy(table, st, size_t(s->L.E) * sizeof(int32_t));
     return MSB_OK;
   }
+  // The remap may have run on any stream: wait for all of them.
+  MSB_CUDA_TRY(cudaDeviceSynchronize());
   MSB_CUDA_TRY(cudaMemcpy(table, st, size_t(s->L.E) * sizeof(int32_t), cudaMemcpyDeviceToHost));
   return MSB_OK;
 }
@@ -297,6 +299,7 @@ int msb_dstreamer_stats(msb_dstreamer_t s, msb_cache_stats_t *out, uint64_t *n_e
   if (s->on_host) {
     std::memcpy(all.data(), s->state, all.size() * sizeof(int32_t));
   } else {
+    MSB_CUDA_TRY(cudaDeviceSynchronize());
     MSB_CUDA_TRY(cudaMemcpy(all.data(), s->state, all.size() * sizeof(int32_t),
                             cudaMemcpyDeviceToHost));
   }
