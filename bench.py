@@ -319,8 +319,9 @@ def streamed_main(args):
     experts of one layer are quantized on the device from N(0, 0.02) and kept
     as one pinned host copy per role that every layer's misses read (the
     bytes do not change the timing; pinned memory stays at 1.7 GB).
-    --remap device: cache decisions, fills, grouping and FFN of all layers
-    in one CUDA graph per step, no host round trip; --remap host: each
+    --remap device: cache decisions, fills (one launch for the three roles),
+    grouping and FFN of all layers in one CUDA graph per step, no host round
+    trip; --remap host: each
     layer's ids go to the host, the host slot streamer decides, DMA fills,
     the slots come back. Both make the same decisions."""
     import numpy as np
@@ -379,14 +380,14 @@ def streamed_main(args):
         ids_d.copy_(ids_all[s])
         w_d.copy_(w_all[s])
 
+    roles = ("gate", "up", "down")
     if args.remap == "device":
         dev = DeviceSlotStreamer(L, E, NS, T * top_k, per_expert)
 
         def step():
             for il in range(L):
                 dev.remap(il, ids_d[il], out=slots[il])
-                for r in ("gate", "up", "down"):
-                    dev.fill(il, pools[il][r], src[r])
+                dev.fill_roles(il, [pools[il][r] for r in roles], [src[r] for r in roles])
                 ops.remap_group(slots[il], NS, route=route)
                 ops.moe_ffn(pools[il]["gate"], pools[il]["up"], pools[il]["down"], x_d, route,
                             w_d[il], top_k, ws=ws, out=y[il])

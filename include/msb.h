@@ -657,6 +657,11 @@ int msb_dstreamer_remap(msb_dstreamer_t s, uint32_t layer, const int32_t *ids,
 int msb_dstreamer_fill(msb_dstreamer_t s, uint32_t layer, msb_pool_t pool,
                        const void *src, int64_t src_expert_stride,
                        void *stream);
+/* msb_dstreamer_fill for n_roles (1..3) pools at once (gate, up and down of
+ * the layer, say): one launch whose CTAs interleave the roles' tiles. */
+int msb_dstreamer_fill_roles(msb_dstreamer_t s, uint32_t layer, int32_t n_roles,
+                             const msb_pool_t *pools, const void *const *srcs,
+                             const int64_t *src_expert_strides, void *stream);
 /* The layer's last miss queue, read from the mapped memory: valid once the
  * remap has completed (after a stream or event synchronize). experts and
  * slots may be NULL; otherwise they hold max_pairs entries. */

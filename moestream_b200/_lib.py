@@ -201,6 +201,9 @@ SIGNATURES = {
                                            c_vp]),
     "msb_dstreamer_fill": (ctypes.c_int, [c_vp, ctypes.c_uint32, c_vp, c_vp, ctypes.c_int64,
                                           c_vp]),
+    "msb_dstreamer_fill_roles": (ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.c_int32,
+                                                ctypes.POINTER(c_vp), ctypes.POINTER(c_vp),
+                                                ctypes.POINTER(ctypes.c_int64), c_vp]),
     "msb_dstreamer_misses": (ctypes.c_int, [c_vp, ctypes.c_uint32, c_i32p, c_i32p, c_i32p]),
     "msb_dstreamer_table": (ctypes.c_int, [c_vp, ctypes.c_uint32, c_i32p]),
     "msb_dstreamer_stats": (ctypes.c_int, [c_vp, ctypes.POINTER(CacheStats), c_u64p]),

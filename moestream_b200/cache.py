@@ -176,6 +176,22 @@ class DeviceSlotStreamer:
         check(lib().msb_dstreamer_fill(self.h, layer, pool.handle, c_vp(src.data_ptr()),
                                        src.stride(0), c_vp(st.cuda_stream)))
 
+    def fill_roles(self, layer, pools, srcs, stream=None):
+        """fill() of several roles (pools[i] from srcs[i]) in one launch."""
+        import torch
+        n = len(pools)
+        assert n == len(srcs) and 1 <= n <= 3
+        for p, src in zip(pools, srcs):
+            assert src.dtype == torch.uint8 and src.dim() == 2 and src.stride(1) == 1
+            assert src.shape[0] >= self.n_expert and src.shape[1] >= p.expert_bytes
+            assert src.is_cuda or src.is_pinned()
+        st = stream if stream is not None else torch.cuda.current_stream()
+        hp = (c_vp * n)(*[p.handle.value for p in pools])
+        sp = (c_vp * n)(*[src.data_ptr() for src in srcs])
+        strides = (ctypes.c_int64 * n)(*[src.stride(0) for src in srcs])
+        check(lib().msb_dstreamer_fill_roles(self.h, layer, n, hp, sp, strides,
+                                             c_vp(st.cuda_stream)))
+
     def misses(self, layer):
         """[(expert, slot)] of the layer's last remap (after it completed)."""
         me = np.empty(self.max_pairs, dtype=np.int32)

@@ -15,7 +15,8 @@
 //                     and the miss queue (experts and slots, first-seen
 //                     order), into device memory for the fills and into
 //                     mapped pinned memory for the host;
-//   dfill_kernel      copies each missed expert, in ggml layout, from pinned
+//   dfill_kernel      copies each missed expert (of up to three roles in one
+//                     launch), in ggml layout, from pinned
 //                     host memory (read by the kernel over the bus) or device
 //                     memory into its slot, repacking into the pool layout;
 //                     it reads the miss count from the device copy of the
@@ -110,21 +111,34 @@ __global__ void __launch_bounds__(kRemapThreads) dc_remap_kernel(
   pdl_trigger();
 }
 
-// Persistent grid over (miss, 32-row tile) items.
-__global__ void __launch_bounds__(256) dfill_kernel(
-    const int32_t *queue, int32_t cap, const uint8_t *src, int64_t src_stride,
-    uint8_t *pool_base, int64_t slot_stride, int64_t N, int64_t nb, int block_bytes,
-    int scale_bytes, int tiles) {
+// The pools and sources of up to three roles filled by one launch.
+struct FillRoles {
+  const uint8_t *src[3];
+  int64_t src_stride[3];
+  uint8_t *base[3];
+  int64_t slot_stride[3], N[3], nb[3];
+  int block_bytes[3], scale_bytes[3], tiles[3];
+  int n;
+};
+
+// Persistent grid over (role, miss, 32-row tile) items, the roles' items
+// interleaved miss by miss so that every role's bytes are in flight at once.
+__global__ void __launch_bounds__(256) dfill_kernel(const int32_t *queue, int32_t cap,
+                                                    const __grid_constant__ FillRoles f) {
   extern __shared__ uint8_t tile[];
   pdl_wait();
   const int32_t n_miss = queue[0];
-  const int64_t items = int64_t(n_miss) * tiles;
+  int per_miss = 0;
+  for (int r = 0; r < f.n; ++r) per_miss += f.tiles[r];
+  const int64_t items = int64_t(n_miss) * per_miss;
   for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
-    const int32_t m = int32_t(w / tiles);
-    const int64_t n0 = (w - int64_t(m) * tiles) * kRepackRows;
+    const int32_t m = int32_t(w / per_miss);
+    int t = int(w - int64_t(m) * per_miss), r = 0;
+    while (t >= f.tiles[r]) t -= f.tiles[r++];
     const int32_t e = queue[4 + m], s = queue[4 + cap + m];
-    repack_tile(tile, src + int64_t(e) * src_stride, pool_base + int64_t(s) * slot_stride, n0, N,
-                nb, block_bytes, scale_bytes);
+    repack_tile(tile, f.src[r] + int64_t(e) * f.src_stride[r],
+                f.base[r] + int64_t(s) * f.slot_stride[r], int64_t(t) * kRepackRows, f.N[r],
+                f.nb[r], f.block_bytes[r], f.scale_bytes[r]);
   }
   pdl_trigger();
 }
@@ -240,33 +254,60 @@ int msb_dstreamer_remap(msb_dstreamer_t s, uint32_t layer, const int32_t *ids, i
   return MSB_OK;
 }
 
-int msb_dstreamer_fill(msb_dstreamer_t s, uint32_t layer, msb_pool_t pool, const void *src,
-                       int64_t src_expert_stride, void *stream) {
-  MSB_CHECK_ARG(s && pool && src && layer < s->n_layer, "msb_dstreamer_fill: bad argument");
+int msb_dstreamer_fill_roles(msb_dstreamer_t s, uint32_t layer, int32_t n_roles,
+                             const msb_pool_t *pools, const void *const *srcs,
+                             const int64_t *src_expert_strides, void *stream) {
+  MSB_CHECK_ARG(s && layer < s->n_layer && n_roles >= 1 && n_roles <= 3 && pools && srcs &&
+                    src_expert_strides,
+                "msb_dstreamer_fill_roles: bad argument");
   MSB_CHECK_ARG(!s->on_host, "msb_dstreamer_fill: a host streamer has no device fills");
-  MSB_CHECK_ARG(pool->n_slot == s->L.n_slot, "msb_dstreamer_fill: the pool has %d slots, the streamer %d",
-                pool->n_slot, s->L.n_slot);
-  MSB_CHECK_ARG(src_expert_stride >= pool->expert_bytes,
-                "msb_dstreamer_fill: expert stride %lld below the expert's %lld bytes",
-                (long long)src_expert_stride, (long long)pool->expert_bytes);
-  const size_t smem = size_t(msb::kRepackRows) * pool->nb * pool->block_bytes;
-  MSB_CHECK_ARG(smem <= 227 * 1024, "msb_dstreamer_fill: rows too long for the repack tile");
+  msb::FillRoles f{};
+  f.n = n_roles;
+  size_t smem = 0;
+  int device = 0;
+  int64_t per_miss = 0;
+  for (int r = 0; r < n_roles; ++r) {
+    const msb_pool_s *p = pools[r];
+    MSB_CHECK_ARG(p && srcs[r], "msb_dstreamer_fill: null pool or source");
+    MSB_CHECK_ARG(p->n_slot == s->L.n_slot,
+                  "msb_dstreamer_fill: the pool has %d slots, the streamer %d", p->n_slot,
+                  s->L.n_slot);
+    MSB_CHECK_ARG(src_expert_strides[r] >= p->expert_bytes,
+                  "msb_dstreamer_fill: expert stride %lld below the expert's %lld bytes",
+                  (long long)src_expert_strides[r], (long long)p->expert_bytes);
+    const size_t sm = size_t(msb::kRepackRows) * p->nb * p->block_bytes;
+    MSB_CHECK_ARG(sm <= 227 * 1024, "msb_dstreamer_fill: rows too long for the repack tile");
+    smem = sm > smem ? sm : smem;
+    f.src[r] = static_cast<const uint8_t *>(srcs[r]);
+    f.src_stride[r] = src_expert_strides[r];
+    f.base[r] = p->data;
+    f.slot_stride[r] = p->slot_stride;
+    f.N[r] = p->N;
+    f.nb[r] = p->nb;
+    f.block_bytes[r] = p->block_bytes;
+    f.scale_bytes[r] = p->scale_bytes;
+    f.tiles[r] = int((p->N + msb::kRepackRows - 1) / msb::kRepackRows);
+    per_miss += f.tiles[r];
+    device = p->device;
+  }
   if (smem > 48 * 1024)
     MSB_CUDA_TRY(cudaFuncSetAttribute(msb::dfill_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   int n_sm = 0;
-  MSB_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, pool->device));
-  const int tiles = int((pool->N + msb::kRepackRows - 1) / msb::kRepackRows);
-  const int64_t most = int64_t(s->L.max_pairs < s->L.n_slot ? s->L.max_pairs : s->L.n_slot) * tiles;
+  MSB_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device));
+  const int64_t most =
+      int64_t(s->L.max_pairs < s->L.n_slot ? s->L.max_pairs : s->L.n_slot) * per_miss;
   const int grid = int(most < 2 * n_sm ? most : 2 * n_sm);
   MSB_CUDA_TRY(msb::launch_pdl(msb::dfill_kernel, dim3(grid), dim3(256), smem,
                                static_cast<cudaStream_t>(stream),
-                               s->dqueue + int64_t(layer) * s->queue_words, s->L.max_pairs,
-                               static_cast<const uint8_t *>(src), src_expert_stride, pool->data,
-                               pool->slot_stride, pool->N, pool->nb, pool->block_bytes,
-                               pool->scale_bytes, tiles));
+                               s->dqueue + int64_t(layer) * s->queue_words, s->L.max_pairs, f));
   msb::count_launch();
   return MSB_OK;
+}
+
+int msb_dstreamer_fill(msb_dstreamer_t s, uint32_t layer, msb_pool_t pool, const void *src,
+                       int64_t src_expert_stride, void *stream) {
+  return msb_dstreamer_fill_roles(s, layer, 1, &pool, &src, &src_expert_stride, stream);
 }
 
 int msb_dstreamer_misses(msb_dstreamer_t s, uint32_t layer, int32_t *n_miss, int32_t *experts,

@@ -67,6 +67,30 @@ def test_device_fill_from_host_memory(wtype, K, N, where):
     assert int(pool.read_slot(n_slot).to(torch.int64).sum()) == 0
 
 
+def test_fill_of_three_roles_in_one_launch():
+    """fill_roles: pools of different shapes and types of block rows (gate
+    and up [K -> N_ff], down [N_ff -> K]) filled by one launch, bit-exact."""
+    from moestream_b200 import DeviceSlotStreamer, ops
+    n_expert, n_slot, K, N_FF = 10, 4, 2880, 640
+    shapes = {"gate": (K, N_FF), "up": (K, N_FF), "down": (N_FF, K)}
+    mats = {r: experts("mxfp4", n_expert, kk, nn, seed=i) for i, (r, (kk, nn)) in
+            enumerate(shapes.items())}
+    src = {r: torch.from_numpy(m).pin_memory() for r, m in mats.items()}
+    pools = {r: ops.SlotPool("mxfp4", kk, nn, n_slot) for r, (kk, nn) in shapes.items()}
+    dev = DeviceSlotStreamer(1, n_expert, n_slot, 8)
+    rng = np.random.default_rng(2)
+    for step in range(4):
+        ids = rng.permutation(n_expert)[:3].astype(np.int32).reshape(1, 3)
+        dev.remap(0, torch.from_numpy(ids).cuda())
+        dev.fill_roles(0, [pools[r] for r in shapes], [src[r] for r in shapes])
+        torch.cuda.synchronize()
+        table = dev.table(0)
+        for r in shapes:
+            for e in ids.ravel():
+                got = pools[r].read_slot(int(table[e])).cpu().numpy()
+                assert np.array_equal(got, mats[r][e]), (step, r, e)
+
+
 def test_graph_captured_decode_step_matches_oracle():
     from moestream_b200 import DeviceSlotStreamer, SlotStreamer, ops
     wtype, K, N_FF, n_expert, n_slot, top_k, n_tok = "mxfp4", 512, 256, 32, 12, 4, 2
@@ -87,8 +111,8 @@ def test_graph_captured_decode_step_matches_oracle():
 
     def step():
         dev.remap(0, ids_d, out=slots)
-        for r in ("gate", "up", "down"):
-            dev.fill(0, pools[r], src[r])
+        roles = ("gate", "up", "down")
+        dev.fill_roles(0, [pools[r] for r in roles], [src[r] for r in roles])
         ops.remap_group(slots, n_slot, route=route)
         ops.moe_ffn(pools["gate"], pools["up"], pools["down"], x_d, route, w_d, top_k,
                     ws=ws, out=y)
