@@ -7,6 +7,7 @@ import sys
 
 from tests.conftest import ROOT
 
+
 def _run(*args, timeout=600):
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
     out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args], cwd=ROOT,
