@@ -93,3 +93,31 @@ def test_arena_ready_refuses_a_layer_it_does_not_hold(tmp_path):
         arena.ready(0)
         with pytest.raises(MsbError, match="two arena buffers"):
             ExpertArena(path, n_buf=1).prefetch(1)
+
+
+def test_arena_is_bit_identical_to_slot_pools(tmp_path):
+    """The reference's arena spike checks mul_mat_id over the arena against
+    the normal buffer bit for bit (research/spikes/s6_arena_mulmatid/
+    main.c:206-243). Here: one layer's FFN over the arena loaded from the
+    GGUF, against the same experts filled into ordinary pools from memory."""
+    from moestream_b200 import ops
+    from moestream_b200.gguf import ExpertArena
+    path, mats = _model(tmp_path)
+    rng = np.random.default_rng(8)
+    ids, w = topk_ids(rng, N_TOK, E, TOP_K)
+    x = torch.from_numpy(rng.normal(0, 1, size=(N_TOK, K)).astype(np.float32)).cuda()
+    ids_d, w_d = torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda()
+    pools = {}
+    for r, (kk, nn) in (("gate", (K, N_FF)), ("up", (K, N_FF)), ("down", (N_FF, K))):
+        pools[r] = ops.SlotPool("mxfp4", kk, nn, E)
+        pools[r].fill(list(range(E)), [torch.from_numpy(mats[1, r][e]).pin_memory()
+                                       for e in range(E)])
+    route = ops.remap_group(ids_d, E)
+    y_pool = ops.moe_ffn(pools["gate"], pools["up"], pools["down"], x, route, w_d, TOP_K)
+    with ExpertArena(path, n_buf=2) as arena:
+        arena.load(1, np.unique(ids))
+        gate, up, down = arena.ready(1)
+        y_arena = ops.moe_ffn(gate, up, down, x, route, w_d, TOP_K)
+        arena.release(1)
+        torch.cuda.synchronize()
+    assert torch.equal(y_arena, y_pool)

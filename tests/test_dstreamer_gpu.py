@@ -154,3 +154,39 @@ def test_graph_captured_decode_step_matches_oracle():
         check(*inp)
     assert ops.device_status() == 0
     assert dev.stats()["miss"] > 6
+
+
+def test_streamed_ffn_is_bit_identical_to_resident():
+    """The reference's streaming spike checks that the streamed MoE FFN is
+    bit-identical to the fully resident one (research/spikes/
+    s1_real_expert_stream/main.c:375-388). Here: experts streamed through
+    the device streamer into 12 slots, against every expert resident in a
+    pool of its own (slot e = expert e), step after step."""
+    from moestream_b200 import DeviceSlotStreamer, ops
+    wtype, K, N_FF, n_expert, n_slot, top_k, n_tok = "mxfp4", 512, 256, 32, 12, 4, 3
+    shapes = {"gate": (K, N_FF), "up": (K, N_FF), "down": (N_FF, K)}
+    mats = {r: experts(wtype, n_expert, kk, nn, seed=40 + i)
+            for i, (r, (kk, nn)) in enumerate(shapes.items())}
+    src = {r: torch.from_numpy(m).pin_memory() for r, m in mats.items()}
+    stream_pools = {r: ops.SlotPool(wtype, kk, nn, n_slot) for r, (kk, nn) in shapes.items()}
+    full = {r: ops.SlotPool(wtype, kk, nn, n_expert) for r, (kk, nn) in shapes.items()}
+    for r in shapes:
+        full[r].fill(list(range(n_expert)), [src[r][e] for e in range(n_expert)])
+    dev = DeviceSlotStreamer(1, n_expert, n_slot, n_tok * top_k)
+    rng = np.random.default_rng(23)
+    bias = zipf_bias(rng, n_expert)
+    roles = ("gate", "up", "down")
+    for step in range(8):
+        ids, w = topk_ids(rng, n_tok, n_expert, top_k, bias=bias)
+        x = torch.from_numpy(rng.normal(0, 1, size=(n_tok, K)).astype(np.float32)).cuda()
+        ids_d, w_d = torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda()
+        slots = dev.remap(0, ids_d)
+        dev.fill_roles(0, [stream_pools[r] for r in roles], [src[r] for r in roles])
+        r_s = ops.remap_group(slots, n_slot)
+        y_s = ops.moe_ffn(stream_pools["gate"], stream_pools["up"], stream_pools["down"], x,
+                          r_s, w_d, top_k)
+        r_f = ops.remap_group(ids_d, n_expert)
+        y_f = ops.moe_ffn(full["gate"], full["up"], full["down"], x, r_f, w_d, top_k)
+        torch.cuda.synchronize()
+        assert int((slots == n_slot).sum()) == 0          # no exhaustion at these sizes
+        assert torch.equal(y_s, y_f), step
