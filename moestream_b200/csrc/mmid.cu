@@ -31,13 +31,17 @@ namespace msb {
 
 // Tensor-core path (mmid_tc.cu).
 int64_t tc_act_bytes(int64_t nb, int64_t rows);
+// Scratch for the split over K of small batches (0 when the batch is not
+// small): partial sums of up to two views with n_out_max rows.
+int64_t tc_split_bytes(int64_t n_out_max, int64_t n_pairs);
 int tc_supported(const msb_pool_s *p);
 int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb2, int32_t top_k,
                  const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st);
 int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
                   uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st,
-                  const RowTarget *res_rows = nullptr, const FfnAct *fa = nullptr);
+                  const RowTarget *res_rows = nullptr, const FfnAct *fa = nullptr,
+                  uint8_t *split_ws = nullptr, int64_t split_bytes = 0);
 
 // MXFP4 arithmetic: 0 = tensor cores where the shapes allow, 1 = CUDA cores
 // with int8 activations (ggml's q8_0 form) everywhere.
@@ -444,6 +448,9 @@ extern "C" int64_t msb_workspace_bytes(int64_t K_max, int32_t n_tok, int32_t top
   tcb = align_up(tcb + tc_act_bytes(nb, pairs), 256);
   tcb = align_up(tcb + tc_act_bytes(nb, pairs), 256);
   tcb = align_up(tcb + pairs * K_max * 4, 256);
+  // Split over K of small batches: partial sums (the largest projection
+  // mul_mat_id serves has 2 K_max rows: a fused gate_up).
+  tcb = align_up(tcb + tc_split_bytes(2 * K_max, pairs), 256);
   return (q8 > tcb ? q8 : tcb) + 256;
 }
 
@@ -484,8 +491,9 @@ extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, in
       return rc;
     const int64_t row0[2] = {0, 0};
     const msb_pool_s *pools[2] = {pool, pool};
+    const int64_t used = align_up(tc_act_bytes(pool->nb, pairs), 256);
     return tc_projection(pools, 1, row0, pool->N, route, pairs, act, res_dev, nullptr, nullptr,
-                         max_active, st);
+                         max_active, st, nullptr, nullptr, ws + used, workspace_bytes - used);
   }
   const int64_t n_rows = int64_t(n_tok) * b_ne1;
   ActQ8 in = carve_act(ws, &off, n_rows, pool->nb);
@@ -554,6 +562,10 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
     // Without router weights (top_k 1) the down projection writes y itself.
     float *rd = w_dev ? reinterpret_cast<float *>(ws + o) : y_dev;
     o = align_up(o + pairs * down->N * 4, 256);
+    // The rest: scratch for the split over K of small batches (gate/up and
+    // down use it one after the other).
+    uint8_t *split_ws = ws + o;
+    const int64_t split_bytes = workspace_bytes - o;
     if (int rc = tc_act_terms(x_dev, x_type, 1, x_nb1, x_nb1, top_k, route->rows, pairs, gate->nb,
                               xa, st))
       return rc;
@@ -562,7 +574,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
     const bool timed = g_gate_up_start && g_gate_up_stop;
     if (timed) MSB_CUDA_TRY(record_timing_event(g_gate_up_start, st));
     if (int rc = tc_projection(gu_pools, 2, rows_gu, n_ff, route, pairs, xa, nullptr, ha, act_dev,
-                               max_active_tc, st, nullptr, &fa))
+                               max_active_tc, st, nullptr, &fa, split_ws, split_bytes))
       return rc;
     if (timed) {
       MSB_CUDA_TRY(record_timing_event(g_gate_up_stop, st));
@@ -571,7 +583,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
     const int64_t rows_dn[2] = {0, 0};
     const msb_pool_s *dn_pools[2] = {down, down};
     if (int rc = tc_projection(dn_pools, 1, rows_dn, down->N, route, pairs, ha, rd, nullptr, nullptr,
-                               max_active_tc, st, rows))
+                               max_active_tc, st, rows, nullptr, split_ws, split_bytes))
       return rc;
     if (!w_dev) return MSB_OK;
     const int64_t total = down->N * n_tok;

@@ -115,6 +115,16 @@ struct Args {
   int64_t o_nb;              // n_out / 32
   float *act;                // two views, optional: f32 silu(gate) * up
   FfnAct fa;                 // two views: the activation
+  // Split over K for small batches (split_max > 0): a work item is also a
+  // segment of the K chunks; the epilogue stores f32 partial sums
+  // part[((seg * NV + view) * a_rows + position) * n_out + row] and
+  // split_reduce_kernel finishes (sums in segment order, then the
+  // activation and terms, or the result rows). The split the launch picks
+  // is written to *split_word.
+  int split_max;
+  float *part;
+  int *split_word;
+  const int32_t *slot_ids;   // slot of each pair (split reduce)
 };
 
 __device__ __forceinline__ float *out_row(const RowTarget &t, int64_t r) {
@@ -256,6 +266,43 @@ __device__ __forceinline__ Item locate(const Args &a, const int *item0, int64_t 
   return Item{slot, int(local % passes), (local / passes) * 128};
 }
 
+// Split over K: sums the segments' partial results in order and finishes
+// the epilogue of tc_kernel<NV> -- the activation and the down projection's
+// terms (two views) or the result rows (one view); pairs routed to the zero
+// slot get exact zeros, as in the epilogue. One warp per (pair position,
+// 32-row block), lane = row.
+template <int NV>
+__global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant__ Args a) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t nblk = (a.n_out + 31) / 32;
+  const int64_t wid = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (wid >= a.a_rows * nblk) return;   // whole warps only
+  const int64_t p = wid / nblk, blk = wid - p * nblk;
+  const int64_t n = blk * 32 + lane;
+  const bool valid = n < a.n_out;
+  const int64_t pair = a.rows[p];
+  const bool zero = a.slot_ids[pair] == a.zero_slot;
+  const int split = *a.split_word;
+  float g = 0.f, u = 0.f;
+  if (!zero && valid) {
+    for (int sg = 0; sg < split; ++sg) {
+      g += a.part[((int64_t(sg) * NV) * a.a_rows + p) * a.n_out + n];
+      if constexpr (NV == 2) u += a.part[((int64_t(sg) * NV + 1) * a.a_rows + p) * a.n_out + n];
+    }
+  }
+  if constexpr (NV == 1) {
+    if (valid && !(zero && a.out.skip_zero)) out_row(a.out, pair)[n] = g;
+  } else {
+    const float h = (!zero && valid) ? ffn_act(a.fa, g, u) : 0.f;
+    if (a.act && valid) a.act[pair * a.n_out + n] = h;
+    if (blk < a.o_nb)
+      warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, p), 16,
+                      a.osf + a4_off(0, blk / 4, a.a_rows, p) + (blk & 3), 16);
+  }
+}
+
 template <int NV>
 __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__ Args a) {
   using C = Cfg<NV>;
@@ -327,18 +374,33 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
   }
   __syncthreads();
   const int64_t n_items = item0[n_active];
+  // Split over K (small batches): as many segments as keep every CTA busy,
+  // at most split_max, each of at least one chunk per MMA warp. Every CTA
+  // computes the same value from the same route.
+  int split = 1;
+  if (a.split_max > 0) {
+    int64_t sp = n_items > 0 ? int64_t(gridDim.x) / n_items : 1;
+    const int64_t by_chunks = n_chunks / (NV == 1 ? C::kMma : 1);
+    if (sp > a.split_max) sp = a.split_max;
+    if (sp > by_chunks) sp = by_chunks;
+    split = sp < 1 ? 1 : int(sp);
+    if (blockIdx.x == 0 && threadIdx.x == 0) *a.split_word = split;
+  }
+  const int64_t n_work = n_items * split;
 
   if (warp == 0) {
     // ---- producer ----
     if (lane == 0) {
       uint32_t it = 0;
       int cur = 0;
-      for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
-        const Item item = locate(a, item0, w, cur);
+      for (int64_t w = blockIdx.x; w < n_work && !*abort_v; w += gridDim.x) {
+        const int64_t wi = w / split, seg = w - wi * split;
+        const Item item = locate(a, item0, wi, cur);
         const int slot = item.slot;
         if (slot == a.zero_slot) continue;
         const int pos = int(a.offsets[slot] + int64_t(item.pass) * kPairs);
-        for (int64_t i = 0; i < n_chunks; ++i, ++it) {
+        const int64_t lo = seg * n_chunks / split, hi = (seg + 1) * n_chunks / split;
+        for (int64_t i = lo; i < hi; ++i, ++it) {
           const int s = it % kStages;
           if (!sm100::mbar_wait_bounded(&empty[s], ((it / kStages) & 1) ^ 1)) {
             atomicOr(&g_status, kStatusProducer);
@@ -381,9 +443,11 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
     if (lane == 0 && m < C::kMma) {
       uint32_t it = 0, acc = 0;
       int cur = 0;
-      for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
-        const Item item = locate(a, item0, w, cur);
+      for (int64_t w = blockIdx.x; w < n_work && !*abort_v; w += gridDim.x) {
+        const int64_t wi = w / split, seg = w - wi * split;
+        const Item item = locate(a, item0, wi, cur);
         if (item.slot == a.zero_slot) continue;
+        const int64_t lo = seg * n_chunks / split, hi = (seg + 1) * n_chunks / split;
         const int buf = acc % kBufs;
         if (!sm100::mbar_wait_bounded(&acc_empty[buf], ((acc / kBufs) & 1) ^ 1)) {
           atomicOr(&g_status, kStatusAccEmpty);
@@ -394,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
         const uint32_t d0 = tmem + buf * C::kAccCols + m * kN;
         const int v = NV == 2 ? m : 0;
         bool first = true;
-        for (int64_t i = 0; i < n_chunks; ++i, ++it) {
+        for (int64_t i = lo; i < hi; ++i, ++it) {
           if (NV == 1 && i % C::kMma != m) continue;   // another warp's stage
           const int s = it % kStages;
           if (!sm100::mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
@@ -438,8 +502,9 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     uint32_t acc = 0;
     int cur = 0;
-    for (int64_t w = blockIdx.x; w < n_items && !*abort_v; w += gridDim.x) {
-      const Item item = locate(a, item0, w, cur);
+    for (int64_t w = blockIdx.x; w < n_work && !*abort_v; w += gridDim.x) {
+      const int64_t wi = w / split, seg = w - wi * split;
+      const Item item = locate(a, item0, wi, cur);
       const int slot = item.slot;
       const int64_t n0 = item.n0;
       const int64_t n = n0 + quad * 32 + lane;
@@ -447,6 +512,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
       const int64_t blk = (n0 >> 5) + quad;   // SwiGLU output block of this warp
       const int c_total = a.counts[slot];
       const int64_t pos0 = a.offsets[slot];
+      if (slot == a.zero_slot && a.split_max > 0) continue;   // the split reduce writes them
       if (slot == a.zero_slot) {
         // Every weight of the zero slot is 0, so the exact result is 0; for
         // the down projection's input, 0 splits into four zero terms with
@@ -520,11 +586,21 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
           // Column 4j + t holds term t of pair j.
           const float gv = (__uint_as_float(dg[4 * j]) + __uint_as_float(dg[4 * j + 1])) +
                            (__uint_as_float(dg[4 * j + 2]) + __uint_as_float(dg[4 * j + 3]));
+          float u = 0.f;
+          if constexpr (NV == 2)
+            u = (__uint_as_float(du[4 * j]) + __uint_as_float(du[4 * j + 1])) +
+                (__uint_as_float(du[4 * j + 2]) + __uint_as_float(du[4 * j + 3]));
+          if (a.split_max > 0) {
+            // This segment's partial sums; the split reduce finishes.
+            if (valid) {
+              a.part[((seg * NV) * a.a_rows + pos + j) * a.n_out + n] = gv;
+              if constexpr (NV == 2) a.part[((seg * NV + 1) * a.a_rows + pos + j) * a.n_out + n] = u;
+            }
+            continue;
+          }
           if constexpr (NV == 1) {
             if (valid) out_row(a.out, pair)[n] = gv;
           } else {
-            const float u = (__uint_as_float(du[4 * j]) + __uint_as_float(du[4 * j + 1])) +
-                            (__uint_as_float(du[4 * j + 2]) + __uint_as_float(du[4 * j + 3]));
             const float h = valid ? ffn_act(a.fa, gv, u) : 0.f;
             if (a.act && valid) a.act[pair * a.n_out + n] = h;
             if (blk < a.o_nb)
@@ -562,6 +638,15 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
+// Batches of up to kSplitPairs pairs may split K into up to kSplitMax
+// segments (tc_projection).
+constexpr int64_t kSplitPairs = 32;
+constexpr int kSplitMax = 4;
+
+int64_t tc_split_bytes(int64_t n_out_max, int64_t n_pairs) {
+  return n_pairs > 0 && n_pairs <= kSplitPairs ? 256 + 2 * kSplitMax * n_pairs * n_out_max * 4 : 0;
+}
+
 int64_t tc_act_bytes(int64_t nb, int64_t rows) {
   return int64_t(tc::kTerms) * (nb + (nb + 3) / 4) * rows * 16;
 }
@@ -604,13 +689,20 @@ static int launch_tc_t(const tc::Args &a, int max_active, int64_t n_pairs, cudaS
     MSB_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
   }
   const int64_t passes = int64_t(max_active) + n_pairs / tc::kPairs + 1;
-  int64_t grid = passes * a.tiles;
+  int64_t grid = passes * a.tiles * (a.split_max > 0 ? a.split_max : 1);
   if (grid > int64_t(C::kCtasPerSm) * n_sm) grid = int64_t(C::kCtasPerSm) * n_sm;
   if (grid == 0) return MSB_OK;
   MSB_CUDA_TRY(launch_pdl(tc::tc_kernel<NV>, dim3(unsigned(grid)), dim3(tc::kThreads), C::kSmem,
                           st, a));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
+  if (a.split_max > 0) {
+    const int64_t warps = n_pairs * ((a.n_out + 31) / 32);
+    MSB_CUDA_TRY(launch_pdl(tc::split_reduce_kernel<NV>, dim3(unsigned((warps + 7) / 8)),
+                            dim3(256), 0, st, a));
+    count_launch();
+    MSB_CUDA_TRY(cudaGetLastError());
+  }
   return MSB_OK;
 }
 
@@ -621,7 +713,8 @@ static int launch_tc_t(const tc::Args &a, int max_active, int64_t n_pairs, cudaS
 int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
                   uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st,
-                  const RowTarget *res_rows, const FfnAct *fa) {
+                  const RowTarget *res_rows, const FfnAct *fa, uint8_t *split_ws,
+                  int64_t split_bytes) {
   const msb_pool_s *pool = pools[0];
   tc::Args a{};
   for (int v = 0; v < 2; ++v) {
@@ -659,6 +752,20 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   a.osf = act_out ? act_out + int64_t(tc::kTerms) * a.o_nb * n_pairs * 16 : nullptr;
   a.act = act_f32;
   a.fa = fa ? *fa : FfnAct{};
+  // Split over K for small batches, where the items alone leave CTAs idle:
+  // up to kSplitMax segments, as many as the caller's scratch holds.
+  a.split_max = 0;
+  if (split_ws && n_pairs > 0 && n_pairs <= kSplitPairs && !(res_rows && res_rows->done)) {
+    const int64_t per = int64_t(nv) * n_pairs * n_out * 4;
+    int64_t sm = (split_bytes - 256) / per;
+    if (sm > kSplitMax) sm = kSplitMax;
+    if (sm >= 2) {
+      a.split_max = int(sm);
+      a.split_word = reinterpret_cast<int *>(split_ws);
+      a.part = reinterpret_cast<float *>(split_ws + 256);
+      a.slot_ids = route->slot_ids;
+    }
+  }
   {
     // A pair's four 16-byte term records of one block are 64 contiguous
     // bytes (8 elements of 8 bytes); a box line is the 8 pairs of one pass
