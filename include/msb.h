@@ -190,7 +190,9 @@ int msb_router_topk(const void *logits_dev, int logits_type, int64_t nb1,
 /* mul_mat_id                                                                 */
 /* ======================================================================== */
 
-/* Workspace bytes for msb_mul_mat_id / msb_moe_ffn with these shapes. */
+/* Workspace bytes for msb_mul_mat_id / msb_moe_ffn with these shapes
+ * (activation copies, intermediate results and, for batches of up to 8
+ * (token, k) pairs, the partial sums of the tensor cores' split over K). */
 int64_t msb_workspace_bytes(int64_t K_max, int32_t n_tok, int32_t top_k,
                             int32_t n_slot);
 

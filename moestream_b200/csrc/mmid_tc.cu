@@ -38,6 +38,10 @@
 //                    (rows), releases the buffer, then stores.
 // With two views (gate and up) the epilogue applies SwiGLU and writes the
 // down projection's activation terms directly.
+// Batches of up to 8 pairs leave most CTAs without an item, so there a work
+// item is also one of up to 4 segments of the K chunks: the epilogue stores
+// f32 partial sums and split_reduce_kernel adds the segments in order and
+// runs the epilogue (every CTA derives the same split from the route).
 // Every mbarrier wait is bounded (about a second); a wait that gives up sets
 // a bit of the device status word (msb_device_status) and the CTA stops
 // issuing work, waits (bounded) for its copies and MMAs in flight and
