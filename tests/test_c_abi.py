@@ -77,3 +77,19 @@ def test_errors_are_reported_not_raised():
         assert "weight type" in str(e)
     else:
         raise AssertionError("check() did not raise")
+
+
+def test_router_rejects_bad_shapes_before_any_device_work():
+    """msb_router_topk validates its arguments before touching the device
+    (these calls pass no device memory)."""
+    from moestream_b200._lib import lib
+    L = lib()
+    for ne, k, mode in ((1024 + 1, 4, 0),   # n_expert above 1024
+                        (128, 33, 0),       # top_k above 32
+                        (16, 17, 0),        # top_k above n_expert
+                        (128, 4, 2)):       # unknown mode
+        assert L.msb_router_topk(None, 0, 512, 4, ne, k, mode, None, None, None) != 0
+    assert L.msb_router_topk(None, 7, 512, 4, 128, 4, 0, None, None, None) != 0  # logit type
+    assert L.msb_router_topk(None, 0, 512, 4, 128, 4, 0, None, None, None) != 0  # null pointers
+    # An empty batch is a no-op.
+    assert L.msb_router_topk(None, 0, 512, 0, 128, 4, 0, None, None, None) == 0

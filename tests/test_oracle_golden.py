@@ -95,3 +95,30 @@ def test_reference_remap_matches_recorded_trace():
     g = load("remap_ref_trace.npz")
     r = O.RefRemap(int(g["n_expert"]), int(g["n_slot"]), 1000)
     _replay(r)
+
+
+def test_oracle_gpt_oss_activation_follows_the_formula():
+    """The oracle's gpt-oss activation (moe_ffn act=(alpha, limit)) equals
+    the formula evaluated in numpy on the oracle's own gate and up
+    projections: x = min(g, limit), y = clamp(u, -limit, limit),
+    h = x * sigmoid(alpha * x) * (y + 1). Activations are scaled so that both
+    clamps are active for some elements."""
+    from tests.helpers import experts
+    K, n_ff, E, T, top_k = 256, 64, 4, 3, 2
+    gate = experts("mxfp4", E, K, n_ff, seed=1)
+    up = experts("mxfp4", E, K, n_ff, seed=2)
+    down = experts("mxfp4", E, n_ff, K, seed=3)
+    rng = np.random.default_rng(4)
+    x = (40 * rng.normal(0, 1, size=(T, K))).astype(np.float32)
+    ids = np.array([[0, 1], [2, 3], [1, 2]], dtype=np.int32)
+    w = np.full((T, top_k), 0.5, dtype=np.float32)
+    g = O.mul_mat_id("mxfp4", gate, K, n_ff, x[:, None, :], ids, mode="exact")
+    u = O.mul_mat_id("mxfp4", up, K, n_ff, x[:, None, :], ids, mode="exact")
+    alpha, limit = 1.702, 7.0
+    xg = np.minimum(g, limit).astype(np.float64)
+    yu = np.clip(u, -limit, limit).astype(np.float64)
+    want = xg / (1 + np.exp(-alpha * xg)) * (yu + 1)
+    assert (g > limit).any() and (u < -limit).any() and (u > limit).any()
+    _, h = O.moe_ffn("mxfp4", gate, up, down, K, n_ff, x, ids, w, mode="exact",
+                     act=(alpha, limit))
+    assert np.abs(h - want).max() <= 1e-5 * np.abs(want).max()
