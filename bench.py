@@ -24,7 +24,9 @@ path (the oracle) on the host cores on a bounded sample of the workload.
 `--workload streamed` (1 GPU, not the default line) times the decode with a
 slot cache per layer and misses filled from pinned host memory, with the
 cache decisions on the device (`--remap device`) or on the host with a round
-trip per layer (`--remap host`); see streamed_main.
+trip per layer (`--remap host`); see streamed_main. `--workload slots`
+(1 GPU) times small decode batches over slot pools whose routed experts are
+all resident (`--model gpt-oss` or `iq4nl-256e`); see slots_main.
 """
 import argparse
 import json
@@ -54,16 +56,22 @@ def parse():
                     help="expert-parallel exchange: NVLink peer-memory kernels or NCCL all-to-all")
     ap.add_argument("--eager", action="store_true",
                     help="launch every kernel from the host instead of replaying CUDA graphs")
-    ap.add_argument("--workload", default="resident", choices=["resident", "streamed"],
+    ap.add_argument("--workload", default="resident", choices=["resident", "streamed", "slots"],
                     help="resident: every expert in HBM (the default line); streamed: a slot "
-                         "cache per layer with misses filled from pinned host memory (1 GPU)")
+                         "cache per layer with misses filled from pinned host memory (1 GPU); "
+                         "slots: small decode batches over slot pools (1 GPU, --model)")
+    ap.add_argument("--model", default="gpt-oss", choices=["gpt-oss", "iq4nl-256e"],
+                    help="slots: gpt-oss layers (MXFP4, 32 of 128 experts, top-4) or a "
+                         "256-expert IQ4_NL model (hidden 2048, expert FFN 512, 64 slots, top-8)")
     ap.add_argument("--slots", type=int, default=32, help="streamed: slots per layer")
     ap.add_argument("--remap", default="device", choices=["device", "host"],
                     help="streamed: cache decisions on the device (one CUDA graph per step) or "
                          "on the host with a round trip per layer")
     args = ap.parse_args()
-    if args.workload == "streamed" and "--tokens" not in sys.argv:
+    if args.workload in ("streamed", "slots") and "--tokens" not in sys.argv:
         args.tokens = 1
+    if args.workload == "slots" and args.model == "iq4nl-256e" and "--layers" not in sys.argv:
+        args.layers = 40
     return args
 
 
@@ -472,8 +480,117 @@ def streamed_main(args):
     return 0
 
 
+def slots_main(args):
+    """--workload slots: a decode batch of --tokens tokens through --layers
+    MoE layers whose routed experts are all resident in slot pools (the
+    reference's decode configurations of a slot cache that hits): gpt-oss
+    layers (MXFP4 2880 x 2880 gate, up and down, 32 slots, top-4) or a
+    256-expert IQ4_NL model (hidden 2048, expert FFN 512, 64 slots, top-8).
+    Weights quantized on the device from N(0, 0.02); ids are top_k distinct
+    random slots per token, new every step and layer. One CUDA graph per step;
+    the roofline counts each distinct referenced slot's bytes once per
+    layer."""
+    import torch
+
+    from moestream_b200 import ops
+    if args.model == "gpt-oss":
+        wtype, K, n_ff, NS, top_k = "mxfp4", SHAPE["hidden"], SHAPE["n_ff"], 32, 4
+    else:
+        wtype, K, n_ff, NS, top_k = "iq4_nl", 2048, 512, 64, 8
+    T, L = args.tokens, args.layers
+    t_setup = time.time()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(77)
+
+    def qpool(kk, nn):
+        pool = ops.SlotPool(wtype, kk, nn, NS, max_fill_batch=8)
+        for j0 in range(0, NS, 8):
+            wts = torch.randn(8 * nn, kk, generator=g, device="cuda") * 0.02
+            q = ops.quantize_rows(wtype, wts).view(8, -1)
+            pool.fill(list(range(j0, j0 + 8)), [q[i] for i in range(8)])
+        return pool
+    layers = [(qpool(K, n_ff), qpool(K, n_ff), qpool(n_ff, K)) for _ in range(L)]
+    S = args.warmup + args.steps
+    ids_all = torch.rand(S, L, T, NS, generator=g, device="cuda").argsort(dim=-1)[..., :top_k]
+    ids_all = ids_all.to(torch.int32).contiguous()
+    w = torch.full((T, top_k), 1.0 / top_k, device="cuda")
+    x = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
+    y = torch.empty(L, T, K, dtype=torch.float32, device="cuda")
+    route = ops.RouteBuffers(T * top_k, NS)
+    ws = ops.workspace(max(K, n_ff), T, top_k, NS)
+    ids_d = torch.empty(L, T, top_k, dtype=torch.int32, device="cuda")
+    eb = sum(p.expert_bytes for p in layers[0])
+    lib = ops.lib()
+
+    def step():
+        for il in range(L):
+            r = ops.remap_group(ids_d[il], NS, route=route)
+            ga, up, dn = layers[il]
+            ops.moe_ffn(ga, up, dn, x, r, w, top_k, ws=ws, out=y[il])
+    for s_ in range(args.warmup):
+        ids_d.copy_(ids_all[s_])
+        step()
+    torch.cuda.synchronize()
+    c0 = int(lib.msb_kernel_launches())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    launches = (int(lib.msb_kernel_launches()) - c0) * args.steps
+    graph.replay()
+    torch.cuda.synchronize()
+    t_setup = time.time() - t_setup
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    time.sleep(0.05)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for i in range(args.steps):
+        ids_d.copy_(ids_all[args.warmup + i])
+        graph.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    timed = ids_all[args.warmup:].view(args.steps * L, T * top_k).cpu()
+    distinct = sum(len(torch.unique(row)) for row in timed)
+    gbs = distinct * eb / (ms / 1e3) / 1e9
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    line = {"metric": "MoE-FFN decode tokens/s over slot pools", "impl": "msb",
+            "value": T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "us_per_layer": ms * 1e3 / args.steps / L,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "mxfp4xe2m1->f32" if wtype == "mxfp4" else "iq4_nlxq8->f32",
+            "data": "synthetic",
+            "config": {"workload": f"{args.model} MoE FFN decode over {NS}-slot pools, every "
+                                   "referenced expert resident",
+                       "n_layer": L, "slots": NS, "hidden": K, "n_ff": n_ff, "top_k": top_k,
+                       "tokens": T, "distinct_per_layer": distinct / (args.steps * L),
+                       "l2": "random slots every step and layer; pools far larger than L2"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                         "frac": gbs / hbm, "traffic": None,
+                         "kernel": "whole step (algorithmic expert bytes / step time)",
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
+            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk,
+            "setup_s": round(t_setup, 1)}
+    print(json.dumps(line), flush=True)
+    graph = None
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "slots":
+        if args.gpus != 1 or args.impl != "msb":
+            print(json.dumps({"workload": "slots", "unavailable": "one GPU, --impl msb only"}))
+            return 0
+        return slots_main(args)
     if args.workload == "streamed":
         if args.gpus != 1 or args.impl != "msb":
             print(json.dumps({"workload": "streamed", "unavailable": "one GPU, --impl msb only"}))

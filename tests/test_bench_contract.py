@@ -21,3 +21,8 @@ def _run(*args, timeout=600):
 def test_streamed_workload_is_one_gpu_only():
     d = _run("--workload", "streamed", "--gpus", "2")
     assert d["workload"] == "streamed" and "unavailable" in d
+
+
+def test_slots_workload_is_one_gpu_only():
+    d = _run("--workload", "slots", "--gpus", "4")
+    assert d["workload"] == "slots" and "unavailable" in d
