@@ -227,14 +227,23 @@ int msb_mul_mat_id_noalloc(msb_pool_t pool, const void *b_dev, int b_type,
                            const msb_route_t *route, int32_t top_k,
                            int32_t n_tok, float *res_dev, void *stream);
 
-/* Status bits of the tensor-core kernels on the current device: nonzero
- * when a kernel's bounded wait (about one second) on its own pipeline gave
- * up, in which case that kernel stopped early and its outputs are
- * incomplete (1 producer, 2 accumulator release, 4 stage arrival,
- * 8 accumulator arrival, 16 teardown drain). Kernels only set bits; call
- * after synchronizing the streams that ran them. clear != 0 resets the
- * word. No counterpart in the reference (ggml's CPU matmul has no waits). */
+/* Status bits of the library's kernels on the current device: nonzero when
+ * a kernel's bounded wait (the wait limit, one second by default; see
+ * MSB_OPT_WAIT_LIMIT_US) gave up, in which case that kernel stopped early
+ * and its outputs are incomplete. Tensor-core pipeline: 1 producer,
+ * 2 accumulator release, 4 stage arrival, 8 accumulator arrival, 16 teardown
+ * drain; expert-parallel exchange: 32 rows from the peers, 64 results from
+ * the peers. Kernels only set bits; call after synchronizing the streams
+ * that ran them. clear != 0 resets the word. No counterpart in the
+ * reference (ggml's CPU matmul has no waits; its remap fails safe to the
+ * zero slot instead, src/llama-moestream.cpp:1913-1928). */
 int msb_device_status(int32_t *status, int32_t clear);
+
+/* Synchronizes `stream` (the host blocks) and reports the device status
+ * word: MSB_OK when every bounded wait completed, MSB_ERR_TIMEOUT (with a
+ * message naming the waits) when one gave up; clear != 0 then resets the
+ * word so that later calls report only new timeouts. */
+int msb_stream_check(void *stream, int32_t clear);
 
 /* ======================================================================== */
 /* MoE FFN layer                                                              */
@@ -380,14 +389,20 @@ int msb_ep_moe_ffn_peers(const msb_ep_peers_t *peers, msb_pool_t gate,
 /* Measurement hooks                                                          */
 /* ======================================================================== */
 
-/* Options (msb_set_option). MSB_OPT_MXFP4_PATH selects the arithmetic of
- * MXFP4 mul_mat_id: 0 (default) = tensor cores (tcgen05 block-scaled FP4,
- * activations as four e2m1 terms per 32-element block) wherever the shapes
- * allow (K a multiple of 64; gate/up views starting on 128-row boundaries),
- * the CUDA-core path otherwise; 1 = the CUDA-core path everywhere (int8
- * activations per 32-element block with an fp16 scale, ggml's q8_0 form).
- * Process-wide. */
+/* Options (msb_set_option), process-wide.
+ * MSB_OPT_MXFP4_PATH selects the arithmetic of MXFP4 mul_mat_id: 0 (default)
+ * = tensor cores (tcgen05 block-scaled FP4, activations as four e2m1 terms
+ * per 32-element block) wherever the shapes allow (K a multiple of 64; an up
+ * view starting on a 32-row boundary), the CUDA-core path otherwise; 1 = the
+ * CUDA-core path everywhere (int8 activations per 32-element block with an
+ * fp16 scale, ggml's q8_0 form).
+ * MSB_OPT_WAIT_LIMIT_US sets how long every bounded device wait (tensor-core
+ * pipeline barriers, expert-parallel flags) spins before it gives up and
+ * sets its status bit: 1 .. 60,000,000 microseconds, default 1,000,000. It
+ * applies to launches set up after the call (a captured CUDA graph keeps the
+ * limit it was captured with). */
 #define MSB_OPT_MXFP4_PATH 1
+#define MSB_OPT_WAIT_LIMIT_US 2
 int msb_set_option(int option, int value);
 
 /* Kernels this library has launched in this process (all threads). */

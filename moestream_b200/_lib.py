@@ -18,6 +18,7 @@ TYPE_MXFP4 = 39
 ORIGIN_DEMAND, ORIGIN_PREFETCH_HIGH, ORIGIN_PREFETCH_LOW, ORIGIN_SWEEP = 0, 1, 2, 3
 NO_SLOT = 0xFFFFFFFF
 OPT_MXFP4_PATH = 1
+OPT_WAIT_LIMIT_US = 2
 ROUTER_SOFTMAX_TOPK, ROUTER_SOFTMAX_ALL = 0, 1
 
 c_i32p = ctypes.POINTER(ctypes.c_int32)
@@ -120,6 +121,7 @@ SIGNATURES = {
                                               ctypes.POINTER(Route), ctypes.c_int32,
                                               ctypes.c_int32, c_vp, c_vp]),
     "msb_device_status": (ctypes.c_int, [c_i32p, ctypes.c_int32]),
+    "msb_stream_check": (ctypes.c_int, [c_vp, ctypes.c_int32]),
     "msb_moe_ffn": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, c_vp, c_vp, ctypes.c_int,
                                    ctypes.c_int64, ctypes.POINTER(Route), c_vp, ctypes.c_int32,
                                    ctypes.c_int32, c_vp, c_vp, c_vp, ctypes.c_int64, c_vp]),

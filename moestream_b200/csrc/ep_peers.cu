@@ -217,6 +217,7 @@ inline FlagWait phase_wait(const Layout &L, int ph, int *status) {
   w.n = L.n_rank;
   w.status = status;
   w.bit = 32 << ph;
+  w.limit_ns = wait_limit_ns();
   return w;
 }
 

@@ -21,6 +21,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "msb_internal.h"
@@ -46,6 +47,10 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
 // MXFP4 arithmetic: 0 = tensor cores where the shapes allow, 1 = CUDA cores
 // with int8 activations (ggml's q8_0 form) everywhere.
 static int g_mxfp4_path = 0;
+
+// Bound of every device wait, in nanoseconds (MSB_OPT_WAIT_LIMIT_US).
+static std::atomic<int64_t> g_wait_ns{1000000000};
+int64_t wait_limit_ns() { return g_wait_ns.load(); }
 
 static constexpr int kThreads = 256;
 static constexpr int kWarps = kThreads / 32;
@@ -460,6 +465,12 @@ extern "C" int msb_set_option(int option, int value) {
     g_mxfp4_path = value;
     return MSB_OK;
   }
+  if (option == MSB_OPT_WAIT_LIMIT_US) {
+    MSB_CHECK_ARG(value >= 1 && value <= 60000000,
+                  "msb_set_option: wait limit must be 1 .. 60000000 microseconds");
+    g_wait_ns.store(int64_t(value) * 1000);
+    return MSB_OK;
+  }
   return fail(MSB_ERR_INVALID, "msb_set_option: unknown option %d", option);
 }
 
@@ -484,8 +495,6 @@ extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, in
     // Tensor cores: activation terms per pair (grouped order), then one
     // projection writing res directly.
     uint8_t *act = ws;
-    const size_t es = b_type == MSB_TYPE_BF16 ? 2 : 4;
-    (void)es;
     if (int rc = tc_act_terms(b_dev, b_type, b_ne1, b_nb1, b_nb2, top_k, route->rows, pairs,
                               pool->nb, act, st))
       return rc;
@@ -548,7 +557,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
   const int64_t pairs = int64_t(n_tok) * top_k;
   const int max_active_tc = int(pairs < gate->n_slot + 1 ? pairs : gate->n_slot + 1);
   const bool tc = g_mxfp4_path == 0 && tc_supported(gate) && tc_supported(up) &&
-                  tc_supported(down) && n_ff % 64 == 0 && up_row0 % 128 == 0;
+                  tc_supported(down) && n_ff % 64 == 0 && up_row0 % 32 == 0;
   if (rows && !tc)
     return fail(MSB_ERR_UNSUPPORTED, "msb_moe_ffn: row targets need the tensor-core path");
   if (tc) {
@@ -597,9 +606,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
   ActQ8 xq = carve_act(ws, &off, n_tok, gate->nb);
   ActQ8 hq = carve_act(ws, &off, pairs, n_ff / 32);
   float *rdown = w_dev ? reinterpret_cast<float *>(ws + off) : y_dev;
-  const int elt = x_type == MSB_TYPE_BF16 ? 2 : 4;
   if (int rc = quantize_act(x_dev, x_type, 1, x_nb1, x_nb1, n_tok, xq, st)) return rc;
-  (void)elt;
   const int max_active = int(pairs < gate->n_slot + 1 ? pairs : gate->n_slot + 1);
 
   GemvArgs g{};

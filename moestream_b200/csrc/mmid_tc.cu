@@ -42,13 +42,15 @@
 // item is also one of up to 4 segments of the K chunks: the epilogue stores
 // f32 partial sums and split_reduce_kernel adds the segments in order and
 // runs the epilogue (every CTA derives the same split from the route).
-// Every mbarrier wait is bounded (about a second); a wait that gives up sets
+// Every mbarrier wait is bounded (the library's wait limit, one second by
+// default); a wait that gives up sets
 // a bit of the device status word (msb_device_status) and the CTA stops
 // issuing work, waits (bounded) for its copies and MMAs in flight and
 // releases its tensor memory.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <cstdio>
 #include <mutex>
 
 #include "msb_internal.h"
@@ -77,7 +79,12 @@ struct Cfg {
   static constexpr int kCtasPerSm = 2;
   static constexpr int kStages = NV == 2 ? 5 : 8;
   static constexpr int kA = NV * kChunk * 2048;          // 128 rows x 16 B per block
-  static constexpr int kSFA = NV * 512;
+  // Scale factors of a weight view: one 512-byte chunk per 128-row tile of
+  // the pool. A view whose first row is not on a tile boundary (the up half
+  // of a fused gate_up tensor, rows from N/2) spans two chunks per window;
+  // with two views there is room for both.
+  static constexpr int kSfaView = NV == 2 ? 1024 : 512;
+  static constexpr int kSFA = NV * kSfaView;
   static constexpr int kBPass = kChunk * kN * 16;        // [block][pair][term] 16 B rows
   static constexpr int kB = kBPass;
   static constexpr int kSFB = 512;                       // [pair][term] 16 B rows
@@ -107,7 +114,8 @@ struct Args {
   const uint8_t *pool[2];    // slot 0 of each view's pool
   int64_t slot_stride[2], N[2];
   int64_t nb;                // blocks per row (K / 32), same for both views
-  int64_t row0[2];           // first row of each view, multiple of 128
+  int64_t row0[2];           // first row of each view: a multiple of 128, or of 32
+                             // for view 1 of a two-view launch
   int64_t n_out;             // rows per view
   int tiles;                 // ceil(n_out / 128)
   const int32_t *counts, *offsets, *rows, *active;
@@ -129,6 +137,7 @@ struct Args {
   float *part;
   int *split_word;
   const int32_t *slot_ids;   // slot of each pair (split reduce)
+  long long wait_ns;         // bound of every mbarrier wait (wait_limit_ns)
 };
 
 __device__ __forceinline__ float *out_row(const RowTarget &t, int64_t r) {
@@ -409,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
         const int64_t lo = seg * n_chunks / split, hi = (seg + 1) * n_chunks / split;
         for (int64_t i = lo; i < hi; ++i, ++it) {
           const int s = it % kStages;
-          if (!sm100::mbar_wait_bounded(&empty[s], ((it / kStages) & 1) ^ 1)) {
+          if (!sm100::mbar_wait_bounded(&empty[s], ((it / kStages) & 1) ^ 1, a.wait_ns)) {
             atomicOr(&g_status, kStatusProducer);
             *abort_v = 1;
             break;
@@ -418,8 +427,16 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
           uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
           const int64_t b0 = i * kChunk;
           // Full boxes are counted (rows or blocks outside the tensors
-          // arrive as zeros).
-          sm100::mbar_expect_tx(&full[s], uint32_t(C::kStage));
+          // arrive as zeros); a window off the tile grid also takes the next
+          // tile's scale chunk when the pool has one.
+          bool next_sf[NV];
+          uint32_t tx = uint32_t(C::kA + C::kB + C::kSFB);
+          for (int v = 0; v < NV; ++v) {
+            const int64_t r0 = a.row0[v] + item.n0;
+            next_sf[v] = NV == 2 && (r0 & 127) != 0 && (r0 >> 7) + 1 < (a.N[v] + 127) / 128;
+            tx += next_sf[v] ? 1024u : 512u;
+          }
+          sm100::mbar_expect_tx(&full[s], tx);
           for (int v = 0; v < NV; ++v) {
             const int64_t r0 = a.row0[v] + item.n0;
             sm100::tma_3d(sA + v * kChunk * 2048, &a.tm_w[v], int(r0) * 2, int(b0), slot,
@@ -427,8 +444,9 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
             const uint8_t *slot_base = a.pool[v] + int64_t(slot) * a.slot_stride[v];
             const uint8_t *sf_base = slot_base + a.nb * a.N[v] * 16;
             const int64_t sf_tiles = (a.N[v] + 127) / 128;
-            sm100::bulk_g2s(sSFA + v * 512, sf_base + (i * sf_tiles + (r0 >> 7)) * 512, 512,
-                            &full[s]);
+            const uint8_t *chunk = sf_base + (i * sf_tiles + (r0 >> 7)) * 512;
+            sm100::bulk_g2s(sSFA + v * C::kSfaView, chunk, 512, &full[s]);
+            if (next_sf[v]) sm100::bulk_g2s(sSFA + v * C::kSfaView + 512, chunk + 512, 512, &full[s]);
           }
           sm100::tma_3d(sB, &a.tm_aq, pos * 8, int(b0), 0, &full[s]);
           sm100::tma_3d(sSFB, &a.tm_asf, pos * 8, int(i), 0, &full[s]);
@@ -437,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
       // No copy may still be landing in shared memory when the CTA exits
       // (only possible after an abort): wait for the last stages issued.
       for (uint32_t k = it > uint32_t(kStages) ? it - kStages : 0; k < it; ++k)
-        if (!sm100::mbar_wait_bounded(&full[k % kStages], (k / kStages) & 1))
+        if (!sm100::mbar_wait_bounded(&full[k % kStages], (k / kStages) & 1, a.wait_ns))
           atomicOr(&g_status, kStatusDrain);
     }
   } else if (warp <= 3) {
@@ -446,62 +464,94 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
     // (about 0.4 us per stage), so several warps issue: with two views each
     // of warps 1-2 takes one (gate, up); with one view warps 1-3 take the
     // stages in turn, each into its own accumulator, added by the epilogue.
+    // The whole warp runs the loop (every lane waits on the barriers, so all
+    // see the staged bytes); lane 0 issues the tensor-core instructions.
     const int m = warp - 1;
-    if (lane == 0 && m < C::kMma) {
+    if (m < C::kMma) {
       uint32_t it = 0, acc = 0;
       int cur = 0;
-      for (int64_t w = blockIdx.x; w < n_work && !*abort_v; w += gridDim.x) {
+      const int v = NV == 2 ? m : 0;
+      // Scale rows of a view that starts `shift` 32-row groups into a tile:
+      // window row 32q + l is pool tile row 32(shift + q) + l, in the next
+      // tile's chunk once shift + q reaches 4.
+      const int shift = NV == 2 ? int((a.row0[v] & 127) >> 5) : 0;
+      for (int64_t w = blockIdx.x; w < n_work && !__shfl_sync(0xffffffffu, *abort_v, 0);
+           w += gridDim.x) {
         const int64_t wi = w / split, seg = w - wi * split;
         const Item item = locate(a, item0, wi, cur);
         if (item.slot == a.zero_slot) continue;
         const int64_t lo = seg * n_chunks / split, hi = (seg + 1) * n_chunks / split;
         const int buf = acc % kBufs;
-        if (!sm100::mbar_wait_bounded(&acc_empty[buf], ((acc / kBufs) & 1) ^ 1)) {
-          atomicOr(&g_status, kStatusAccEmpty);
-          *abort_v = 1;
+        if (!__all_sync(0xffffffffu,
+                        sm100::mbar_wait_bounded(&acc_empty[buf], ((acc / kBufs) & 1) ^ 1, a.wait_ns))) {
+          if (lane == 0) {
+            atomicOr(&g_status, kStatusAccEmpty);
+            *abort_v = 1;
+          }
           break;
         }
         sm100::tc_fence_after();
         const uint32_t d0 = tmem + buf * C::kAccCols + m * kN;
-        const int v = NV == 2 ? m : 0;
+        const int64_t r0 = a.row0[v] + item.n0;
+        const bool has_next = (r0 >> 7) + 1 < (a.N[v] + 127) / 128;
         bool first = true;
         for (int64_t i = lo; i < hi; ++i, ++it) {
           if (NV == 1 && i % C::kMma != m) continue;   // another warp's stage
           const int s = it % kStages;
-          if (!sm100::mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
-            atomicOr(&g_status, kStatusFull);
-            *abort_v = 1;
+          if (!__all_sync(0xffffffffu, sm100::mbar_wait_bounded(&full[s], (it / kStages) & 1, a.wait_ns))) {
+            if (lane == 0) {
+              atomicOr(&g_status, kStatusFull);
+              *abort_v = 1;
+            }
             break;
           }
-          const uint8_t *st = smem + s * C::kStage;
-          const uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
-          const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols + (NV == 2 ? m * 8 : 0);
-          sm100::tmem_cp_32x128b_x4(sf_col,
-                                    sm100::smem_desc(sm100::smem_u32(sSFA + v * 512), 0, 128));
-          sm100::tmem_cp_32x128b_x4(sf_col + 4,
-                                    sm100::smem_desc(sm100::smem_u32(sSFB), 0, 128));
-          const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
-          for (int j = 0; j < kbn / 2; ++j) {
-            const uint32_t sel = uint32_t(2 * j);
-            // B: 32 stacked rows of 16 B per block; K-halves one block apart.
-            const uint64_t bdesc =
-                sm100::smem_desc(sm100::smem_u32(sB + 2 * j * (kN * 16)), kN * 16, 128);
-            const uint64_t adesc =
-                sm100::smem_desc(sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
-            sm100::mma_mxf4(d0, adesc, bdesc, sm100::idesc_mxf4(kN, sel, sel),
-                            sf_col | (sel << 30), (sf_col + 4) | (sel << 30),
-                            (first && j == 0) ? 0u : 1u);
+          uint8_t *st = smem + s * C::kStage;
+          uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
+          uint8_t *sfa_v = sSFA + v * C::kSfaView;
+          if (shift) {
+            // Reassemble the window's chunk in place: lane l owns 16-byte
+            // row l of both staged chunks (words = 32-row groups).
+            const uint4 c0 = *reinterpret_cast<const uint4 *>(sfa_v + lane * 16);
+            uint4 c1 = make_uint4(0u, 0u, 0u, 0u);   // rows past the pool: scale 2^-127
+            if (has_next) c1 = *reinterpret_cast<const uint4 *>(sfa_v + 512 + lane * 16);
+            const uint4 o = shift == 1   ? make_uint4(c0.y, c0.z, c0.w, c1.x)
+                            : shift == 2 ? make_uint4(c0.z, c0.w, c1.x, c1.y)
+                                         : make_uint4(c0.w, c1.x, c1.y, c1.z);
+            *reinterpret_cast<uint4 *>(sfa_v + lane * 16) = o;
+            sm100::fence_proxy_async_smem();
           }
+          __syncwarp();
+          if (lane == 0) {
+            const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols + (NV == 2 ? m * 8 : 0);
+            sm100::tmem_cp_32x128b_x4(sf_col, sm100::smem_desc(sm100::smem_u32(sfa_v), 0, 128));
+            sm100::tmem_cp_32x128b_x4(sf_col + 4,
+                                      sm100::smem_desc(sm100::smem_u32(sSFB), 0, 128));
+            const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
+            for (int j = 0; j < kbn / 2; ++j) {
+              const uint32_t sel = uint32_t(2 * j);
+              // B: 32 stacked rows of 16 B per block; K-halves one block apart.
+              const uint64_t bdesc =
+                  sm100::smem_desc(sm100::smem_u32(sB + 2 * j * (kN * 16)), kN * 16, 128);
+              const uint64_t adesc =
+                  sm100::smem_desc(sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
+              sm100::mma_mxf4(d0, adesc, bdesc, sm100::idesc_mxf4(kN, sel, sel),
+                              sf_col | (sel << 30), (sf_col + 4) | (sel << 30),
+                              (first && j == 0) ? 0u : 1u);
+            }
+            sm100::tc_commit(&empty[s]);
+          }
+          __syncwarp();
           first = false;
-          sm100::tc_commit(&empty[s]);
         }
-        sm100::tc_commit(&acc_full[buf]);
+        if (lane == 0) sm100::tc_commit(&acc_full[buf]);
         ++acc;
       }
       // Every MMA and scale-factor copy is complete before tensor memory is
       // released.
-      sm100::tc_commit(drained);
-      if (!sm100::mbar_wait_bounded(drained, 0)) atomicOr(&g_status, kStatusDrain);
+      if (lane == 0) {
+        sm100::tc_commit(drained);
+        if (!sm100::mbar_wait_bounded(drained, 0, a.wait_ns)) atomicOr(&g_status, kStatusDrain);
+      }
     }
   } else {
     // ---- epilogue (warps 4-7) ----
@@ -546,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
       }
       const uint32_t a_i = acc++;
       const int buf = a_i % kBufs;
-      if (!sm100::mbar_wait_bounded(&acc_full[buf], (a_i / kBufs) & 1)) {
+      if (!sm100::mbar_wait_bounded(&acc_full[buf], (a_i / kBufs) & 1, a.wait_ns)) {
         atomicOr(&g_status, kStatusAccFull);
         *abort_v = 1;
         break;
@@ -742,6 +792,7 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   a.rows = route->rows;
   a.active = route->active;
   a.zero_slot = pool->n_slot;
+  a.wait_ns = wait_limit_ns();
   if (pool->n_slot + 1 > tc::kMaxActive)
     return fail(MSB_ERR_UNSUPPORTED, "tensor-core path: %d slots exceed %d", pool->n_slot,
                 tc::kMaxActive - 1);
@@ -816,6 +867,23 @@ int status_word(int **out) {
   return MSB_OK;
 }
 }  // namespace msb
+
+extern "C" int msb_stream_check(void *stream, int32_t clear) {
+  MSB_CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int32_t v = 0;
+  if (int rc = msb_device_status(&v, clear)) return rc;
+  if (v == 0) return MSB_OK;
+  static const char *names[] = {"tensor-core producer", "accumulator release", "stage arrival",
+                                "accumulator arrival", "teardown drain",
+                                "expert-parallel rows", "expert-parallel results"};
+  char buf[256];
+  int n = 0;
+  for (int b = 0; b < 7; ++b)
+    if (v & (1 << b))
+      n += snprintf(buf + n, sizeof(buf) - size_t(n), "%s%s", n ? ", " : "", names[b]);
+  if (n == 0) snprintf(buf, sizeof(buf), "unknown");
+  return msb::fail(MSB_ERR_TIMEOUT, "a bounded device wait gave up (status 0x%x: %s)", v, buf);
+}
 
 extern "C" int msb_device_status(int32_t *status, int32_t clear) {
   MSB_CHECK_ARG(status, "msb_device_status: null status");

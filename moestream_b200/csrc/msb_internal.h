@@ -25,10 +25,15 @@ void count_launch(int n = 1);
 // set by kernels whose bounded waits gave up; msb_device_status reads it).
 int status_word(int **out);
 
+// How long a bounded device wait spins before it gives up, in nanoseconds
+// (MSB_OPT_WAIT_LIMIT_US; one second by default). Read when a launch is set
+// up, so a captured CUDA graph keeps the limit it was captured with.
+int64_t wait_limit_ns();
+
 // An optional wait at the start of a kernel for flags that other GPUs raise
 // (expert-parallel exchange): threads 0..n-1 of every CTA spin, bounded
-// (~1 s), until flags[t] reached *seq * mult, then the CTA synchronizes. A wait
-// that gives up sets `bit` in *status. n == 0: no wait.
+// (limit_ns), until flags[t] reached *seq * mult, then the CTA synchronizes. A
+// wait that gives up sets `bit` in *status. n == 0: no wait.
 struct FlagWait {
   const uint32_t *flags = nullptr;
   const uint32_t *seq = nullptr;
@@ -36,6 +41,7 @@ struct FlagWait {
   int n = 0;
   int *status = nullptr;
   int bit = 0;
+  long long limit_ns = 1000000000ll;
 };
 
 // Where a projection's f32 result rows go when they are not one contiguous
@@ -109,12 +115,15 @@ __device__ __forceinline__ void flag_wait_block(const FlagWait &w) {
   if (int(threadIdx.x) < w.n) {
     const uint32_t seq = *reinterpret_cast<const volatile uint32_t *>(w.seq) * w.mult;
     const uint32_t *f = w.flags + threadIdx.x;
-    const long long t0 = clock64();
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     for (;;) {
       uint32_t v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
       if (int32_t(v - seq) >= 0) break;
-      if (clock64() - t0 > (1ll << 31)) { ok = false; break; }
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > uint64_t(w.limit_ns)) { ok = false; break; }
     }
   }
   if (!ok) atomicOr(w.status, w.bit);

@@ -49,17 +49,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase of `parity` for at most ~`limit` SM clock cycles
-// (default about one second); false if it gave up. try_wait suspends the
-// thread in hardware between checks, so waiting warps take no issue slots.
+// Nanoseconds of the GPU's global timer (wall time, independent of the SM
+// clock).
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase of `parity` for at most `limit_ns` nanoseconds (the
+// library's wait limit, one second unless msb_set_option changed it); false
+// if it gave up. try_wait suspends the thread in hardware between checks, so
+// waiting warps take no issue slots.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
-                                                  long long limit = (1ll << 31)) {
+                                                  long long limit_ns) {
   if (mbar_test_wait(bar, parity)) return true;
-  const long long t0 = clock64();
+  const uint64_t t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > limit) return false;
+    if (globaltimer_ns() - t0 > uint64_t(limit_ns)) return false;
   }
   return true;
+}
+
+// Makes this thread's ordinary shared-memory stores visible to the async
+// proxy (TMA, tcgen05.cp and the MMA's operand reads) that reads them next.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---- bulk copy global -> shared (completes transaction bytes on `bar`) -----

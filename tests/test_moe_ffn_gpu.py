@@ -3,7 +3,7 @@ combine) against the CPU oracle, for separate gate/up tensors and for a
 fused gate_up tensor whose first N_ff rows are the gate.
 
 MXFP4 layers whose shapes allow it (K and N_ff multiples of 64, the up rows
-starting on a 128-row boundary) run on the tensor cores with activations as
+starting on a 32-row boundary) run on the tensor cores with activations as
 four e2m1 terms; the rest, and every layer with the q8 option, on the CUDA
 cores with int8 activations (ggml's q8_0 form).
 Tolerances (max |got - want| / max |want|):
@@ -66,7 +66,8 @@ def build_layer(wtype, K, n_ff, n_expert, n_slot, fused, seed):
 
 CASES = [
     # wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, fused
-    ("mxfp4", 2880, 2880, 6, 4, 2, 4, True),     # gpt-oss widths, fused gate_up (CUDA cores)
+    ("mxfp4", 2880, 2880, 6, 4, 2, 4, True),     # gpt-oss widths, fused gate_up (up half off
+                                                 # the 128-row tile grid)
     ("mxfp4", 2880, 2880, 6, 4, 3, 4, False),    # gpt-oss widths, separate gate and up
     ("iq4_nl", 2048, 512, 10, 8, 8, 8, False),   # 256-expert model widths
     ("mxfp4", 512, 256, 8, 8, 40, 4, True),      # several passes per slot
@@ -102,7 +103,7 @@ def test_moe_ffn_matches_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, 
     up = slabs["gate"] if fused else slabs["up"]
     kw = dict(up_row0=n_ff if fused else 0)
     tc = (path == "tc" and wtype == "mxfp4" and K % 64 == 0 and n_ff % 64 == 0 and
-          (not fused or n_ff % 128 == 0))
+          (not fused or n_ff % 32 == 0))
     mode = "e2m1x4" if tc else "q8"
     y_f, h_f = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
                          mode=mode, **kw)
@@ -181,3 +182,38 @@ def test_unknown_activation_is_refused():
         with pytest.raises(MsbError, match="activation"):
             ops.moe_ffn(pools["gate"], pools["up"], pools["down"], x, r, None, 1,
                         activation=bad)
+
+
+@pytest.mark.parametrize("n_ff,pad", [(256, 32), (256, 96), (320, 0), (256, 64)])
+def test_up_view_off_the_tile_grid(n_ff, pad):
+    """A gate_up tensor whose up rows start 32, 64 or 96 rows into a 128-row
+    tile (up_row0 = n_ff + pad, pad rows unused): the tensor cores take the
+    up view's scale factors from two tiles. With n_ff = 320 the last window
+    has no second tile in the pool."""
+    from moestream_b200 import ops
+    wtype, K, n_expert, n_slot, n_tok, top_k = "mxfp4", 512, 6, 5, 20, 4
+    rows = 2 * n_ff + pad
+    up_row0 = n_ff + pad
+    gu = experts(wtype, n_expert, K, rows, seed=rows)
+    dn = experts(wtype, n_expert, n_ff, K, seed=rows + 1)
+    p_gu = ops.SlotPool(wtype, K, rows, n_slot)
+    p_dn = ops.SlotPool(wtype, n_ff, K, n_slot)
+    for p, m in ((p_gu, gu), (p_dn, dn)):
+        p.fill(list(range(n_slot)), [torch.from_numpy(m[e]).pin_memory() for e in range(n_slot)])
+    rng = np.random.default_rng(n_ff + pad)
+    x = rng.normal(0, 1, size=(n_tok, K)).astype(np.float32)
+    ids_e, w = topk_ids(rng, n_tok, n_expert, top_k)   # expert n_slot is not resident
+    table = np.full(n_expert, -1, dtype=np.int32)
+    table[:n_slot] = np.arange(n_slot)
+    slots = O.remap_table(ids_e, table, n_slot)
+    r = ops.remap_group(torch.from_numpy(ids_e).cuda(), n_slot,
+                        table=torch.from_numpy(table).cuda(), n_expert=n_expert)
+    act = torch.empty(n_tok, top_k, n_ff, dtype=torch.float32, device="cuda")
+    y = ops.moe_ffn(p_gu, p_gu, p_dn, torch.from_numpy(x).cuda(), r, torch.from_numpy(w).cuda(),
+                    top_k, up_row0=up_row0, act=act)
+    torch.cuda.synchronize()
+    pad_slab = lambda m: np.concatenate([m[:n_slot], np.zeros((1, m.shape[1]), np.uint8)])
+    y_f, h_f = O.moe_ffn(wtype, pad_slab(gu), pad_slab(gu), pad_slab(dn), K, n_ff, x, slots, w,
+                         mode="e2m1x4", up_row0=up_row0)
+    assert O.max_abs_normalized(act.cpu().numpy(), h_f) < 1e-4
+    assert O.max_abs_normalized(y.cpu().numpy(), y_f) < 1e-3

@@ -6,7 +6,9 @@ the library instead of from the caller.
 
 Called through the C ABI and compared with msb_mul_mat_id (caller-provided
 workspace) on two calls in a row with different inputs, so that the second
-call runs over the first call's leftovers in the shared array. Tolerances
+call runs over the first call's leftovers in the shared array. The 1- and
+2-token cases split K over idle CTAs, so their partial sums and the split
+word also live in the shared array. Tolerances
 are those of tests/test_mul_mat_id_gpu.py for the path each weight type
 takes. This file is collected last on purpose.
 """
@@ -38,6 +40,8 @@ def _call_noalloc(L, pool, b, route, top_k, out):
 
 @pytest.mark.parametrize("wtype,K,N,n_expert,n_slot,n_tok,top_k", [
     ("mxfp4", 2880, 512, 16, 12, 64, 4),     # gpt-oss hidden width, decode batch
+    ("mxfp4", 2880, 2880, 16, 12, 1, 4),     # 4 pairs: K split over idle CTAs, the
+    ("mxfp4", 2880, 2880, 16, 12, 2, 4),     # partial sums in the shared array too
     ("iq4_nl", 2048, 256, 12, 8, 16, 8),
 ])
 def test_noalloc_matches_mul_mat_id_twice(wtype, K, N, n_expert, n_slot, n_tok, top_k):
@@ -64,6 +68,8 @@ def test_noalloc_matches_mul_mat_id_twice(wtype, K, N, n_expert, n_slot, n_tok, 
         torch.cuda.synchronize()
         err = O.max_abs_normalized(got.cpu().numpy(), want.cpu().numpy())
         assert err < TOL[wtype], (call, err)
+        # Same kernels, same split over K, same summation order: the same bits.
+        assert torch.equal(got, want), call
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch():
