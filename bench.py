@@ -19,7 +19,8 @@ finds its weights in cache.
 through the public API with host buffers: the step's activations and routing
 copied from pinned host memory and every layer's output read back, inside
 the timed region. `--impl reference` times the CPU restatement of the same
-path (the oracle) on the host cores on a bounded sample of the workload.
+path (the oracle's vectorized form of ggml's q8_0 mul_mat_id) on all host
+threads, every layer of every step.
 
 `--workload streamed` (1 GPU, not the default line) times the decode with a
 slot cache per layer and misses filled from pinned host memory, with the
@@ -237,9 +238,19 @@ def run_layer(ctx, layer, x, ids, w, y, timed_events=None):
     ep.layer(x, ids, w, local_ffn, y, pools=(ga, up, dn, 0, ctx["ws"]))
 
 
-def cpu_sample(layer0, tokens, top_k, K, n_ff, n_expert, ids0, w0, x0, threads):
-    """Times the oracle (CPU restatement, q8 arithmetic) on one layer of the
-    step; returns seconds per layer (best of 2)."""
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_sample(layer0, top_k, K, n_ff, n_expert, ids_step, w_step, x0, threads):
+    """Times the CPU baseline (the oracle's vectorized q8 restatement of
+    ggml's CPU path, all host threads) on one whole step: every layer's
+    routing of the step, each layer over layer 0's weights as read back from
+    the GPU's pools (the bytes the GPU read; 1.7 GB, far larger than the host
+    caches). Returns seconds per step (best of 2)."""
     import numpy as np
 
     from oracle import oracle as O
@@ -251,8 +262,9 @@ def cpu_sample(layer0, tokens, top_k, K, n_ff, n_expert, ids0, w0, x0, threads):
     best = None
     for _ in range(2):
         t0 = time.perf_counter()
-        O.moe_ffn("mxfp4", gu_h, gu_h, dn_h, K, n_ff, x0, ids0, w0, mode="q8", up_row0=n_ff,
-                  up_rows=2 * n_ff, nthreads=threads)
+        for il in range(ids_step.shape[0]):
+            O.moe_ffn_fast("mxfp4", gu_h, gu_h, dn_h, K, n_ff, x0, ids_step[il], w_step[il],
+                           up_row0=n_ff, nthreads=threads)
         dt = time.perf_counter() - t0
         best = dt if best is None else min(best, dt)
     return best
@@ -261,7 +273,47 @@ def cpu_sample(layer0, tokens, top_k, K, n_ff, n_expert, ids0, w0, x0, threads):
 # ---------------------------------------------------------------------------
 # Reference arm: the CPU restatement on the host cores
 # ---------------------------------------------------------------------------
+def reference_weight_sets(n_sets, n_base, K, n_ff, E, threads, seed=0):
+    """n_sets distinct slot slabs of one layer (fused gate_up [E + 1, 2 x 2880
+    rows] and down [E + 1, 2880 rows], ggml MXFP4 bytes, slot E the zero
+    slot). Every slot holds its own copy of one of n_base experts per role
+    quantized from N(0, 0.02) by the oracle's quantizer (gguf's MXFP4
+    algorithm, the same as the GPU arm's device quantizer)."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    w_gu = rng.normal(0.0, 0.02, size=(n_base * 2 * n_ff, K)).astype(np.float32)
+    w_dn = rng.normal(0.0, 0.02, size=(n_base * K, n_ff)).astype(np.float32)
+
+    def q(a):   # quantize row chunks in parallel (the C call releases the GIL)
+        parts = np.array_split(a, threads * 4)
+        with ThreadPoolExecutor(threads) as ex:
+            return np.concatenate(list(ex.map(lambda c: O.quantize("mxfp4", c), parts)))
+    base_gu = q(w_gu).reshape(n_base, -1)
+    base_dn = q(w_dn).reshape(n_base, -1)
+    del w_gu, w_dn
+    sets = []
+    for s in range(n_sets):
+        gu = np.empty((E + 1, base_gu.shape[1]), np.uint8)
+        dn = np.empty((E + 1, base_dn.shape[1]), np.uint8)
+        for e in range(E):
+            b = (7 * e + 3 * s) % n_base
+            gu[e] = base_gu[b]
+            dn[e] = base_dn[b]
+        gu[E] = 0
+        dn[E] = 0
+        sets.append((gu, dn))
+    return sets
+
+
 def reference_arm(args, world, rank):
+    """The reference's CPU implementation of this path is ggml's CPU
+    mul_mat_id (q8_0 activations, int8 block dots), which is not vendored;
+    its published algorithm is restated by the oracle (msb_cpu_fast.c,
+    vectorized like ggml's x86 code) and timed here on all host threads over
+    the whole step: every one of the 36 layers, each with its own routing."""
     if rank != 0:
         return 0
     import numpy as np
@@ -269,48 +321,56 @@ def reference_arm(args, world, rank):
     from oracle import oracle as O
     K, n_ff, E, top_k = SHAPE["hidden"], SHAPE["n_ff"], SHAPE["n_expert"], SHAPE["top_k"]
     T, L = args.tokens, args.layers
-    threads = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    # One layer's weights per step sample: N(0, 0.02) experts quantized by the
-    # oracle's quantizer would take minutes on the host, so the sample uses
-    # MXFP4 blocks with uniform nibbles and scale exponents 118-120 (the range
-    # N(0, 0.02) weights quantize to). Timing does not depend on the values.
-    def slab(rows, cols):
-        nb = cols // 32
-        a = rng.integers(0, 256, size=(E + 1, rows * nb, 17), dtype=np.uint8)
-        a[:, :, 0] = rng.integers(118, 121, size=(E + 1, rows * nb), dtype=np.uint8)
-        a[E] = 0
-        return a.reshape(E + 1, -1)
-    gu, dn = slab(2 * n_ff, K), slab(K, n_ff)
+    threads = host_threads()
+    t_setup = time.time()
+    # Layer l reads weight set l % n_sets: each set (1.7 GB) is far larger
+    # than the host caches, so no layer finds its weights cached, while the
+    # host holds 4 sets instead of 36.
+    n_sets, n_base = min(L, 4), 4
+    sets = reference_weight_sets(n_sets, n_base, K, n_ff, E, threads)
+    rng = np.random.default_rng(1)
+    S = args.warmup + args.steps
+    logits = rng.normal(0, 1, size=(S, L, T, E))
+    ids = np.argsort(-logits, axis=-1, kind="stable")[..., :top_k].astype(np.int32)
+    sel = np.take_along_axis(logits, ids, -1)
+    w = np.exp(sel - sel.max(-1, keepdims=True))
+    w = (w / w.sum(-1, keepdims=True)).astype(np.float32)
+    del logits, sel
+    # bf16-valued activations, as the GPU arm's
+    x = rng.normal(0, 1, size=(S, T, K)).astype(np.float32)
+    x = (x.view(np.uint32) & 0xFFFF0000).view(np.float32)
+    t_setup = time.time() - t_setup
     times = []
-    for step in range(args.warmup + args.steps):
-        logits = rng.normal(0, 1, size=(T, E))
-        ids = np.argsort(-logits, axis=1)[:, :top_k].astype(np.int32)
-        sel = np.take_along_axis(logits, ids, 1)
-        w = np.exp(sel - sel.max(1, keepdims=True))
-        w = (w / w.sum(1, keepdims=True)).astype(np.float32)
-        x = rng.normal(0, 1, size=(T, K)).astype(np.float32)
+    for step in range(S):
         t0 = time.perf_counter()
-        O.moe_ffn("mxfp4", gu, gu, dn, K, n_ff, x, ids, w, mode="q8", up_row0=n_ff,
-                  up_rows=2 * n_ff, nthreads=threads)
+        for il in range(L):
+            gu, dn = sets[il % n_sets]
+            O.moe_ffn_fast("mxfp4", gu, gu, dn, K, n_ff, x[step], ids[step, il], w[step, il],
+                           up_row0=n_ff, nthreads=threads)
         dt = time.perf_counter() - t0
         if step >= args.warmup:
-            times.append(dt * L)  # one layer sampled, the step has L layers
+            times.append(dt)
     step_s = sum(times) / len(times)
     v = T / step_s
+    macs = 3 * n_ff * K * T * top_k * L
+    sample = (f"every step whole: {L} layers x {T} tokens x top-{top_k} ({macs / 1e9:.0f} GMAC); "
+              f"{threads} threads, {O.fast_isa()} int8 dots; weights: {n_sets} sets of 128 "
+              f"MXFP4 experts from N(0,0.02), layer l reads set l % {n_sets}; CPU "
+              "restatement of ggml's q8_0 mul_mat_id (ggml is not available offline)")
     line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "mxfp4xq8->f32", "data": "synthetic", "impl": "reference",
+            "dtype": "mxfp4 x q8_0 (int8 dots) -> f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": "gpt-oss-120b-shaped MoE FFN decode, all experts resident",
                        "n_layer": L, "n_expert": E, "hidden": K, "n_ff": n_ff,
                        "top_k": top_k, "tokens": T},
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": f"1 of {L} layers per step ({T} tokens), scaled x{L}; "
-                                       "CPU restatement of ggml's q8_0 vec_dot (ggml is not "
-                                       "available offline)"},
+                             "nproc": os.cpu_count(), "isa": O.fast_isa(),
+                             "gmac_per_s_per_core": macs / step_s / threads / 1e9,
+                             "sample": sample},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+                    "d2h_bytes_per_step": 0},
+            "setup_s": round(t_setup, 1)}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -459,7 +519,7 @@ def streamed_main(args):
             "value": T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "mxfp4xe2m1->f32", "data": "synthetic",
+            "dtype": "mxfp4 x bf16 as 4 e2m1 terms per 32-block -> f32", "data": "synthetic",
             "config": {"workload": "gpt-oss-120b-shaped MoE FFN decode, slot cache per layer, "
                                    "misses filled from pinned host memory",
                        "n_layer": L, "n_expert": E, "slots_per_layer": NS, "hidden": K,
@@ -566,7 +626,7 @@ def slots_main(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "us_per_layer": ms * 1e3 / args.steps / L,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "mxfp4xe2m1->f32" if wtype == "mxfp4" else "iq4_nlxq8->f32",
+            "dtype": "mxfp4 x bf16 as 4 e2m1 terms per 32-block -> f32" if wtype == "mxfp4" else "iq4_nl x q8_0 -> f32",
             "data": "synthetic",
             "config": {"workload": f"{args.model} MoE FFN decode over {NS}-slot pools, every "
                                    "referenced expert resident",
@@ -773,21 +833,23 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        threads = os.cpu_count() or 1
+        from oracle import oracle as O
+        threads = host_threads()
         s = args.warmup
-        ids0 = ids_np[s, 0]
-        w0 = w_all[s, 0].cpu().numpy()
-        x0 = xs[s].float().cpu().numpy()
-        t_layer = cpu_sample(layers[0], T, top_k, K, n_ff, E, ids0, w0, x0, threads)
-        cpu = {"value": T / (t_layer * L), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"layer 0 of step {s} ({T} tokens), best of 2, scaled x{L} layers; CPU "
-                         "restatement of ggml's q8_0 vec_dot (ggml is not available offline)"}
+        t_step = cpu_sample(layers[0], top_k, K, n_ff, E, ids_np[s], w_all[s].cpu().numpy(),
+                            xs[s].float().cpu().numpy(), threads)
+        cpu = {"value": T / t_step, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "nproc": os.cpu_count(), "isa": O.fast_isa(),
+               "sample": f"step {s} whole ({L} layers x {T} tokens, each layer's own routing), "
+                         "every layer over layer 0's weights read back from the GPU pools, "
+                         "best of 2; CPU restatement of ggml's q8_0 mul_mat_id, vectorized "
+                         "(ggml is not available offline)"}
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "mxfp4xe2m1->f32", "data": "synthetic",
+                "dtype": "mxfp4 x bf16 as 4 e2m1 terms per 32-block -> f32", "data": "synthetic",
                 "config": {"workload": "gpt-oss-120b-shaped MoE FFN decode, all experts resident"
                                        + (", expert-parallel" if world > 1 else ""),
                            "n_layer": L, "n_expert": E, "hidden": K, "n_ff": n_ff,

@@ -66,6 +66,13 @@ def orc():
         L.orc_f32_to_f16.restype = ctypes.c_uint16
         L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
         L.orc_f16_to_f32.restype = ctypes.c_float
+        L.orc_moe_ffn_fast.argtypes = [ctypes.c_int, _u8p, ctypes.c_int64, _u8p, ctypes.c_int64,
+                                       ctypes.c_int64, _u8p, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_int64, _f32p, _i32p, _f32p, ctypes.c_int,
+                                       ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                       ctypes.c_float, _f32p, ctypes.c_int]
+        L.orc_fast_isa.restype = ctypes.c_int
+        L.orc_fast_set_isa.argtypes = [ctypes.c_int]
         _orc = L
     return _orc
 
@@ -287,6 +294,41 @@ def moe_ffn(wtype, gate, up, down, K, n_ff, x, ids, w, mode="exact", up_row0=0, 
                            _p(h, _f32p), nthreads or os.cpu_count() or 1)
     assert rc == 0, rc
     return y, h
+
+
+FAST_ISA = {0: "scalar", 1: "avx2", 2: "avx512-vnni"}
+
+
+def fast_isa(force=None):
+    """Instruction set of the vectorized CPU baseline ("avx512-vnni", "avx2"
+    or "scalar"); force an index to compare them (-1 restores detection)."""
+    if force is not None:
+        orc().orc_fast_set_isa(force)
+    return FAST_ISA[orc().orc_fast_isa()]
+
+
+def moe_ffn_fast(wtype, gate, up, down, K, n_ff, x, ids, w, up_row0=0, nthreads=None, act=None):
+    """The FFN in ggml's q8 form, vectorized and threaded (msb_cpu_fast.c):
+    the timed CPU baseline. Arguments as moe_ffn; returns y [T, K]. Works on
+    views of the slabs without copying them (each a C-contiguous uint8 array
+    [n_slots, bytes])."""
+    t = TYPES.get(wtype, wtype)
+    for a in (gate, up, down):
+        assert a.dtype == np.uint8 and a.flags["C_CONTIGUOUS"]
+    row_bytes = (K // 32) * BLOCK_BYTES[t]
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    T, top_k = ids.shape
+    y = np.empty((T, K), dtype=np.float32)
+    rc = orc().orc_moe_ffn_fast(t, _p(gate, _u8p), gate.shape[1] // row_bytes, _p(up, _u8p),
+                                up.shape[1] // row_bytes, up_row0, _p(down, _u8p), K, n_ff,
+                                gate.shape[0], _p(x, _f32p), _p(ids, _i32p), _p(w, _f32p), top_k,
+                                T, 1 if act else 0, act[0] if act else 1.0,
+                                act[1] if act else 0.0, _p(y, _f32p),
+                                nthreads or os.cpu_count() or 1)
+    assert rc == 0, rc
+    return y
 
 
 def group(slot_ids, n_slot):

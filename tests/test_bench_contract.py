@@ -26,3 +26,20 @@ def test_streamed_workload_is_one_gpu_only():
 def test_slots_workload_is_one_gpu_only():
     d = _run("--workload", "slots", "--gpus", "4")
     assert d["workload"] == "slots" and "unavailable" in d
+
+
+def test_reference_arm_times_every_layer_of_every_step():
+    """--impl reference: the CPU restatement over whole steps (all layers),
+    one JSON line with the contract's keys; the time it claims fits in the
+    wall time it took."""
+    import time
+    t0 = time.time()
+    d = _run("--impl", "reference", "--layers", "2", "--steps", "2", "--warmup", "1",
+             "--tokens", "8")
+    wall = time.time() - t0
+    assert d["impl"] == "reference" and d["unit"] == "tokens/s" and d["value"] > 0
+    assert d["config"]["n_layer"] == 2 and d["config"]["tokens"] == 8
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    assert "every step whole: 2 layers" in d["cpu_baseline"]["sample"]
+    assert d["e2e"]["h2d_bytes_per_step"] == 0
+    assert d["steps"] * d["ms_per_step"] / 1e3 < wall
