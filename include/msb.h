@@ -259,6 +259,10 @@ int msb_stream_check(void *stream, int32_t clear);
  * 1, in which case y = r (the expert outputs, no weighting);
  * y: f32 [K, n_tok].
  * act_dev (optional, may be NULL): f32 [N_ff, top_k, n_tok] receives a.
+ * Rows routed to the zero slot contribute exactly 0. With router weights the
+ * weighted sum runs in the down projection's epilogue (no separate combine
+ * kernel), over k in increasing order with one f32 fused multiply-add per k,
+ * so y does not depend on which CTA finishes last.
  * Composition restated from research/spikes/s1_real_expert_stream/main.c:
  * 186-209 and research/spikes/s4_sweep_math/main.c:89-92. */
 int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0,
@@ -273,7 +277,7 @@ int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0,
  * y = clamp(u, -limit, limit), h = x * sigmoid(alpha * x) * (y + 1)
  * (llama.cpp's swiglu_oai, alpha 1.702 and limit 7 for gpt-oss; the
  * reference's spikes use plain SwiGLU and the reference itself leaves the
- * activation to llama.cpp). Expert biases are not applied. */
+ * activation to llama.cpp). Expert biases: msb_moe_ffn_ex. */
 #define MSB_ACT_SILU        0
 #define MSB_ACT_SWIGLU_OAI  1
 typedef struct {
@@ -289,6 +293,33 @@ int msb_moe_ffn_act(msb_pool_t gate, msb_pool_t up, int64_t up_row0,
                     int32_t top_k, int32_t n_tok, float *y_dev, float *act_dev,
                     const msb_ffn_act_t *act, void *workspace,
                     int64_t workspace_bytes, void *stream);
+
+/* Expert biases of one MoE FFN layer (gpt-oss's ffn_{gate,up,down}_exps.bias:
+ * f32 [n_expert][rows] in device memory), indexed by the router's expert id
+ * as llama.cpp's add_id does, so a bias follows its expert to whatever slot
+ * the remap gives it (the reference rewrites only the ids passed to
+ * mul_mat_id, src/apply.py:100-140, and leaves the bias lookup on the
+ * expert ids). Each is added to the f32 matmul result of every pair not
+ * routed to the zero slot (before the activation for gate and up, before
+ * the router weighting for down); pairs routed to the zero slot stay exactly
+ * 0, and ids outside [0, n_expert) add no bias. A NULL row pointer skips
+ * that projection's bias. For a fused gate_up bias [n_expert][2 N_ff]:
+ * gate_b = base, up_b = base + up_row0, both lds 2 N_ff. */
+typedef struct {
+  const float *gate_b, *up_b, *down_b;  /* row of expert e at ptr + e * ld  */
+  int64_t gate_ld, up_ld, down_ld;      /* floats between experts' rows     */
+  const int32_t *ids;                   /* router ids [top_k, n_tok] (device) */
+  int64_t ids_nb0, ids_nb1;             /* byte strides of ids              */
+  int32_t n_expert;
+} msb_ffn_bias_t;
+
+/* msb_moe_ffn_act with optional expert biases (NULL: none). */
+int msb_moe_ffn_ex(msb_pool_t gate, msb_pool_t up, int64_t up_row0,
+                   msb_pool_t down, const void *x_dev, int x_type,
+                   int64_t x_nb1, const msb_route_t *route, const float *w_dev,
+                   int32_t top_k, int32_t n_tok, float *y_dev, float *act_dev,
+                   const msb_ffn_act_t *act, const msb_ffn_bias_t *bias,
+                   void *workspace, int64_t workspace_bytes, void *stream);
 
 /* ======================================================================== */
 /* Expert parallelism (packing around the all-to-all exchanges)               */

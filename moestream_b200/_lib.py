@@ -68,6 +68,13 @@ class FfnActCfg(ctypes.Structure):
     _fields_ = [("kind", ctypes.c_int), ("alpha", ctypes.c_float), ("limit", ctypes.c_float)]
 
 
+class FfnBiasCfg(ctypes.Structure):
+    _fields_ = [("gate_b", c_vp), ("up_b", c_vp), ("down_b", c_vp), ("gate_ld", ctypes.c_int64),
+                ("up_ld", ctypes.c_int64), ("down_ld", ctypes.c_int64), ("ids", c_vp),
+                ("ids_nb0", ctypes.c_int64), ("ids_nb1", ctypes.c_int64),
+                ("n_expert", ctypes.c_int32)]
+
+
 class Route(ctypes.Structure):
     _fields_ = [("slot_ids", c_vp), ("counts", c_vp), ("offsets", c_vp),
                 ("rows", c_vp), ("active", c_vp)]
@@ -129,6 +136,11 @@ SIGNATURES = {
                                        ctypes.c_int64, ctypes.POINTER(Route), c_vp,
                                        ctypes.c_int32, ctypes.c_int32, c_vp, c_vp,
                                        ctypes.POINTER(FfnActCfg), c_vp, ctypes.c_int64, c_vp]),
+    "msb_moe_ffn_ex": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int64, c_vp, c_vp, ctypes.c_int,
+                                      ctypes.c_int64, ctypes.POINTER(Route), c_vp,
+                                      ctypes.c_int32, ctypes.c_int32, c_vp, c_vp,
+                                      ctypes.POINTER(FfnActCfg), ctypes.POINTER(FfnBiasCfg),
+                                      c_vp, ctypes.c_int64, c_vp]),
     "msb_ep_dispatch": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_int32, c_vp, ctypes.c_int64,

@@ -1,5 +1,6 @@
-// mul_mat_id over the slot pool, the fused SwiGLU variant, the router-weighted
-// combine, and the MoE FFN layer built from them.
+// mul_mat_id over the slot pool, the fused SwiGLU variant, and the MoE FFN
+// layer built from them (the router-weighted combine runs in the down
+// projection's epilogue: Combine in msb_internal.h).
 //
 // Operator contract (ggml_mul_mat_id; call sites research/spikes/
 // s0_slot_slab/main.c:117-148, s6_arena_mulmatid/main.c:82-134):
@@ -37,12 +38,14 @@ int64_t tc_act_bytes(int64_t nb, int64_t rows);
 int64_t tc_split_bytes(int64_t n_out_max, int64_t n_pairs);
 int tc_supported(const msb_pool_s *p);
 int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb2, int32_t top_k,
-                 const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st);
+                 const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st,
+                 uint32_t *zero = nullptr, int64_t zero_n = 0);
 int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
                   uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st,
                   const RowTarget *res_rows = nullptr, const FfnAct *fa = nullptr,
-                  uint8_t *split_ws = nullptr, int64_t split_bytes = 0);
+                  uint8_t *split_ws = nullptr, int64_t split_bytes = 0,
+                  const FfnBias *bias = nullptr, const Combine *comb = nullptr);
 
 // MXFP4 arithmetic: 0 = tensor cores where the shapes allow, 1 = CUDA cores
 // with int8 activations (ggml's q8_0 form) everywhere.
@@ -91,9 +94,11 @@ __device__ __forceinline__ void store_q8_block(ActQ8 out, int64_t row, int64_t b
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) quantize_act_kernel(
-    const char *b, int64_t nb1, int64_t nb2, int64_t ne1, int64_t n_rows, ActQ8 out) {
+    const char *b, int64_t nb1, int64_t nb2, int64_t ne1, int64_t n_rows, ActQ8 out,
+    uint32_t *zero, int64_t zero_n) {
   pdl_wait();
   pdl_trigger();
+  grid_zero(zero, zero_n);   // the call's combine counters
   const int lane = threadIdx.x & 31;
   const int64_t item = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5);
   if (item >= n_rows * out.nb) return;
@@ -119,6 +124,8 @@ struct GemvArgs {
   ActQ8 out;         // SWIGLU: quantized silu(g) * u, nb = n_out / 32
   float *act;        // SWIGLU, optional: f32 silu(g) * u [pair * n_out + n]
   FfnAct fa;         // SWIGLU: the activation
+  FfnBias bias;      // expert biases (view 0, and view 1 with SWIGLU)
+  Combine comb;      // plain: the fused router-weighted combine (optional)
 };
 
 template <int WT>
@@ -264,8 +271,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
         a.out.q[(pair * a.out.nb + tile) * 32 + lane] = 0;
         if (lane == 0) a.out.d[pair * a.out.nb + tile] = 0.f;
         if (a.act && valid) a.act[pair * a.n_out + n] = 0.f;
-      } else if (valid) {
-        a.res[pair * a.n_out + n] = 0.f;
+      } else {
+        if (valid) a.res[pair * a.n_out + n] = 0.f;
+        combine_arrive(a.comb, pair, 1, tile, lane);
       }
     }
     return;
@@ -317,29 +325,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
         tot[v] = s;
       }
       const int64_t pair = prs[c0 + r];
+      if (valid) {
+        if (const float *br = bias_row(a.bias, 0, pair)) tot[0] += br[n];
+        if constexpr (SWIGLU)
+          if (const float *br = bias_row(a.bias, 1, pair)) tot[NV - 1] += br[n];
+      }
       if constexpr (SWIGLU) {
         const float g = tot[0], up = tot[1];
         float h = valid ? ffn_act(a.fa, g, up) : 0.f;
         if (a.act && valid) a.act[pair * a.n_out + n] = h;
         store_q8_block(a.out, pair, tile, h, lane);
-      } else if (valid) {
-        a.res[pair * a.n_out + n] = tot[0];
+      } else {
+        if (valid) a.res[pair * a.n_out + n] = tot[0];
+        combine_arrive(a.comb, pair, 1, tile, lane);
       }
     }
   }
-}
-
-// y[t, n] = sum_k w[k, t] * r[n, k, t], k in increasing order.
-__global__ void combine_kernel(const float *r, const float *w, int32_t top_k, int64_t N,
-                               int64_t n_tok, float *y) {
-  pdl_wait();
-  pdl_trigger();
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= N * n_tok) return;
-  const int64_t t = i / N, n = i - t * N;
-  float s = 0.f;
-  for (int k = 0; k < top_k; ++k) s = fmaf(w[t * top_k + k], r[(t * top_k + k) * N + n], s);
-  y[i] = s;
 }
 
 // ---------------------------------------------------------------------------
@@ -359,17 +360,18 @@ static ActQ8 carve_act(uint8_t *ws, int64_t *off, int64_t n_rows, int64_t nb) {
 }
 
 static int quantize_act(const void *b, int b_type, int64_t b_ne1, int64_t b_nb1, int64_t b_nb2,
-                        int64_t n_rows, ActQ8 out, cudaStream_t st) {
+                        int64_t n_rows, ActQ8 out, cudaStream_t st, uint32_t *zero = nullptr,
+                        int64_t zero_n = 0) {
   const int64_t items = n_rows * out.nb;
   if (items == 0) return MSB_OK;
   const int64_t grid = (items + kWarps - 1) / kWarps;
   const char *p = static_cast<const char *>(b);
   if (b_type == MSB_TYPE_F32)
     MSB_CUDA_TRY(launch_pdl(quantize_act_kernel<float>, dim3(unsigned(grid)), dim3(kThreads), 0, st,
-                            p, b_nb1, b_nb2, b_ne1, n_rows, out));
+                            p, b_nb1, b_nb2, b_ne1, n_rows, out, zero, zero_n));
   else if (b_type == MSB_TYPE_BF16)
     MSB_CUDA_TRY(launch_pdl(quantize_act_kernel<__nv_bfloat16>, dim3(unsigned(grid)), dim3(kThreads),
-                            0, st, p, b_nb1, b_nb2, b_ne1, n_rows, out));
+                            0, st, p, b_nb1, b_nb2, b_ne1, n_rows, out, zero, zero_n));
   else
     return fail(MSB_ERR_INVALID, "activation type %d is not F32 or BF16", b_type);
   count_launch();
@@ -437,22 +439,31 @@ extern "C" void msb_time_next_gate_up(void *start, void *stop) {
   g_gate_up_stop = static_cast<cudaEvent_t>(stop);
 }
 
+// Words of the fused combine's counters: one per (token, 32-row block of the
+// output width).
+static int64_t combine_words(int64_t n_tok, int64_t n_out) { return n_tok * ((n_out + 31) / 32); }
+
 extern "C" int64_t msb_workspace_bytes(int64_t K_max, int32_t n_tok, int32_t top_k, int32_t n_slot) {
   (void)n_slot;
   if (K_max <= 0 || K_max % 32 || n_tok < 0 || top_k <= 0) return -1;
   const int64_t nb = K_max / 32, pairs = int64_t(n_tok) * top_k;
-  // CUDA-core path: int8 activations in and SwiGLU out, down result.
+  const int64_t cnt = align_up(combine_words(n_tok, K_max) * 4, 256);
+  // CUDA-core path: int8 activations in and SwiGLU out, down result, the
+  // combine's counters.
   int64_t q8 = 0;
   q8 = align_up(q8 + pairs * nb * 32, 256);
   q8 = align_up(q8 + pairs * nb * 4, 256);
   q8 = align_up(q8 + pairs * nb * 32, 256);
   q8 = align_up(q8 + pairs * nb * 4, 256);
   q8 = align_up(q8 + pairs * K_max * 4, 256);
-  // Tensor-core path: activation terms in and SwiGLU out, down result.
+  q8 += cnt;
+  // Tensor-core path: activation terms in and SwiGLU out, down result, the
+  // combine's counters.
   int64_t tcb = 0;
   tcb = align_up(tcb + tc_act_bytes(nb, pairs), 256);
   tcb = align_up(tcb + tc_act_bytes(nb, pairs), 256);
   tcb = align_up(tcb + pairs * K_max * 4, 256);
+  tcb += cnt;
   // Split over K of small batches: partial sums (the largest projection
   // mul_mat_id serves has 2 K_max rows: a fused gate_up).
   tcb = align_up(tcb + tc_split_bytes(2 * K_max, pairs), 256);
@@ -521,13 +532,35 @@ extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, in
   return launch_gemv(pool->wtype, false, g, max_active, st);
 }
 
+// Internal bias views of one FFN call: gate/up (views 0 and 1) and down.
+static void split_bias(const msb_ffn_bias_t *b, int32_t top_k, FfnBias *gu, FfnBias *dn) {
+  *gu = FfnBias{};
+  *dn = FfnBias{};
+  if (!b) return;
+  FfnBias base;
+  base.ids = reinterpret_cast<const char *>(b->ids);
+  base.nb0 = b->ids_nb0;
+  base.nb1 = b->ids_nb1;
+  base.top_k = top_k;
+  base.n_expert = b->n_expert;
+  *gu = base;
+  gu->b[0] = b->gate_b;
+  gu->ld[0] = b->gate_ld;
+  gu->b[1] = b->up_b;
+  gu->ld[1] = b->up_ld;
+  *dn = base;
+  dn->b[0] = b->down_b;
+  dn->ld[0] = b->down_ld;
+}
+
 // msb_moe_ffn; with `rows` the down projection stores its result rows there
 // instead of y (top_k 1, no weights, tensor-core shapes only).
 static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
                         const void *x_dev, int x_type, int64_t x_nb1, const msb_route_t *route,
                         const float *w_dev, int32_t top_k, int32_t n_tok, float *y_dev,
                         float *act_dev, void *workspace, int64_t workspace_bytes,
-                        const RowTarget *rows, void *stream, const FfnAct &fa) {
+                        const RowTarget *rows, void *stream, const FfnAct &fa,
+                        const msb_ffn_bias_t *bias) {
   MSB_CHECK_ARG(fa.kind == 0 || (fa.kind == 1 && fa.limit > 0.f),
                 "msb_moe_ffn: unknown activation %d (or limit <= 0)", fa.kind);
   MSB_CHECK_ARG(gate && up && down && route && (y_dev || rows) && workspace,
@@ -536,6 +569,9 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
   MSB_CHECK_ARG(w_dev || top_k == 1, "msb_moe_ffn: router weights may be omitted only for top_k 1");
   MSB_CHECK_ARG(x_dev || n_tok == 0, "msb_moe_ffn: null x");
   MSB_CHECK_ARG(top_k > 0 && n_tok >= 0, "msb_moe_ffn: bad shape");
+  MSB_CHECK_ARG(!bias || ((bias->ids || n_tok == 0) && bias->n_expert > 0 &&
+                          (bias->gate_b || bias->up_b || bias->down_b)),
+                "msb_moe_ffn: biases need the router's expert ids, n_expert > 0 and a bias row");
   const int64_t n_ff = down->K;
   MSB_CHECK_ARG(gate->wtype == up->wtype && up->wtype == down->wtype,
                 "msb_moe_ffn: gate, up and down must share a weight type");
@@ -555,35 +591,52 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   const int64_t pairs = int64_t(n_tok) * top_k;
-  const int max_active_tc = int(pairs < gate->n_slot + 1 ? pairs : gate->n_slot + 1);
+  FfnBias bias_gu, bias_dn;
+  split_bias(bias, top_k, &bias_gu, &bias_dn);
+  const int max_active = int(pairs < gate->n_slot + 1 ? pairs : gate->n_slot + 1);
   const bool tc = g_mxfp4_path == 0 && tc_supported(gate) && tc_supported(up) &&
                   tc_supported(down) && n_ff % 64 == 0 && up_row0 % 32 == 0;
   if (rows && !tc)
     return fail(MSB_ERR_UNSUPPORTED, "msb_moe_ffn: row targets need the tensor-core path");
+  // With router weights the down projection's epilogue also combines: its
+  // result rows go to the workspace and y is written by the last warp to
+  // store each (token, 32-row block); without them (top_k 1) it writes y.
+  const int64_t cnt_n = w_dev ? combine_words(n_tok, down->N) : 0;
+  Combine comb;
   if (tc) {
     // Tensor cores: x terms per pair -> fused gate/up + SwiGLU writing the
-    // down projection's terms -> down projection -> weighted combine.
+    // down projection's terms -> down projection with the combine.
     int64_t o = 0;
     uint8_t *xa = ws + o;
     o = align_up(o + tc_act_bytes(gate->nb, pairs), 256);
     uint8_t *ha = ws + o;
     o = align_up(o + tc_act_bytes(n_ff / 32, pairs), 256);
-    // Without router weights (top_k 1) the down projection writes y itself.
     float *rd = w_dev ? reinterpret_cast<float *>(ws + o) : y_dev;
     o = align_up(o + pairs * down->N * 4, 256);
+    uint32_t *cnt = reinterpret_cast<uint32_t *>(ws + o);
+    o += align_up(cnt_n * 4, 256);
+    if (w_dev) {
+      comb.w = w_dev;
+      comb.y = y_dev;
+      comb.r = rd;
+      comb.cnt = cnt;
+      comb.top_k = top_k;
+      comb.n_out = down->N;
+      comb.nblk = (down->N + 31) / 32;
+    }
     // The rest: scratch for the split over K of small batches (gate/up and
     // down use it one after the other).
     uint8_t *split_ws = ws + o;
     const int64_t split_bytes = workspace_bytes - o;
     if (int rc = tc_act_terms(x_dev, x_type, 1, x_nb1, x_nb1, top_k, route->rows, pairs, gate->nb,
-                              xa, st))
+                              xa, st, w_dev ? cnt : nullptr, cnt_n))
       return rc;
     const int64_t rows_gu[2] = {0, up_row0};
     const msb_pool_s *gu_pools[2] = {gate, up};
     const bool timed = g_gate_up_start && g_gate_up_stop;
     if (timed) MSB_CUDA_TRY(record_timing_event(g_gate_up_start, st));
     if (int rc = tc_projection(gu_pools, 2, rows_gu, n_ff, route, pairs, xa, nullptr, ha, act_dev,
-                               max_active_tc, st, nullptr, &fa, split_ws, split_bytes))
+                               max_active, st, nullptr, &fa, split_ws, split_bytes, &bias_gu))
       return rc;
     if (timed) {
       MSB_CUDA_TRY(record_timing_event(g_gate_up_stop, st));
@@ -591,23 +644,27 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
     }
     const int64_t rows_dn[2] = {0, 0};
     const msb_pool_s *dn_pools[2] = {down, down};
-    if (int rc = tc_projection(dn_pools, 1, rows_dn, down->N, route, pairs, ha, rd, nullptr, nullptr,
-                               max_active_tc, st, rows, nullptr, split_ws, split_bytes))
-      return rc;
-    if (!w_dev) return MSB_OK;
-    const int64_t total = down->N * n_tok;
-    MSB_CUDA_TRY(launch_pdl(combine_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, st,
-                            rd, w_dev, top_k, down->N, int64_t(n_tok), y_dev));
-    count_launch();
-    MSB_CUDA_TRY(cudaGetLastError());
-    return MSB_OK;
+    return tc_projection(dn_pools, 1, rows_dn, down->N, route, pairs, ha, rd, nullptr, nullptr,
+                         max_active, st, rows, nullptr, split_ws, split_bytes, &bias_dn, &comb);
   }
   int64_t off = 0;
   ActQ8 xq = carve_act(ws, &off, n_tok, gate->nb);
   ActQ8 hq = carve_act(ws, &off, pairs, n_ff / 32);
   float *rdown = w_dev ? reinterpret_cast<float *>(ws + off) : y_dev;
-  if (int rc = quantize_act(x_dev, x_type, 1, x_nb1, x_nb1, n_tok, xq, st)) return rc;
-  const int max_active = int(pairs < gate->n_slot + 1 ? pairs : gate->n_slot + 1);
+  off = align_up(off + pairs * down->N * 4, 256);
+  uint32_t *cnt = reinterpret_cast<uint32_t *>(ws + off);
+  if (w_dev) {
+    comb.w = w_dev;
+    comb.y = y_dev;
+    comb.r = rdown;
+    comb.cnt = cnt;
+    comb.top_k = top_k;
+    comb.n_out = down->N;
+    comb.nblk = (down->N + 31) / 32;
+  }
+  if (int rc = quantize_act(x_dev, x_type, 1, x_nb1, x_nb1, n_tok, xq, st, w_dev ? cnt : nullptr,
+                            cnt_n))
+    return rc;
 
   GemvArgs g{};
   g.w = view_of(gate, 0);
@@ -622,6 +679,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
   g.in = xq;
   g.out = hq;
   g.act = act_dev;
+  g.bias = bias_gu;
   if (int rc = launch_gemv(gate->wtype, true, g, max_active, st)) return rc;
 
   GemvArgs d{};
@@ -635,15 +693,19 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
   d.b_ne1 = top_k;
   d.in = hq;
   d.res = rdown;
-  if (int rc = launch_gemv(down->wtype, false, d, max_active, st)) return rc;
-  if (!w_dev) return MSB_OK;
+  d.bias = bias_dn;
+  d.comb = comb;
+  return launch_gemv(down->wtype, false, d, max_active, st);
+}
 
-  const int64_t total = down->N * n_tok;
-  MSB_CUDA_TRY(launch_pdl(combine_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, st,
-                          rdown, w_dev, top_k, down->N, int64_t(n_tok), y_dev));
-  count_launch();
-  MSB_CUDA_TRY(cudaGetLastError());
-  return MSB_OK;
+static FfnAct act_of(const msb_ffn_act_t *act) {
+  FfnAct fa;
+  if (act) {
+    fa.kind = act->kind;
+    fa.alpha = act->alpha;
+    fa.limit = act->limit;
+  }
+  return fa;
 }
 
 extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
@@ -651,7 +713,8 @@ extern "C" int msb_moe_ffn(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_
                            const float *w_dev, int32_t top_k, int32_t n_tok, float *y_dev,
                            float *act_dev, void *workspace, int64_t workspace_bytes, void *stream) {
   return moe_ffn_core(gate, up, up_row0, down, x_dev, x_type, x_nb1, route, w_dev, top_k, n_tok,
-                      y_dev, act_dev, workspace, workspace_bytes, nullptr, stream, FfnAct{});
+                      y_dev, act_dev, workspace, workspace_bytes, nullptr, stream, FfnAct{},
+                      nullptr);
 }
 
 extern "C" int msb_moe_ffn_act(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
@@ -660,14 +723,20 @@ extern "C" int msb_moe_ffn_act(msb_pool_t gate, msb_pool_t up, int64_t up_row0, 
                                int32_t n_tok, float *y_dev, float *act_dev,
                                const msb_ffn_act_t *act, void *workspace,
                                int64_t workspace_bytes, void *stream) {
-  FfnAct fa;
-  if (act) {
-    fa.kind = act->kind;
-    fa.alpha = act->alpha;
-    fa.limit = act->limit;
-  }
   return moe_ffn_core(gate, up, up_row0, down, x_dev, x_type, x_nb1, route, w_dev, top_k, n_tok,
-                      y_dev, act_dev, workspace, workspace_bytes, nullptr, stream, fa);
+                      y_dev, act_dev, workspace, workspace_bytes, nullptr, stream, act_of(act),
+                      nullptr);
+}
+
+extern "C" int msb_moe_ffn_ex(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
+                              const void *x_dev, int x_type, int64_t x_nb1,
+                              const msb_route_t *route, const float *w_dev, int32_t top_k,
+                              int32_t n_tok, float *y_dev, float *act_dev,
+                              const msb_ffn_act_t *act, const msb_ffn_bias_t *bias,
+                              void *workspace, int64_t workspace_bytes, void *stream) {
+  return moe_ffn_core(gate, up, up_row0, down, x_dev, x_type, x_nb1, route, w_dev, top_k, n_tok,
+                      y_dev, act_dev, workspace, workspace_bytes, nullptr, stream, act_of(act),
+                      bias);
 }
 
 int msb::moe_ffn_to_rows(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,
@@ -675,7 +744,7 @@ int msb::moe_ffn_to_rows(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_po
                          int32_t n_tok, const RowTarget &rows, void *workspace,
                          int64_t workspace_bytes, void *stream, const FfnAct &fa) {
   return moe_ffn_core(gate, up, up_row0, down, x_dev, x_type, x_nb1, route, nullptr, 1, n_tok,
-                      nullptr, nullptr, workspace, workspace_bytes, &rows, stream, fa);
+                      nullptr, nullptr, workspace, workspace_bytes, &rows, stream, fa, nullptr);
 }
 
 // ---- mul_mat_id without allocation ------------------------------------------

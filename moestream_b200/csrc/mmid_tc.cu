@@ -138,6 +138,8 @@ struct Args {
   int *split_word;
   const int32_t *slot_ids;   // slot of each pair (split reduce)
   long long wait_ns;         // bound of every mbarrier wait (wait_limit_ns)
+  FfnBias bias;              // expert biases of each view (optional)
+  Combine comb;              // one view: the fused router-weighted combine (optional)
 };
 
 __device__ __forceinline__ float *out_row(const RowTarget &t, int64_t r) {
@@ -242,9 +244,11 @@ template <typename T>
 __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t nb1, int64_t nb2,
                                                         int32_t ne1, int32_t top_k,
                                                         const int32_t *rows, int64_t n_pairs,
-                                                        int64_t nb, uint8_t *q, uint8_t *sf) {
+                                                        int64_t nb, uint8_t *q, uint8_t *sf,
+                                                        uint32_t *zero, int64_t zero_n) {
   pdl_wait();
   pdl_trigger();
+  grid_zero(zero, zero_n);   // the call's combine counters
   const int lane = threadIdx.x & 31, grp = lane >> 3, l = lane & 7;
   const int64_t nc = (nb + 3) / 4;
   const int64_t item = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
@@ -305,9 +309,13 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant
       g += a.part[((int64_t(sg) * NV) * a.a_rows + p) * a.n_out + n];
       if constexpr (NV == 2) u += a.part[((int64_t(sg) * NV + 1) * a.a_rows + p) * a.n_out + n];
     }
+    if (const float *br = bias_row(a.bias, 0, pair)) g += br[n];
+    if constexpr (NV == 2)
+      if (const float *br = bias_row(a.bias, 1, pair)) u += br[n];
   }
   if constexpr (NV == 1) {
     if (valid && !(zero && a.out.skip_zero)) out_row(a.out, pair)[n] = g;
+    combine_arrive(a.comb, pair, 1, blk, lane);
   } else {
     const float h = (!zero && valid) ? ffn_act(a.fa, g, u) : 0.f;
     if (a.act && valid) a.act[pair * a.n_out + n] = h;
@@ -582,6 +590,12 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
             if (a.act && valid) a.act[pair * a.n_out + n] = 0.f;
           }
         }
+        if constexpr (NV == 1) {
+          for (int j0 = 0; j0 < c_total; j0 += 32) {
+            const int m = min(32, c_total - j0);
+            combine_arrive(a.comb, lane < m ? a.rows[pos0 + j0 + lane] : 0, m, blk, lane);
+          }
+        }
         if constexpr (NV == 2) {
           if (blk < a.o_nb) {
             const int t = lane & 3;
@@ -656,15 +670,26 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
             continue;
           }
           if constexpr (NV == 1) {
-            if (valid) out_row(a.out, pair)[n] = gv;
+            if (valid) {
+              const float *br = bias_row(a.bias, 0, pair);
+              out_row(a.out, pair)[n] = br ? gv + br[n] : gv;
+            }
           } else {
-            const float h = valid ? ffn_act(a.fa, gv, u) : 0.f;
+            float gb = gv, ub = u;
+            if (valid) {
+              if (const float *br = bias_row(a.bias, 0, pair)) gb += br[n];
+              if (const float *br = bias_row(a.bias, 1, pair)) ub += br[n];
+            }
+            const float h = valid ? ffn_act(a.fa, gb, ub) : 0.f;
             if (a.act && valid) a.act[pair * a.n_out + n] = h;
             if (blk < a.o_nb)
               warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, pos + j), 16,
                               a.osf + a4_off(0, blk / 4, a.a_rows, pos + j) + (blk & 3), 16);
           }
         }
+        // The pass's rows of this 32-row block are stored: count them.
+        if constexpr (NV == 1)
+          if (!split_mode) combine_arrive(a.comb, lane < cc ? a.rows[pos + lane] : 0, cc, blk, lane);
       }
     }
   }
@@ -714,17 +739,19 @@ int tc_supported(const msb_pool_s *p) {
 }
 
 int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb2, int32_t top_k,
-                 const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st) {
+                 const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st,
+                 uint32_t *zero, int64_t zero_n) {
   if (n_pairs == 0) return MSB_OK;
   uint8_t *q = ws, *sf = ws + int64_t(tc::kTerms) * nb * n_pairs * 16;
   const int64_t grid = (n_pairs * ((nb + 3) / 4) + 7) / 8;
   const char *p = static_cast<const char *>(b);
   if (b_type == MSB_TYPE_F32)
     MSB_CUDA_TRY(launch_pdl(tc::act_terms_kernel<float>, dim3(unsigned(grid)), dim3(256), 0, st, p,
-                            nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, sf));
+                            nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, sf, zero, zero_n));
   else if (b_type == MSB_TYPE_BF16)
     MSB_CUDA_TRY(launch_pdl(tc::act_terms_kernel<__nv_bfloat16>, dim3(unsigned(grid)), dim3(256), 0,
-                            st, p, nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, sf));
+                            st, p, nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, sf, zero,
+                            zero_n));
   else
     return fail(MSB_ERR_INVALID, "activation type %d is not F32 or BF16", b_type);
   count_launch();
@@ -772,9 +799,11 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
                   uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st,
                   const RowTarget *res_rows, const FfnAct *fa, uint8_t *split_ws,
-                  int64_t split_bytes) {
+                  int64_t split_bytes, const FfnBias *bias, const Combine *comb) {
   const msb_pool_s *pool = pools[0];
   tc::Args a{};
+  if (bias) a.bias = *bias;
+  if (comb) a.comb = *comb;
   for (int v = 0; v < 2; ++v) {
     const msb_pool_s *p = pools[nv == 2 ? v : 0];
     if (!p->has_tmap) return fail(MSB_ERR_UNSUPPORTED, "tensor-core path: pool has no tensor map");

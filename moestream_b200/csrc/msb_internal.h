@@ -60,6 +60,36 @@ struct RowTarget {
   int32_t n_arrive = 0;
 };
 
+// The router-weighted combine fused into the down projection's epilogue:
+// y[t][n] = sum_k w[t][k] * r[t*top_k + k][n] in k order (one f32 fma per
+// k, starting from 0), where r is the projection's result rows. Each warp
+// that stores a 32-row block of one pair's row counts itself on cnt[t][blk];
+// the warp that brings the count to top_k (all of the token's rows of that
+// block are stored) reads them back and writes y's block, so the sum runs in
+// the same order whichever CTA finishes last. cnt starts at zero (zeroed by
+// the kernel that prepares the call's activations).
+struct Combine {
+  const float *w = nullptr;   // [n_tok][top_k]; null: no combine
+  float *y = nullptr;         // [n_tok][n_out]
+  const float *r = nullptr;   // [n_tok * top_k][n_out], the rows just stored
+  uint32_t *cnt = nullptr;    // [n_tok][nblk]
+  int32_t top_k = 0;
+  int64_t n_out = 0, nblk = 0;
+};
+
+// Expert biases (gpt-oss): f32 rows indexed by expert id, added to the f32
+// result of every pair not routed to the zero slot. The expert of pair p =
+// t * top_k + k is ids[t * nb1 + k * nb0] (byte strides; the router's ids,
+// before the remap); ids outside [0, n_expert) add nothing. View v's row of
+// expert e starts at b[v] + e * ld[v]. Null b[v]: no bias for that view.
+struct FfnBias {
+  const float *b[2] = {nullptr, nullptr};
+  int64_t ld[2] = {0, 0};
+  const char *ids = nullptr;
+  int64_t nb0 = 0, nb1 = 0;
+  int32_t top_k = 1, n_expert = 0;
+};
+
 // The activation between the gate/up and down projections: kind 0 is
 // silu(g) * u; kind 1 (MSB_ACT_SWIGLU_OAI) is gpt-oss's clamped form
 // min(g, limit) * sigmoid(alpha * min(g, limit)) * (clamp(u, -limit, limit) + 1).
@@ -145,6 +175,57 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+// Called by all 32 lanes of a warp after the warp stored its 32-row block
+// `blk` (row n = blk*32 + lane, rows past n_out skipped) of the result rows of
+// m pairs; lane l < m passes the l-th pair. One acquire-release atomic per
+// pair counts the block (the warp barrier orders every lane's stores before
+// it, and release is cumulative); for each pair whose count reached top_k --
+// all of its token's rows of the block are stored -- the warp sums them in
+// k order and writes y's block (see Combine).
+__device__ __forceinline__ void combine_arrive(const Combine &c, int64_t my_pair, int m,
+                                               int64_t blk, int lane) {
+  if (!c.w || blk >= c.nblk) return;
+  __syncwarp();
+  uint32_t old = 0;
+  int64_t t = 0;
+  if (lane < m) {
+    t = my_pair / c.top_k;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(old)
+                 : "l"(c.cnt + t * c.nblk + blk)
+                 : "memory");
+  }
+  unsigned last = __ballot_sync(0xffffffffu, lane < m && old == uint32_t(c.top_k - 1));
+  const int64_t n = blk * 32 + lane;
+  while (last) {
+    const int j = __ffs(last) - 1;
+    last &= last - 1;
+    const int64_t tj = __shfl_sync(0xffffffffu, t, j);
+    if (n < c.n_out) {
+      float s = 0.f;
+      for (int k = 0; k < c.top_k; ++k)
+        s = fmaf(c.w[tj * c.top_k + k], __ldcg(c.r + (tj * c.top_k + k) * c.n_out + n), s);
+      c.y[tj * c.n_out + n] = s;
+    }
+  }
+}
+
+// Zeroes n words with every thread of the grid (grid-stride).
+__device__ __forceinline__ void grid_zero(uint32_t *p, int64_t n) {
+  if (!p) return;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x)
+    p[i] = 0u;
+}
+
+// Row of view v's bias for `pair` (null when none applies).
+__device__ __forceinline__ const float *bias_row(const FfnBias &f, int v, int64_t pair) {
+  if (!f.b[v]) return nullptr;
+  const int64_t t = pair / f.top_k, k = pair - t * f.top_k;
+  const int32_t e = *reinterpret_cast<const int32_t *>(f.ids + t * f.nb1 + k * f.nb0);
+  return (e >= 0 && e < f.n_expert) ? f.b[v] + int64_t(e) * f.ld[v] : nullptr;
+}
+
 // h = act(g, u) of FfnAct, in f32 with expf.
 __device__ __forceinline__ float ffn_act(const FfnAct &f, float g, float u) {
   if (f.kind == 1) {

@@ -8,7 +8,7 @@ import ctypes
 import torch
 
 from ._lib import (OPT_MXFP4_PATH, TYPE_BF16, TYPE_F32, TYPE_IQ4_NL, TYPE_MXFP4, FfnActCfg,
-                   PoolInfo, Route, c_vp, check, lib)
+                   FfnBiasCfg, PoolInfo, Route, c_vp, check, lib)
 
 WEIGHT_TYPES = {"iq4_nl": TYPE_IQ4_NL, "mxfp4": TYPE_MXFP4}
 _ACT_TYPES = {torch.float32: TYPE_F32, torch.bfloat16: TYPE_BF16}
@@ -175,10 +175,13 @@ def mul_mat_id(pool, b, route, top_k, ws=None, out=None, stream=None):
 
 
 def moe_ffn(gate, up, down, x, route, w, top_k, up_row0=0, ws=None, out=None, act=None,
-            stream=None, activation=None):
+            stream=None, activation=None, bias=None):
     """x: [n_tok, K] f32/bf16; w: [n_tok, top_k] f32, or None with top_k 1 (y is
     the expert output itself). activation: None for silu(g) * u, or
-    ("swiglu_oai", alpha, limit) for gpt-oss's clamped form. Returns y
+    ("swiglu_oai", alpha, limit) for gpt-oss's clamped form. bias: None, or
+    (gate_b, up_b, down_b, ids) -- f32 device tensors [n_expert, >= rows]
+    (row stride free; None skips one) looked up by the router's expert ids
+    (int32 [n_tok, top_k]) of every pair not in the zero slot. Returns y
     [n_tok, K] f32."""
     n_tok, K = x.shape
     assert x.stride(1) == 1
@@ -188,6 +191,23 @@ def moe_ffn(gate, up, down, x, route, w, top_k, up_row0=0, ws=None, out=None, ac
         ws = workspace(kmax, n_tok, top_k, gate.n_slot, x.device)
     if out is None:
         out = torch.empty(n_tok, K, dtype=torch.float32, device=x.device)
+    if bias is not None:
+        gb, ub, db, ids = bias
+        n_expert = next(b.shape[0] for b in (gb, ub, db) if b is not None)
+        for b in (gb, ub, db):
+            assert b is None or (b.dtype == torch.float32 and b.stride(1) == 1 and b.is_cuda)
+        assert ids.dtype == torch.int32 and ids.shape == (n_tok, top_k)
+        bc = FfnBiasCfg(*[b.data_ptr() if b is not None else None for b in (gb, ub, db)],
+                        *[b.stride(0) if b is not None else 0 for b in (gb, ub, db)],
+                        ids.data_ptr(), ids.stride(1) * 4, ids.stride(0) * 4, n_expert)
+        kind, alpha, limit = activation if activation is not None else ("silu", 1.0, 0.0)
+        cfg = FfnActCfg({"silu": 0, "swiglu_oai": 1}[kind], alpha, limit)
+        check(lib().msb_moe_ffn_ex(gate.handle, up.handle, up_row0, down.handle, _ptr(x),
+                                   _ACT_TYPES[x.dtype], x.stride(0) * x.element_size(),
+                                   ctypes.byref(route.c), _ptr(w), top_k, n_tok, _ptr(out),
+                                   _ptr(act), ctypes.byref(cfg), ctypes.byref(bc), _ptr(ws),
+                                   ws.numel(), _stream(stream)))
+        return out
     if activation is None:
         check(lib().msb_moe_ffn(gate.handle, up.handle, up_row0, down.handle, _ptr(x),
                                 _ACT_TYPES[x.dtype], x.stride(0) * x.element_size(),

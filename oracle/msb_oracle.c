@@ -408,11 +408,61 @@ int orc_mul_mat_id(int type, const uint8_t *as, int64_t K, int64_t N, int64_t n_
  * bytes; up rows start at up_row0 within up (fused gate_up tensors).
  * In q8 mode h is re-quantized before the down projection, as the device
  * path does. x: f32 [T][K]; w: f32 [T][top_k]; y: f32 [T][K]. */
+/* Expert biases (gpt-oss; llama.cpp adds them with add_id over the router's
+ * expert ids): gate_b / up_b / down_b are f32 rows [n_expert][ld], expert e's
+ * row at +e*ld (NULL: none), looked up by eids[t][k] (the expert id of the
+ * pair, before the remap); added to the f32 matmul result of every pair not
+ * routed to the zero slot (slot n_slots - 1), before the activation (gate,
+ * up) or the weighting (down). Ids outside [0, n_expert) add nothing. */
+typedef struct {
+  const float *gate_b, *up_b, *down_b;
+  int64_t gate_ld, up_ld, down_ld;
+  const int32_t *eids;
+  int n_expert;
+} orc_bias;
+
+static void add_bias(float *res, int64_t pairs, int64_t n, const float *b, int64_t ld,
+                     const int32_t *eids, int n_expert, const int32_t *ids, int64_t zero_slot) {
+  if (!b) return;
+  for (int64_t p = 0; p < pairs; ++p) {
+    const int32_t e = eids[p];
+    if (ids[p] == zero_slot || e < 0 || e >= n_expert) continue;
+    for (int64_t i = 0; i < n; ++i) res[p * n + i] += b[(int64_t)e * ld + i];
+  }
+}
+
+static int moe_ffn_impl(int type, const uint8_t *gate, int64_t gate_rows, const uint8_t *up,
+                        int64_t up_rows, int64_t up_row0, const uint8_t *down, int64_t K,
+                        int64_t n_ff, int64_t n_slots, const float *x, const int32_t *ids,
+                        const float *w, int top_k, int T, int mode, int act, float alpha,
+                        float limit, float *y, float *h_out, int nthreads, const orc_bias *bias);
+
 int orc_moe_ffn(int type, const uint8_t *gate, int64_t gate_rows, const uint8_t *up,
                 int64_t up_rows, int64_t up_row0, const uint8_t *down, int64_t K, int64_t n_ff,
                 int64_t n_slots, const float *x, const int32_t *ids, const float *w, int top_k,
                 int T, int mode, int act, float alpha, float limit, float *y, float *h_out,
                 int nthreads) {
+  return moe_ffn_impl(type, gate, gate_rows, up, up_rows, up_row0, down, K, n_ff, n_slots, x, ids,
+                      w, top_k, T, mode, act, alpha, limit, y, h_out, nthreads, NULL);
+}
+
+int orc_moe_ffn_bias(int type, const uint8_t *gate, int64_t gate_rows, const uint8_t *up,
+                     int64_t up_rows, int64_t up_row0, const uint8_t *down, int64_t K,
+                     int64_t n_ff, int64_t n_slots, const float *x, const int32_t *ids,
+                     const float *w, int top_k, int T, int mode, int act, float alpha,
+                     float limit, float *y, float *h_out, int nthreads, const float *gate_b,
+                     const float *up_b, const float *down_b, int64_t gate_ld, int64_t up_ld,
+                     int64_t down_ld, const int32_t *eids, int n_expert) {
+  const orc_bias b = {gate_b, up_b, down_b, gate_ld, up_ld, down_ld, eids, n_expert};
+  return moe_ffn_impl(type, gate, gate_rows, up, up_rows, up_row0, down, K, n_ff, n_slots, x, ids,
+                      w, top_k, T, mode, act, alpha, limit, y, h_out, nthreads, &b);
+}
+
+static int moe_ffn_impl(int type, const uint8_t *gate, int64_t gate_rows, const uint8_t *up,
+                        int64_t up_rows, int64_t up_row0, const uint8_t *down, int64_t K,
+                        int64_t n_ff, int64_t n_slots, const float *x, const int32_t *ids,
+                        const float *w, int top_k, int T, int mode, int act, float alpha,
+                        float limit, float *y, float *h_out, int nthreads, const orc_bias *bias) {
   const int64_t pairs = (int64_t)T * top_k;
   const int64_t bb = block_bytes(type);
   if (bb < 0 || K % 32 || n_ff % 32) return -1;
@@ -432,6 +482,12 @@ int orc_moe_ffn(int type, const uint8_t *gate, int64_t gate_rows, const uint8_t 
   if (!rc) rc = orc_mul_mat_id(type, uv, K, n_ff, n_slots, x, 1, ids, top_k, T, mode, u, nthreads);
   free(gv);
   free(uv);
+  if (!rc && bias) {
+    add_bias(g, pairs, n_ff, bias->gate_b, bias->gate_ld, bias->eids, bias->n_expert, ids,
+             n_slots - 1);
+    add_bias(u, pairs, n_ff, bias->up_b, bias->up_ld, bias->eids, bias->n_expert, ids,
+             n_slots - 1);
+  }
   if (!rc) {
     float *h = (float *)malloc(sizeof(float) * (size_t)(pairs * n_ff));
     for (int64_t i = 0; i < pairs * n_ff; ++i) {
@@ -445,8 +501,16 @@ int orc_moe_ffn(int type, const uint8_t *gate, int64_t gate_rows, const uint8_t 
         h[i] = g[i] / (1.f + expf(-g[i])) * u[i];
       }
     }
+    /* rows of the zero slot are exactly 0 before the down projection */
+    if (bias)
+      for (int64_t p = 0; p < pairs; ++p)
+        if (ids[p] == n_slots - 1)
+          for (int64_t i = 0; i < n_ff; ++i) h[p * n_ff + i] = 0.f;
     if (h_out) memcpy(h_out, h, sizeof(float) * (size_t)(pairs * n_ff));
     rc = orc_mul_mat_id(type, down, n_ff, K, n_slots, h, top_k, ids, top_k, T, mode, r, nthreads);
+    if (!rc && bias)
+      add_bias(r, pairs, K, bias->down_b, bias->down_ld, bias->eids, bias->n_expert, ids,
+               n_slots - 1);
     free(h);
   }
   if (!rc) {

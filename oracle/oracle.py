@@ -60,6 +60,9 @@ def orc():
                                   ctypes.c_int64, _f32p, _i32p, _f32p, ctypes.c_int, ctypes.c_int,
                                   ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float,
                                   _f32p, _f32p, ctypes.c_int]
+        L.orc_moe_ffn_bias.argtypes = L.orc_moe_ffn.argtypes + [
+            _f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _i32p,
+            ctypes.c_int]
         L.orc_e2m1_split.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, _f32p, _u8p, _u8p]
         L.orc_quantize_q8.argtypes = [_f32p, ctypes.c_int64, ctypes.POINTER(ctypes.c_int8), _f32p]
         L.orc_f32_to_f16.argtypes = [ctypes.c_float]
@@ -269,13 +272,17 @@ def mul_mat_id(wtype, slab, K, N, b, ids, mode="exact", nthreads=None):
 
 
 def moe_ffn(wtype, gate, up, down, K, n_ff, x, ids, w, mode="exact", up_row0=0, up_rows=None,
-            nthreads=None, act=None):
+            nthreads=None, act=None, bias=None):
     """gate/up/down: uint8 [n_slots, bytes]; x: f32 [T, K]; ids: [T, top_k] slot
     ids; w: f32 [T, top_k]. The gate is rows [0, n_ff) and the up projection
     rows [up_row0, up_row0 + n_ff) of their slots (the same array for a fused
     gate_up tensor). act: None for silu(gate) * up, or (alpha, limit) for the
     gpt-oss form min(g, limit) * sigmoid(alpha * min(g, limit)) *
-    (clamp(u, -limit, limit) + 1). Returns (y [T, K], h [T, top_k, n_ff])."""
+    (clamp(u, -limit, limit) + 1). bias: None, or (gate_b, up_b, down_b,
+    expert_ids, n_expert) with f32 rows [n_expert, >= rows] (None to skip one)
+    looked up by the pairs' expert ids [T, top_k] and added to the matmul
+    results of pairs not in the zero slot (the last slab row). Returns
+    (y [T, K], h [T, top_k, n_ff])."""
     t = TYPES.get(wtype, wtype)
     gate, up, down = (np.ascontiguousarray(a, dtype=np.uint8) for a in (gate, up, down))
     row_bytes = (K // 32) * BLOCK_BYTES[t]
@@ -287,11 +294,24 @@ def moe_ffn(wtype, gate, up, down, K, n_ff, x, ids, w, mode="exact", up_row0=0, 
     T, top_k = ids.shape
     y = np.empty((T, K), dtype=np.float32)
     h = np.empty((T, top_k, n_ff), dtype=np.float32)
-    rc = orc().orc_moe_ffn(t, _p(gate, _u8p), gate_rows, _p(up, _u8p), up_rows, up_row0,
-                           _p(down, _u8p), K, n_ff, gate.shape[0], _p(x, _f32p), _p(ids, _i32p),
-                           _p(w, _f32p), top_k, T, MODES[mode], 1 if act else 0,
-                           act[0] if act else 1.0, act[1] if act else 0.0, _p(y, _f32p),
-                           _p(h, _f32p), nthreads or os.cpu_count() or 1)
+    args = (t, _p(gate, _u8p), gate_rows, _p(up, _u8p), up_rows, up_row0,
+            _p(down, _u8p), K, n_ff, gate.shape[0], _p(x, _f32p), _p(ids, _i32p),
+            _p(w, _f32p), top_k, T, MODES[mode], 1 if act else 0,
+            act[0] if act else 1.0, act[1] if act else 0.0, _p(y, _f32p),
+            _p(h, _f32p), nthreads or os.cpu_count() or 1)
+    if bias is None:
+        rc = orc().orc_moe_ffn(*args)
+    else:
+        gb, ub, db, eids, n_expert = bias
+        keep = [np.ascontiguousarray(b, dtype=np.float32) if b is not None else None
+                for b in (gb, ub, db)]
+        eids = np.ascontiguousarray(eids, dtype=np.int32)
+        assert eids.shape == ids.shape
+        ptr = lambda b: _p(b, _f32p) if b is not None else None
+        ld = lambda b: b.shape[1] if b is not None else 0
+        rc = orc().orc_moe_ffn_bias(*args, ptr(keep[0]), ptr(keep[1]), ptr(keep[2]),
+                                    ld(keep[0]), ld(keep[1]), ld(keep[2]), _p(eids, _i32p),
+                                    n_expert)
     assert rc == 0, rc
     return y, h
 

@@ -217,3 +217,88 @@ def test_up_view_off_the_tile_grid(n_ff, pad):
                          mode="e2m1x4", up_row0=up_row0)
     assert O.max_abs_normalized(act.cpu().numpy(), h_f) < 1e-4
     assert O.max_abs_normalized(y.cpu().numpy(), y_f) < 1e-3
+
+
+@pytest.mark.parametrize("wtype,K,n_ff,n_expert,n_slot,n_tok,top_k,fused", [
+    ("mxfp4", 2880, 2880, 6, 4, 2, 4, True),     # 8 pairs: split over K, the reduce adds them
+    ("mxfp4", 2880, 2880, 6, 4, 5, 4, True),     # fused gate_up, up view off the tile grid
+    ("mxfp4", 512, 256, 8, 6, 40, 4, False),     # several passes per slot
+    ("iq4_nl", 2048, 512, 10, 8, 8, 8, False),   # CUDA cores
+])
+def test_expert_biases_match_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, fused):
+    """gpt-oss expert biases, looked up by the router's expert ids (not the
+    slots), added to every pair not routed to the zero slot; non-resident
+    experts go to the zero slot and contribute exactly 0."""
+    from moestream_b200 import ops
+    pools, slabs, slot_of = build_layer(wtype, K, n_ff, n_expert, n_slot, fused, seed=K + 3)
+    rng = np.random.default_rng(n_tok + 11)
+    x = rng.normal(0, 1, size=(n_tok, K)).astype(np.float32)
+    ids_e, w = topk_ids(rng, n_tok, n_expert, top_k)
+    table = np.full(n_expert, -1, dtype=np.int32)
+    for e, s in slot_of.items():
+        table[e] = s
+    slots = O.remap_table(ids_e, table, n_slot)
+    assert (slots == n_slot).any() and (slots < n_slot).any()
+    gb = rng.normal(0, 0.5, size=(n_expert, 2 * n_ff if fused else n_ff)).astype(np.float32)
+    ub = None if fused else rng.normal(0, 0.5, size=(n_expert, n_ff)).astype(np.float32)
+    db = rng.normal(0, 0.5, size=(n_expert, K)).astype(np.float32)
+    ids_t = torch.from_numpy(ids_e).cuda()
+    gb_t, db_t = torch.from_numpy(gb).cuda(), torch.from_numpy(db).cuda()
+    ub_t = gb_t[:, n_ff:] if fused else torch.from_numpy(ub).cuda()
+    r = ops.remap_group(ids_t, n_slot, table=torch.from_numpy(table).cuda(), n_expert=n_expert)
+    act = torch.empty(n_tok, top_k, n_ff, dtype=torch.float32, device="cuda")
+    y = ops.moe_ffn(pools["gate"], pools["up"], pools["down"], torch.from_numpy(x).cuda(), r,
+                    torch.from_numpy(w).cuda(), top_k, up_row0=n_ff if fused else 0, act=act,
+                    bias=(gb_t, ub_t, db_t, ids_t), activation=("swiglu_oai", 1.702, 7.0))
+    torch.cuda.synchronize()
+    tc = wtype == "mxfp4"
+    up = slabs["gate"] if fused else slabs["up"]
+    ub_o = gb[:, n_ff:] if fused else ub
+    y_f, h_f = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
+                         mode="e2m1x4" if tc else "q8", up_row0=n_ff if fused else 0,
+                         act=(1.702, 7.0), bias=(gb[:, :n_ff], ub_o, db, ids_e, n_expert))
+    y_0, _ = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
+                       mode="e2m1x4" if tc else "q8", up_row0=n_ff if fused else 0,
+                       act=(1.702, 7.0))
+    assert O.max_abs_normalized(y_f, y_0) > 1e-2   # the biases matter
+    a = act.cpu().numpy()
+    assert np.all(a[slots == n_slot] == 0.0)
+    assert O.max_abs_normalized(a, h_f) < (1e-4 if tc else 1e-5)
+    assert O.max_abs_normalized(y.cpu().numpy(), y_f) < (1e-3 if tc else 2e-3)
+
+
+@pytest.mark.parametrize("wtype,K,n_ff,n_tok", [("mxfp4", 512, 256, 48), ("mxfp4", 512, 256, 2),
+                                               ("iq4_nl", 512, 256, 48)])
+def test_combine_runs_in_the_down_epilogue(wtype, K, n_ff, n_tok):
+    """No separate combine kernel: one FFN call launches the activation
+    preparation, gate/up and down (plus the split-over-K reduce of each
+    projection for batches of up to 8 pairs), and y is the same bits on
+    every call whichever CTA finishes a token's rows last."""
+    from moestream_b200 import ops
+    from moestream_b200._lib import lib
+    top_k, n_expert = 4, 8
+    pools, slabs, slot_of = build_layer(wtype, K, n_ff, n_expert, n_expert, False, seed=5)
+    rng = np.random.default_rng(1)
+    x = torch.from_numpy(rng.normal(0, 1, size=(n_tok, K)).astype(np.float32)).cuda()
+    ids_e, w = topk_ids(rng, n_tok, n_expert, top_k)
+    table = np.full(n_expert, -1, dtype=np.int32)
+    for e, s in slot_of.items():
+        table[e] = s
+    r = ops.remap_group(torch.from_numpy(ids_e).cuda(), n_expert,
+                        table=torch.from_numpy(table).cuda(), n_expert=n_expert)
+    w_t = torch.from_numpy(w).cuda()
+    ws = ops.workspace(K, n_tok, top_k, n_expert)
+    torch.cuda.synchronize()
+    c0 = int(lib().msb_kernel_launches())
+    y0 = ops.moe_ffn(pools["gate"], pools["up"], pools["down"], x, r, w_t, top_k, ws=ws)
+    launched = int(lib().msb_kernel_launches()) - c0
+    split = wtype == "mxfp4" and n_tok * top_k <= 8
+    assert launched == (5 if split else 3)
+    ys = [ops.moe_ffn(pools["gate"], pools["up"], pools["down"], x, r, w_t, top_k, ws=ws).clone()
+          for _ in range(3)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(y0, yi) for yi in ys)
+    slots = O.remap_table(ids_e, table, n_expert)
+    want, _ = O.moe_ffn(wtype, slabs["gate"], slabs["up"], slabs["down"], K, n_ff,
+                        x.cpu().numpy(), slots, w, mode="e2m1x4" if wtype == "mxfp4" else "q8")
+    assert O.max_abs_normalized(y0.cpu().numpy(), want) < (1e-3 if wtype == "mxfp4" else 2e-3)
