@@ -57,10 +57,16 @@ def parse():
                     help="expert-parallel exchange: NVLink peer-memory kernels or NCCL all-to-all")
     ap.add_argument("--eager", action="store_true",
                     help="launch every kernel from the host instead of replaying CUDA graphs")
-    ap.add_argument("--workload", default="resident", choices=["resident", "streamed", "slots"],
+    ap.add_argument("--workload", default="resident",
+                    choices=["resident", "streamed", "slots", "prefill"],
                     help="resident: every expert in HBM (the default line); streamed: a slot "
                          "cache per layer with misses filled from pinned host memory (1 GPU); "
-                         "slots: small decode batches over slot pools (1 GPU, --model)")
+                         "slots: small decode batches over slot pools (1 GPU, --model); "
+                         "prefill: 512-token Zipf prompt batches with ~30%% of each layer's "
+                         "experts filled from pinned host memory during the grouped GEMM "
+                         "(1 GPU)")
+    ap.add_argument("--miss-frac", type=float, default=0.3,
+                    help="prefill: fraction of each layer's referenced experts not resident")
     ap.add_argument("--model", default="gpt-oss", choices=["gpt-oss", "iq4nl-256e"],
                     help="slots: gpt-oss layers (MXFP4, 32 of 128 experts, top-4) or a "
                          "256-expert IQ4_NL model (hidden 2048, expert FFN 512, 64 slots, top-8)")
@@ -71,6 +77,11 @@ def parse():
     args = ap.parse_args()
     if args.workload in ("streamed", "slots") and "--tokens" not in sys.argv:
         args.tokens = 1
+    if args.workload == "prefill":
+        if "--tokens" not in sys.argv:
+            args.tokens = 512
+        if "--layers" not in sys.argv:
+            args.layers = 4
     if args.workload == "slots" and args.model == "iq4nl-256e" and "--layers" not in sys.argv:
         args.layers = 40
     return args
@@ -644,8 +655,215 @@ def slots_main(args):
     return 0
 
 
+def prefill_main(args):
+    """--workload prefill: prompt processing of --tokens (512) tokens through
+    --layers (4) gpt-oss-shaped layers whose pools hold one slot per expert
+    (the arena size the reference uses for prompt batches), with Zipf(1.1)
+    expert popularity per layer (top-4 softmax over N(0,1) logits plus
+    log p_e, p_e ~ rank^-1.1 over a per-layer permutation). At every step
+    --miss-frac (30%) of each layer's referenced experts are not resident:
+    a side stream fills them from pinned host memory (msb_fill_slots_async:
+    one cudaMemcpyAsync per expert and role, then the repack kernel), one
+    layer after the other, while the compute stream runs each layer's grouped
+    GEMM over its resident experts; the filled experts' pairs follow in a
+    second FFN call that waits on the layer's fill event and adds into y.
+    Reported: tokens/s of that overlapped step, and from the same run the
+    fills alone, the compute alone (every expert resident) and the two one
+    after the other; overlap = (serial - overlapped) / min(fills, compute)."""
+    import numpy as np
+    import torch
+
+    from moestream_b200 import ops
+    K, n_ff, E, top_k = SHAPE["hidden"], SHAPE["n_ff"], SHAPE["n_expert"], SHAPE["top_k"]
+    T, L = args.tokens, args.layers
+    t_setup = time.time()
+    # One layer's experts quantized on the device and kept as pinned host
+    # copies; every layer's pools start from them and its misses are filled
+    # from them.
+    (g0, u0, d0), = build_layers(1, 0, E, K, n_ff, seed=4321)
+    host = [torch.stack([p.read_slot(e) for e in range(E)]).cpu().pin_memory()
+            for p in (g0, u0, d0)]
+    for p in (g0, u0, d0):
+        p.close()
+    del g0, u0, d0
+    torch.cuda.synchronize()
+    layers = []
+    for _ in range(L):
+        pools = tuple(ops.SlotPool("mxfp4", kk, nn, E, max_fill_batch=64)
+                      for kk, nn in ((K, n_ff), (K, n_ff), (n_ff, K)))
+        for p, h in zip(pools, host):
+            for j0 in range(0, E, 64):
+                p.fill(list(range(j0, min(E, j0 + 64))), [h[e] for e in range(j0, min(E, j0 + 64))])
+        layers.append(pools)
+    torch.cuda.synchronize()
+    S = args.warmup + args.steps
+    rng = np.random.default_rng(11)
+    ids, w, pending = [], [], []
+    for s_ in range(S):
+        ids.append([])
+        w.append([])
+        pending.append([])
+        for il in range(L):
+            perm_rng = np.random.default_rng(1000 + il)   # the layer's popularity order
+            ranks = perm_rng.permutation(E) + 1
+            bias = np.log(ranks ** -1.1 / (ranks ** -1.1).sum())
+            logits = rng.normal(0, 1, size=(T, E)) + bias
+            i_ = np.argsort(-logits, axis=1, kind="stable")[:, :top_k].astype(np.int32)
+            sel = np.take_along_axis(logits, i_, 1)
+            w_ = np.exp(sel - sel.max(1, keepdims=True))
+            ids[-1].append(torch.from_numpy(i_).cuda())
+            w[-1].append(torch.from_numpy((w_ / w_.sum(1, keepdims=True)).astype(np.float32)).cuda())
+            ref = np.unique(i_)
+            n_miss = int(round(args.miss_frac * len(ref)))
+            pending[-1].append(np.sort(rng.choice(ref, n_miss, replace=False)).astype(np.int32))
+    tables = []
+    for s_ in range(S):
+        tables.append([])
+        for il in range(L):
+            ta = np.arange(E, dtype=np.int32)
+            ta[pending[s_][il]] = -1
+            tb = np.full(E, -1, dtype=np.int32)
+            tb[pending[s_][il]] = pending[s_][il]
+            tables[-1].append((torch.from_numpy(ta).cuda(), torch.from_numpy(tb).cuda()))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    x = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
+    y = torch.empty(L, T, K, dtype=torch.float32, device="cuda")
+    ws = ops.workspace(K, T, top_k, E)
+    ra, rb = ops.RouteBuffers(T * top_k, E), ops.RouteBuffers(T * top_k, E)
+    side = torch.cuda.Stream()
+    main_s = torch.cuda.current_stream()
+    lib = ops.lib()
+    eb = sum(p.expert_bytes for p in layers[0])
+    torch.cuda.synchronize()
+    t_setup = time.time() - t_setup
+
+    def fills(s_, il, stream):
+        for p, h in zip(layers[il], host):
+            es = pending[s_][il].tolist()
+            p.fill(es, [h[e] for e in es], stream=stream)
+
+    def compute_all_resident(s_, il):
+        ga, up, dn = layers[il]
+        r = ops.remap_group(ids[s_][il], E, route=ra)
+        ops.moe_ffn(ga, up, dn, x, r, w[s_][il], top_k, ws=ws, out=y[il])
+
+    def timed(fn, s_):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(main_s)
+        fn(s_)
+        b.record(main_s)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b)
+
+    def step_overlapped(s_):
+        start = torch.cuda.Event()
+        start.record(main_s)
+        side.wait_event(start)
+        for il in range(L):
+            ga, up, dn = layers[il]
+            ta, tb = tables[s_][il]
+            r = ops.remap_group(ids[s_][il], E, table=ta, n_expert=E, route=ra)
+            ops.moe_ffn(ga, up, dn, x, r, w[s_][il], top_k, ws=ws, out=y[il])
+            fills(s_, il, side)
+            done = torch.cuda.Event()
+            done.record(side)
+            main_s.wait_event(done)
+            r = ops.remap_group(ids[s_][il], E, table=tb, n_expert=E, route=rb)
+            ops.moe_ffn(ga, up, dn, x, r, w[s_][il], top_k, ws=ws, out=y[il], accumulate=True)
+
+    def step_fills(s_):
+        for il in range(L):
+            fills(s_, il, main_s)
+
+    def step_compute(s_):
+        for il in range(L):
+            compute_all_resident(s_, il)
+
+    def step_serial(s_):
+        step_fills(s_)
+        step_compute(s_)
+
+    for s_ in range(args.warmup):
+        step_overlapped(s_)
+        step_serial(s_)
+    torch.cuda.synchronize()
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    time.sleep(0.05)
+    c0 = int(lib.msb_kernel_launches())
+    t_over = [timed(step_overlapped, args.warmup + i) for i in range(args.steps)]
+    launches = int(lib.msb_kernel_launches()) - c0
+    clk = clocks.stop()
+    t_fill = [timed(step_fills, args.warmup + i) for i in range(args.steps)]
+    t_comp = [timed(step_compute, args.warmup + i) for i in range(args.steps)]
+    t_ser = [timed(step_serial, args.warmup + i) for i in range(args.steps)]
+    ms = sum(t_over) / len(t_over)
+    ms_fill, ms_comp, ms_ser = (sum(v) / len(v) for v in (t_fill, t_comp, t_ser))
+    miss = [len(pending[args.warmup + i][il]) for i in range(args.steps) for il in range(L)]
+    distinct = [len(np.unique(ids[args.warmup + i][il].cpu().numpy())) for i in range(args.steps)
+                for il in range(L)]
+    fill_bytes = sum(miss) / args.steps * eb
+    fill_gbs = fill_bytes / (ms_fill / 1e3) / 1e9
+    # pinned host-to-device copy bandwidth, the fills' bound, measured here
+    big = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    big_d = torch.empty_like(big, device="cuda")
+    best = None
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        big_d.copy_(big, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        best = a.elapsed_time(b) if best is None else min(best, a.elapsed_time(b))
+    h2d_gbs = big.numel() / (best / 1e3) / 1e9
+    del big, big_d
+    comp_bytes = sum(distinct) / args.steps * eb
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    overlap = (ms_ser - ms) / min(ms_fill, ms_comp) if min(ms_fill, ms_comp) > 0 else None
+    line = {"metric": "MoE-FFN prefill tokens/s with slot fills overlapped", "impl": "msb",
+            "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "mxfp4 x bf16 as 4 e2m1 terms per 32-block -> f32", "data": "synthetic",
+            "config": {"workload": "gpt-oss-120b-shaped MoE FFN prefill, one slot per expert, "
+                                   f"{args.miss_frac:.0%} of each layer's referenced experts "
+                                   "filled from pinned host memory during the step",
+                       "n_layer": L, "n_expert": E, "hidden": K, "n_ff": n_ff, "top_k": top_k,
+                       "tokens": T, "routing": "top-4 softmax over N(0,1) logits + per-layer "
+                                               "Zipf(1.1) bias",
+                       "distinct_per_layer": sum(distinct) / len(distinct),
+                       "misses_per_layer": sum(miss) / len(miss),
+                       "l2": "expert bytes per step far larger than L2"},
+            "fills_ms": ms_fill, "compute_ms": ms_comp, "serial_ms": ms_ser,
+            "overlap": overlap,
+            "fill_gbs": fill_gbs, "pinned_h2d_gbs": h2d_gbs,
+            "compute_gbs": comp_bytes / (ms_comp / 1e3) / 1e9,
+            "roofline": {"bound": "pcie", "achieved": fill_gbs, "peak": h2d_gbs, "unit": "GB/s",
+                         "frac": fill_gbs / h2d_gbs, "traffic": None,
+                         "kernel": "fills (cudaMemcpyAsync + repack), side stream",
+                         "peak_source": "pinned host-to-device copy of 1 GiB measured in this "
+                                        "run",
+                         "compute_frac_of_hbm": comp_bytes / (ms_comp / 1e3) / 1e9 / hbm},
+            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk,
+            "setup_s": round(t_setup, 1)}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "prefill":
+        if args.gpus != 1 or args.impl != "msb":
+            print(json.dumps({"workload": "prefill", "unavailable": "one GPU, --impl msb only"}))
+            return 0
+        return prefill_main(args)
     if args.workload == "slots":
         if args.gpus != 1 or args.impl != "msb":
             print(json.dumps({"workload": "slots", "unavailable": "one GPU, --impl msb only"}))

@@ -313,13 +313,21 @@ typedef struct {
   int32_t n_expert;
 } msb_ffn_bias_t;
 
-/* msb_moe_ffn_act with optional expert biases (NULL: none). */
+/* msb_moe_ffn_act with optional expert biases (NULL: none) and, with
+ * accumulate != 0 (router weights required), y += the weighted sum instead
+ * of y = it. Accumulation lets a batch run in two calls over two routes of
+ * the same ids, each sending the other's experts to the zero slot: the
+ * experts already resident first, the ones being filled on another stream
+ * second (after an event of the fill), so the fill overlaps the first
+ * call's grouped GEMM. The two-call y differs from one call's only in the
+ * rounding of that last addition. */
 int msb_moe_ffn_ex(msb_pool_t gate, msb_pool_t up, int64_t up_row0,
                    msb_pool_t down, const void *x_dev, int x_type,
                    int64_t x_nb1, const msb_route_t *route, const float *w_dev,
                    int32_t top_k, int32_t n_tok, float *y_dev, float *act_dev,
                    const msb_ffn_act_t *act, const msb_ffn_bias_t *bias,
-                   void *workspace, int64_t workspace_bytes, void *stream);
+                   int32_t accumulate, void *workspace, int64_t workspace_bytes,
+                   void *stream);
 
 /* ======================================================================== */
 /* Expert parallelism (packing around the all-to-all exchanges)               */

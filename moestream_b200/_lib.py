@@ -140,7 +140,7 @@ SIGNATURES = {
                                       ctypes.c_int64, ctypes.POINTER(Route), c_vp,
                                       ctypes.c_int32, ctypes.c_int32, c_vp, c_vp,
                                       ctypes.POINTER(FfnActCfg), ctypes.POINTER(FfnBiasCfg),
-                                      c_vp, ctypes.c_int64, c_vp]),
+                                      ctypes.c_int32, c_vp, ctypes.c_int64, c_vp]),
     "msb_ep_dispatch": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_int32, c_vp, ctypes.c_int64,

@@ -560,7 +560,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
                         const float *w_dev, int32_t top_k, int32_t n_tok, float *y_dev,
                         float *act_dev, void *workspace, int64_t workspace_bytes,
                         const RowTarget *rows, void *stream, const FfnAct &fa,
-                        const msb_ffn_bias_t *bias) {
+                        const msb_ffn_bias_t *bias, bool accumulate = false) {
   MSB_CHECK_ARG(fa.kind == 0 || (fa.kind == 1 && fa.limit > 0.f),
                 "msb_moe_ffn: unknown activation %d (or limit <= 0)", fa.kind);
   MSB_CHECK_ARG(gate && up && down && route && (y_dev || rows) && workspace,
@@ -569,6 +569,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
   MSB_CHECK_ARG(w_dev || top_k == 1, "msb_moe_ffn: router weights may be omitted only for top_k 1");
   MSB_CHECK_ARG(x_dev || n_tok == 0, "msb_moe_ffn: null x");
   MSB_CHECK_ARG(top_k > 0 && n_tok >= 0, "msb_moe_ffn: bad shape");
+  MSB_CHECK_ARG(!accumulate || w_dev, "msb_moe_ffn: accumulating into y needs router weights");
   MSB_CHECK_ARG(!bias || ((bias->ids || n_tok == 0) && bias->n_expert > 0 &&
                           (bias->gate_b || bias->up_b || bias->down_b)),
                 "msb_moe_ffn: biases need the router's expert ids, n_expert > 0 and a bias row");
@@ -623,6 +624,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
       comb.top_k = top_k;
       comb.n_out = down->N;
       comb.nblk = (down->N + 31) / 32;
+      comb.accumulate = accumulate;
     }
     // The rest: scratch for the split over K of small batches (gate/up and
     // down use it one after the other).
@@ -661,6 +663,7 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
     comb.top_k = top_k;
     comb.n_out = down->N;
     comb.nblk = (down->N + 31) / 32;
+    comb.accumulate = accumulate;
   }
   if (int rc = quantize_act(x_dev, x_type, 1, x_nb1, x_nb1, n_tok, xq, st, w_dev ? cnt : nullptr,
                             cnt_n))
@@ -733,10 +736,11 @@ extern "C" int msb_moe_ffn_ex(msb_pool_t gate, msb_pool_t up, int64_t up_row0, m
                               const msb_route_t *route, const float *w_dev, int32_t top_k,
                               int32_t n_tok, float *y_dev, float *act_dev,
                               const msb_ffn_act_t *act, const msb_ffn_bias_t *bias,
-                              void *workspace, int64_t workspace_bytes, void *stream) {
+                              int32_t accumulate, void *workspace, int64_t workspace_bytes,
+                              void *stream) {
   return moe_ffn_core(gate, up, up_row0, down, x_dev, x_type, x_nb1, route, w_dev, top_k, n_tok,
                       y_dev, act_dev, workspace, workspace_bytes, nullptr, stream, act_of(act),
-                      bias);
+                      bias, accumulate != 0);
 }
 
 int msb::moe_ffn_to_rows(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_pool_t down,

@@ -75,6 +75,7 @@ struct Combine {
   uint32_t *cnt = nullptr;    // [n_tok][nblk]
   int32_t top_k = 0;
   int64_t n_out = 0, nblk = 0;
+  bool accumulate = false;    // y += the sum instead of y = the sum
 };
 
 // Expert biases (gpt-oss): f32 rows indexed by expert id, added to the f32
@@ -205,7 +206,8 @@ __device__ __forceinline__ void combine_arrive(const Combine &c, int64_t my_pair
       float s = 0.f;
       for (int k = 0; k < c.top_k; ++k)
         s = fmaf(c.w[tj * c.top_k + k], __ldcg(c.r + (tj * c.top_k + k) * c.n_out + n), s);
-      c.y[tj * c.n_out + n] = s;
+      float *yp = c.y + tj * c.n_out + n;
+      *yp = c.accumulate ? *yp + s : s;
     }
   }
 }

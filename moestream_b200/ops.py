@@ -175,14 +175,14 @@ def mul_mat_id(pool, b, route, top_k, ws=None, out=None, stream=None):
 
 
 def moe_ffn(gate, up, down, x, route, w, top_k, up_row0=0, ws=None, out=None, act=None,
-            stream=None, activation=None, bias=None):
+            stream=None, activation=None, bias=None, accumulate=False):
     """x: [n_tok, K] f32/bf16; w: [n_tok, top_k] f32, or None with top_k 1 (y is
     the expert output itself). activation: None for silu(g) * u, or
     ("swiglu_oai", alpha, limit) for gpt-oss's clamped form. bias: None, or
     (gate_b, up_b, down_b, ids) -- f32 device tensors [n_expert, >= rows]
     (row stride free; None skips one) looked up by the router's expert ids
-    (int32 [n_tok, top_k]) of every pair not in the zero slot. Returns y
-    [n_tok, K] f32."""
+    (int32 [n_tok, top_k]) of every pair not in the zero slot. accumulate:
+    out += the weighted sum (out must be given). Returns y [n_tok, K] f32."""
     n_tok, K = x.shape
     assert x.stride(1) == 1
     assert (w is None and top_k == 1) or (w.dtype == torch.float32 and w.is_contiguous())
@@ -191,22 +191,26 @@ def moe_ffn(gate, up, down, x, route, w, top_k, up_row0=0, ws=None, out=None, ac
         ws = workspace(kmax, n_tok, top_k, gate.n_slot, x.device)
     if out is None:
         out = torch.empty(n_tok, K, dtype=torch.float32, device=x.device)
-    if bias is not None:
-        gb, ub, db, ids = bias
-        n_expert = next(b.shape[0] for b in (gb, ub, db) if b is not None)
-        for b in (gb, ub, db):
-            assert b is None or (b.dtype == torch.float32 and b.stride(1) == 1 and b.is_cuda)
-        assert ids.dtype == torch.int32 and ids.shape == (n_tok, top_k)
-        bc = FfnBiasCfg(*[b.data_ptr() if b is not None else None for b in (gb, ub, db)],
-                        *[b.stride(0) if b is not None else 0 for b in (gb, ub, db)],
-                        ids.data_ptr(), ids.stride(1) * 4, ids.stride(0) * 4, n_expert)
+    assert not accumulate or (out is not None and w is not None)
+    if bias is not None or accumulate:
+        gb, ub, db, ids = bias if bias is not None else (None, None, None, None)
+        bc = None
+        if bias is not None:
+            n_expert = next(b.shape[0] for b in (gb, ub, db) if b is not None)
+            for b in (gb, ub, db):
+                assert b is None or (b.dtype == torch.float32 and b.stride(1) == 1 and b.is_cuda)
+            assert ids.dtype == torch.int32 and ids.shape == (n_tok, top_k)
+            bc = FfnBiasCfg(*[b.data_ptr() if b is not None else None for b in (gb, ub, db)],
+                            *[b.stride(0) if b is not None else 0 for b in (gb, ub, db)],
+                            ids.data_ptr(), ids.stride(1) * 4, ids.stride(0) * 4, n_expert)
         kind, alpha, limit = activation if activation is not None else ("silu", 1.0, 0.0)
         cfg = FfnActCfg({"silu": 0, "swiglu_oai": 1}[kind], alpha, limit)
         check(lib().msb_moe_ffn_ex(gate.handle, up.handle, up_row0, down.handle, _ptr(x),
                                    _ACT_TYPES[x.dtype], x.stride(0) * x.element_size(),
                                    ctypes.byref(route.c), _ptr(w), top_k, n_tok, _ptr(out),
-                                   _ptr(act), ctypes.byref(cfg), ctypes.byref(bc), _ptr(ws),
-                                   ws.numel(), _stream(stream)))
+                                   _ptr(act), ctypes.byref(cfg),
+                                   ctypes.byref(bc) if bc is not None else None,
+                                   1 if accumulate else 0, _ptr(ws), ws.numel(), _stream(stream)))
         return out
     if activation is None:
         check(lib().msb_moe_ffn(gate.handle, up.handle, up_row0, down.handle, _ptr(x),

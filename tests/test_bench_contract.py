@@ -43,3 +43,8 @@ def test_reference_arm_times_every_layer_of_every_step():
     assert "every step whole: 2 layers" in d["cpu_baseline"]["sample"]
     assert d["e2e"]["h2d_bytes_per_step"] == 0
     assert d["steps"] * d["ms_per_step"] / 1e3 < wall
+
+
+def test_prefill_workload_is_one_gpu_only():
+    d = _run("--workload", "prefill", "--gpus", "2")
+    assert d["workload"] == "prefill" and "unavailable" in d
