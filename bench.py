@@ -65,6 +65,13 @@ def parse():
                          "prefill: 512-token Zipf prompt batches with ~30%% of each layer's "
                          "experts filled from pinned host memory during the grouped GEMM "
                          "(1 GPU)")
+    ap.add_argument("--passes", default="auto", choices=["auto", "narrow", "wide"],
+                    help="tensor-core passes per weight tile: by batch size (8 or 24 pairs), "
+                         "always 8, or always 24 (MSB_OPT_WIDE_PASSES)")
+    ap.add_argument("--iq4nl", default="auto", choices=["auto", "cuda", "tc"],
+                    help="IQ4_NL arithmetic: tensor cores for prompt-sized batches (auto), the "
+                         "CUDA-core q8_0 form, or the tensor cores wherever shapes allow "
+                         "(MSB_OPT_IQ4NL_PATH)")
     ap.add_argument("--miss-frac", type=float, default=0.3,
                     help="prefill: fraction of each layer's referenced experts not resident")
     ap.add_argument("--model", default="gpt-oss", choices=["gpt-oss", "iq4nl-256e"],
@@ -637,7 +644,9 @@ def slots_main(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "us_per_layer": ms * 1e3 / args.steps / L,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "mxfp4 x bf16 as 4 e2m1 terms per 32-block -> f32" if wtype == "mxfp4" else "iq4_nl x q8_0 -> f32",
+            "dtype": ("mxfp4 x bf16 as 4 e2m1 terms per 32-block -> f32" if wtype == "mxfp4"
+                      else "iq4_nl x q8_0 -> f32 (CUDA cores) or f16 x f16 -> f32 (tensor cores, "
+                           "prompt-sized batches)"),
             "data": "synthetic",
             "config": {"workload": f"{args.model} MoE FFN decode over {NS}-slot pools, every "
                                    "referenced expert resident",
@@ -859,6 +868,14 @@ def prefill_main(args):
 
 def main():
     args = parse()
+    if args.impl == "msb" and args.passes != "auto":
+        from moestream_b200 import ops
+        from moestream_b200._lib import OPT_WIDE_PASSES
+        ops.check(ops.lib().msb_set_option(OPT_WIDE_PASSES, {"narrow": 1, "wide": 2}[args.passes]))
+    if args.impl == "msb" and args.iq4nl != "auto":
+        from moestream_b200 import ops
+        from moestream_b200._lib import OPT_IQ4NL_PATH
+        ops.check(ops.lib().msb_set_option(OPT_IQ4NL_PATH, {"cuda": 1, "tc": 2}[args.iq4nl]))
     if args.workload == "prefill":
         if args.gpus != 1 or args.impl != "msb":
             print(json.dumps({"workload": "prefill", "unavailable": "one GPU, --impl msb only"}))

@@ -442,6 +442,21 @@ int msb_ep_moe_ffn_peers(const msb_ep_peers_t *peers, msb_pool_t gate,
  * limit it was captured with). */
 #define MSB_OPT_MXFP4_PATH 1
 #define MSB_OPT_WAIT_LIMIT_US 2
+/* MSB_OPT_WIDE_PASSES: how many (token, k) pairs one tensor-core pass over a
+ * weight tile serves. 0 (default) = 24 when the batch has at least 12 pairs
+ * per slot it can reach (prompt-sized batches; one CTA per SM), else 8
+ * (decode; two CTAs per SM); 1 = always 8; 2 = always 24 (except where K is
+ * split over idle CTAs, batches of up to 8 pairs). The arithmetic is the
+ * same either way. */
+#define MSB_OPT_WIDE_PASSES 3
+/* MSB_OPT_IQ4NL_PATH selects the arithmetic of IQ4_NL mul_mat_id: 0
+ * (default) = tensor cores for batches with at least 8 pairs per slot they
+ * can reach (weights dequantized to fp16 d * kvalue in shared memory,
+ * activations rounded to fp16, f32 accumulation; K a multiple of 64, rows a
+ * multiple of 8, gate/up views on 128-row boundaries), the CUDA-core path
+ * (q8_0 form) otherwise; 1 = the CUDA-core path everywhere; 2 = the tensor
+ * cores wherever the shapes allow. */
+#define MSB_OPT_IQ4NL_PATH 4
 int msb_set_option(int option, int value);
 
 /* Kernels this library has launched in this process (all threads). */

@@ -19,6 +19,8 @@ ORIGIN_DEMAND, ORIGIN_PREFETCH_HIGH, ORIGIN_PREFETCH_LOW, ORIGIN_SWEEP = 0, 1, 2
 NO_SLOT = 0xFFFFFFFF
 OPT_MXFP4_PATH = 1
 OPT_WAIT_LIMIT_US = 2
+OPT_WIDE_PASSES = 3
+OPT_IQ4NL_PATH = 4
 ROUTER_SOFTMAX_TOPK, ROUTER_SOFTMAX_ALL = 0, 1
 
 c_i32p = ctypes.POINTER(ctypes.c_int32)

@@ -12,7 +12,7 @@ PKG = os.path.dirname(HERE)
 OUT = os.path.join(PKG, "libmsb.so")
 BUILD = os.path.join(PKG, "_build")
 
-SOURCES = ["host_api.cpp", "expert_cache.cpp", "pool.cu", "route.cu", "mmid.cu", "mmid_tc.cu", "ep.cu", "ep_peers.cu", "gguf.cpp", "arena.cpp", "router.cu", "dstreamer.cu"]
+SOURCES = ["host_api.cpp", "expert_cache.cpp", "pool.cu", "route.cu", "mmid.cu", "mmid_tc.cu", "mmid_f16.cu", "ep.cu", "ep_peers.cu", "gguf.cpp", "arena.cpp", "router.cu", "dstreamer.cu"]
 HEADERS = ["msb_internal.h", "dcache.cuh", "expert_cache.hpp", "pool.cuh", "quant.cuh", "sm100.cuh",
            os.path.join("..", "..", "include", "msb.h")]
 

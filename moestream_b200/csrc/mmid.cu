@@ -37,6 +37,18 @@ int64_t tc_act_bytes(int64_t nb, int64_t rows);
 // small): partial sums of up to two views with n_out_max rows.
 int64_t tc_split_bytes(int64_t n_out_max, int64_t n_pairs);
 int tc_supported(const msb_pool_s *p);
+int set_wide_policy(int v);
+// IQ4_NL on the tensor cores (mmid_f16.cu).
+int64_t f16_act_bytes(int64_t K, int64_t rows);
+int f16_supported(const msb_pool_s *p);
+int f16_act(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb2, int32_t top_k,
+            const int32_t *rows, int64_t n_pairs, int64_t K, void *xo, cudaStream_t st,
+            uint32_t *zero, int64_t zero_n);
+int f16_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, int64_t n_out,
+                   const msb_route_t *route, int64_t n_pairs, const void *x_in, float *res,
+                   void *x_out, float *act_f32, int max_active, cudaStream_t st,
+                   const RowTarget *res_rows, const FfnAct *fa, const FfnBias *bias,
+                   const Combine *comb);
 int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb2, int32_t top_k,
                  const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st,
                  uint32_t *zero = nullptr, int64_t zero_n = 0);
@@ -50,6 +62,18 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
 // MXFP4 arithmetic: 0 = tensor cores where the shapes allow, 1 = CUDA cores
 // with int8 activations (ggml's q8_0 form) everywhere.
 static int g_mxfp4_path = 0;
+
+// IQ4_NL arithmetic: 0 = tensor cores (f16 dequantization) for prompt-sized
+// batches where the shapes allow, CUDA cores otherwise; 1 = CUDA cores
+// everywhere; 2 = tensor cores wherever the shapes allow.
+static int g_iq4nl_path = 0;
+constexpr int64_t kF16PairsPerSlot = 8;
+
+static bool use_f16(int64_t pairs, int max_active) {
+  if (g_iq4nl_path == 1) return false;
+  if (g_iq4nl_path == 2) return true;
+  return pairs >= kF16PairsPerSlot * max_active;
+}
 
 // Bound of every device wait, in nanoseconds (MSB_OPT_WAIT_LIMIT_US).
 static std::atomic<int64_t> g_wait_ns{1000000000};
@@ -467,13 +491,28 @@ extern "C" int64_t msb_workspace_bytes(int64_t K_max, int32_t n_tok, int32_t top
   // Split over K of small batches: partial sums (the largest projection
   // mul_mat_id serves has 2 K_max rows: a fused gate_up).
   tcb = align_up(tcb + tc_split_bytes(2 * K_max, pairs), 256);
-  return (q8 > tcb ? q8 : tcb) + 256;
+  // IQ4_NL tensor-core path: f16 activations in and SwiGLU out, down result,
+  // the combine's counters.
+  int64_t f16b = 0;
+  f16b = align_up(f16b + f16_act_bytes(K_max, pairs), 256);
+  f16b = align_up(f16b + f16_act_bytes(K_max, pairs), 256);
+  f16b = align_up(f16b + pairs * K_max * 4, 256);
+  f16b += cnt;
+  int64_t need = q8 > tcb ? q8 : tcb;
+  if (f16b > need) need = f16b;
+  return need + 256;
 }
 
 extern "C" int msb_set_option(int option, int value) {
   if (option == MSB_OPT_MXFP4_PATH) {
     MSB_CHECK_ARG(value == 0 || value == 1, "msb_set_option: MXFP4 path must be 0 or 1");
     g_mxfp4_path = value;
+    return MSB_OK;
+  }
+  if (option == MSB_OPT_WIDE_PASSES) return set_wide_policy(value);
+  if (option == MSB_OPT_IQ4NL_PATH) {
+    MSB_CHECK_ARG(value >= 0 && value <= 2, "msb_set_option: IQ4_NL path must be 0, 1 or 2");
+    g_iq4nl_path = value;
     return MSB_OK;
   }
   if (option == MSB_OPT_WAIT_LIMIT_US) {
@@ -514,6 +553,17 @@ extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, in
     const int64_t used = align_up(tc_act_bytes(pool->nb, pairs), 256);
     return tc_projection(pools, 1, row0, pool->N, route, pairs, act, res_dev, nullptr, nullptr,
                          max_active, st, nullptr, nullptr, ws + used, workspace_bytes - used);
+  }
+  if (f16_supported(pool) && use_f16(pairs, max_active)) {
+    // Tensor cores: f16 activations per pair (grouped order), then one
+    // projection writing res directly.
+    if (int rc = f16_act(b_dev, b_type, b_ne1, b_nb1, b_nb2, top_k, route->rows, pairs, pool->K,
+                         ws, st, nullptr, 0))
+      return rc;
+    const int64_t row0[2] = {0, 0};
+    const msb_pool_s *pools[2] = {pool, pool};
+    return f16_projection(pools, 1, row0, pool->N, route, pairs, ws, res_dev, nullptr, nullptr,
+                          max_active, st, nullptr, nullptr, nullptr, nullptr);
   }
   const int64_t n_rows = int64_t(n_tok) * b_ne1;
   ActQ8 in = carve_act(ws, &off, n_rows, pool->nb);
@@ -648,6 +698,49 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
     const msb_pool_s *dn_pools[2] = {down, down};
     return tc_projection(dn_pools, 1, rows_dn, down->N, route, pairs, ha, rd, nullptr, nullptr,
                          max_active, st, rows, nullptr, split_ws, split_bytes, &bias_dn, &comb);
+  }
+  const bool f16 = !rows && f16_supported(gate) && f16_supported(up) && f16_supported(down) &&
+                   up_row0 % 128 == 0 && use_f16(pairs, max_active);
+  if (f16) {
+    // Tensor cores with f16 dequantization: x in f16 per pair -> gate/up +
+    // activation writing the down projection's f16 input -> down with the
+    // combine.
+    int64_t o = 0;
+    uint8_t *xa = ws + o;
+    o = align_up(o + f16_act_bytes(K, pairs), 256);
+    uint8_t *ha = ws + o;
+    o = align_up(o + f16_act_bytes(n_ff, pairs), 256);
+    float *rd = w_dev ? reinterpret_cast<float *>(ws + o) : y_dev;
+    o = align_up(o + pairs * down->N * 4, 256);
+    uint32_t *cnt = reinterpret_cast<uint32_t *>(ws + o);
+    if (w_dev) {
+      comb.w = w_dev;
+      comb.y = y_dev;
+      comb.r = rd;
+      comb.cnt = cnt;
+      comb.top_k = top_k;
+      comb.n_out = down->N;
+      comb.nblk = (down->N + 31) / 32;
+      comb.accumulate = accumulate;
+    }
+    if (int rc = f16_act(x_dev, x_type, 1, x_nb1, x_nb1, top_k, route->rows, pairs, K, xa, st,
+                         w_dev ? cnt : nullptr, cnt_n))
+      return rc;
+    const int64_t rows_gu[2] = {0, up_row0};
+    const msb_pool_s *gu_pools[2] = {gate, up};
+    const bool timed = g_gate_up_start && g_gate_up_stop;
+    if (timed) MSB_CUDA_TRY(record_timing_event(g_gate_up_start, st));
+    if (int rc = f16_projection(gu_pools, 2, rows_gu, n_ff, route, pairs, xa, nullptr, ha,
+                                act_dev, max_active, st, nullptr, &fa, &bias_gu, nullptr))
+      return rc;
+    if (timed) {
+      MSB_CUDA_TRY(record_timing_event(g_gate_up_stop, st));
+      g_gate_up_start = g_gate_up_stop = nullptr;
+    }
+    const int64_t rows_dn[2] = {0, 0};
+    const msb_pool_s *dn_pools[2] = {down, down};
+    return f16_projection(dn_pools, 1, rows_dn, down->N, route, pairs, ha, rd, nullptr, nullptr,
+                          max_active, st, nullptr, nullptr, &bias_dn, &comb);
   }
   int64_t off = 0;
   ActQ8 xq = carve_act(ws, &off, n_tok, gate->nb);

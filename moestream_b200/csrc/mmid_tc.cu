@@ -62,22 +62,32 @@ namespace msb {
 namespace tc {
 
 constexpr int kTerms = 4;        // e2m1 terms per activation block
-constexpr int kPairs = 8;        // (token, k) pairs per pass
-constexpr int kN = kTerms * kPairs;   // MMA N: the pass's terms stacked
 constexpr int kChunk = 4;        // 32-element blocks per stage (two K=64 MMAs)
-constexpr int kThreads = 256;    // producer warp, 3 MMA warps, 4 epilogue warps
+constexpr int kThreads = 256;    // producer warp, 2-3 MMA warps, 4 epilogue warps
 constexpr int kMaxActive = 1024; // slots (with the zero slot) one launch can walk
 
 // Shapes of one launch with NV weight views (2: gate and up); a work item
-// is one pass of up to kPairs pairs over one 128-row weight tile. (Feeding
-// four passes' accumulators from one staged tile -- one CTA per SM,
-// single-buffered tensor memory -- ran a 2048-token layer 1.4x slower: the
-// four passes' epilogue serialized with the MMAs.)
-template <int NV>
+// is one pass of up to kPairs pairs over one 128-row weight tile.
+//   narrow (W false): 8 pairs per pass (MMA N = 32), two CTAs per SM with
+//     256 tensor-memory columns each -- decode batches, where a slot has a
+//     few pairs and many CTAs streaming different tiles keep HBM busy;
+//   wide (W true): 24 pairs per pass (N = 96), one CTA per SM with all 512
+//     columns (two accumulator buffers of 2 x 96 columns plus each stage's
+//     scale factors) -- prompt-sized batches, where a tile's weights are
+//     streamed once per pass and 3x fewer passes mean 3x fewer re-reads.
+// (Feeding four narrow passes' accumulators from one staged tile -- one CTA
+// per SM, single-buffered tensor memory -- ran a 2048-token layer 1.4x
+// slower: the four passes' epilogue serialized with the MMAs.)
+template <int NV, bool W>
 struct Cfg {
-  // Two CTAs per SM, double-buffered accumulators.
-  static constexpr int kCtasPerSm = 2;
-  static constexpr int kStages = NV == 2 ? 5 : 8;
+  static constexpr int kPairs = W ? 24 : 8;              // (token, k) pairs per pass
+  static constexpr int kN = kTerms * kPairs;             // MMA N: the pass's terms stacked
+  static constexpr int kCtasPerSm = W ? 1 : 2;
+  // MMA-issuing warps: one per view (gate and up), or two / three taking
+  // turns over the stages of a single view. One accumulator buffer holds one
+  // N = kN accumulator per MMA warp.
+  static constexpr int kMma = NV == 2 ? 2 : (W ? 2 : 3);
+  static constexpr int kStages = W ? (NV == 2 ? 7 : 12) : (NV == 2 ? 5 : 8);
   static constexpr int kA = NV * kChunk * 2048;          // 128 rows x 16 B per block
   // Scale factors of a weight view: one 512-byte chunk per 128-row tile of
   // the pool. A view whose first row is not on a tile boundary (the up half
@@ -85,26 +95,33 @@ struct Cfg {
   // with two views there is room for both.
   static constexpr int kSfaView = NV == 2 ? 1024 : 512;
   static constexpr int kSFA = NV * kSfaView;
-  static constexpr int kBPass = kChunk * kN * 16;        // [block][pair][term] 16 B rows
-  static constexpr int kB = kBPass;
-  static constexpr int kSFB = 512;                       // [pair][term] 16 B rows
-  static constexpr int kStage = kA + kSFA + kB + kSFB;
+  static constexpr int kB = kChunk * kN * 16;            // [block][pair][term] 16 B rows
+  // The activation terms' scale records of the pass, [pair][term] 16 B rows
+  // (the 4 block scales in the first word). With 8 pairs they are the MMA's
+  // 32-row scale atom as they stand; with 24 each MMA warp gathers rows
+  // 32j + l into word j of atom row l (kSfbAtom).
+  static constexpr int kSfbRec = kN * 16;
+  static constexpr int kSfbAtom = W ? 512 * kMma : 0;
+  static constexpr int kStage = kA + kSFA + kB + kSfbRec + kSfbAtom;
   static constexpr int kBarOff = kStages * kStage;
   static constexpr int kItemOff = kBarOff + 256;           // item prefix, kMaxActive + 1 ints
-  static constexpr int kSmem = kItemOff + (kMaxActive + 1) * 4;
-  // MMA-issuing warps: one per view (gate and up), or three taking turns
-  // over the stages of a single view. One accumulator buffer holds one N=32
-  // accumulator per MMA warp.
-  static constexpr int kMma = NV == 2 ? 2 : 3;
+  // Gate/up epilogue: each epilogue warp stages the activation of one
+  // 8-pair group over its 32 rows ([pair][row] f32) to re-split it with 4
+  // lanes per 32-row block.
+  static constexpr int kStageHOff = kItemOff + (kMaxActive + 1) * 4;
+  static constexpr int kStageH = NV == 2 ? 4 * 8 * 32 * 4 : 0;
+  static constexpr int kSmem = kStageHOff + kStageH;
   static constexpr int kAccCols = kMma * kN;
   // TMEM columns per stage: each MMA warp's scale factors (A then B).
   static constexpr int kSfCols = NV == 2 ? 16 : 8;
-  static constexpr int kTmemCols = 256;
+  static constexpr int kTmemCols = W ? 512 : 256;
   static constexpr int kAccBufs = 2 * kAccCols + kStages * kSfCols <= kTmemCols ? 2 : 1;
   static constexpr int kSfBase = kAccBufs * kAccCols;    // after the buffers
   static_assert(kSfBase + kStages * kSfCols <= kTmemCols, "tensor memory map");
+  static_assert(kAccBufs == 2, "double-buffered accumulators");
   static_assert(kCtasPerSm * (kSmem + 1024) <= 228 * 1024, "shared memory per SM");
   static_assert(kStage % 128 == 0, "TMA destinations stay 128-byte aligned");
+  static_assert(kPairs % 8 == 0 && kPairs <= 32, "passes of whole 8-pair column groups");
 };
 
 struct Args {
@@ -141,11 +158,6 @@ struct Args {
   FfnBias bias;              // expert biases of each view (optional)
   Combine comb;              // one view: the fused router-weighted combine (optional)
 };
-
-__device__ __forceinline__ float *out_row(const RowTarget &t, int64_t r) {
-  const int64_t b = r / t.cap;
-  return t.blk[b] + (r - b * t.cap) * t.ld;
-}
 
 // Status bits of the tensor-core kernels on this device (see
 // msb_device_status): which bounded wait gave up.
@@ -233,6 +245,51 @@ __device__ __forceinline__ void group_e2m1_terms(float (&r)[4], int l, bool stor
       *reinterpret_cast<uint16_t *>(q_t0 + t * q_step + 2 * l) =
           uint16_t(nib[0] | (nib[2] << 4) | (nib[1] << 8) | (nib[3] << 12));
       if (l == 0) sf_t0[t * sf_step] = skip ? uint8_t(0) : uint8_t(k > 127 ? 254 : k + 127);
+    }
+  }
+}
+
+// The same split with 4 lanes per block: lane s of the group holds elements
+// 4s..4s+3 and 4s+16..4s+19 (r[0..3] and r[4..7]) and writes packed bytes
+// 4s..4s+3 of each term as one word. Called by the lanes of `mask`, whole
+// 4-lane groups (the amax reduction shuffles within each group).
+__device__ __forceinline__ void group4_e2m1_terms(float (&r)[8], int sub, unsigned mask,
+                                                  uint8_t *q_t0, int64_t q_step, uint8_t *sf_t0,
+                                                  int64_t sf_step) {
+#pragma unroll
+  for (int t = 0; t < kTerms; ++t) {
+    float amax = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(r[e]));
+    amax = fmaxf(amax, __shfl_xor_sync(mask, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(mask, amax, 2));
+    int k = -127;
+    if (amax > 0.f) {
+      int ex;
+      const float m = frexpf(amax, &ex);
+      k = m > 0.75f ? ex - 2 : ex - 3;
+    }
+    const bool skip = k < -126;
+    uint32_t nib[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      int code = 0, neg = 0;
+      if (!skip) {
+        const float v = fabsf(r[e]) * __int_as_float((127 - k) << 23);  // exact
+        code = (v >= 0.25f) + (v >= 0.75f) + (v >= 1.25f) + (v >= 1.75f) + (v >= 2.5f) +
+               (v >= 3.5f) + (v >= 5.f);
+        neg = (r[e] < 0.f) && code > 0;
+        const float mag = code < 5 ? 0.5f * code : (code == 5 ? 3.f : (code == 6 ? 4.f : 6.f));
+        const float q = mag * __int_as_float((k + 127) << 23);          // exact
+        r[e] = neg ? r[e] + q : r[e] - q;                               // exact
+      }
+      nib[e] = uint32_t(code | (neg << 3));
+    }
+    {
+      const uint32_t w = (nib[0] | (nib[4] << 4)) | ((nib[1] | (nib[5] << 4)) << 8) |
+                         ((nib[2] | (nib[6] << 4)) << 16) | ((nib[3] | (nib[7] << 4)) << 24);
+      *reinterpret_cast<uint32_t *>(q_t0 + t * q_step + 4 * sub) = w;
+      if (sub == 0) sf_t0[t * sf_step] = skip ? uint8_t(0) : uint8_t(k > 127 ? 254 : k + 127);
     }
   }
 }
@@ -325,9 +382,11 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant
   }
 }
 
-template <int NV>
-__global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__ Args a) {
-  using C = Cfg<NV>;
+template <int NV, bool W>
+__global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_constant__ Args a) {
+  using C = Cfg<NV, W>;
+  constexpr int kPairs = C::kPairs;
+  constexpr int kN = C::kN;
   constexpr int kStages = C::kStages;
   constexpr int kBufs = C::kAccBufs;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -438,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
           // arrive as zeros); a window off the tile grid also takes the next
           // tile's scale chunk when the pool has one.
           bool next_sf[NV];
-          uint32_t tx = uint32_t(C::kA + C::kB + C::kSFB);
+          uint32_t tx = uint32_t(C::kA + C::kB + C::kSfbRec);
           for (int v = 0; v < NV; ++v) {
             const int64_t r0 = a.row0[v] + item.n0;
             next_sf[v] = NV == 2 && (r0 & 127) != 0 && (r0 >> 7) + 1 < (a.N[v] + 127) / 128;
@@ -528,12 +587,24 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
             *reinterpret_cast<uint4 *>(sfa_v + lane * 16) = o;
             sm100::fence_proxy_async_smem();
           }
+          const uint8_t *sfb = sSFB;
+          if constexpr (W) {
+            // Scale atom of the pass's 96 B rows: word j of row l is the
+            // record of B row 32j + l (rows 96-127 do not exist: scale 0).
+            uint8_t *atom = sSFB + C::kSfbRec + m * 512;
+            const uint4 o = make_uint4(*reinterpret_cast<const uint32_t *>(sSFB + lane * 16),
+                                       *reinterpret_cast<const uint32_t *>(sSFB + (32 + lane) * 16),
+                                       *reinterpret_cast<const uint32_t *>(sSFB + (64 + lane) * 16),
+                                       0u);
+            *reinterpret_cast<uint4 *>(atom + lane * 16) = o;
+            sm100::fence_proxy_async_smem();
+            sfb = atom;
+          }
           __syncwarp();
           if (lane == 0) {
             const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols + (NV == 2 ? m * 8 : 0);
             sm100::tmem_cp_32x128b_x4(sf_col, sm100::smem_desc(sm100::smem_u32(sfa_v), 0, 128));
-            sm100::tmem_cp_32x128b_x4(sf_col + 4,
-                                      sm100::smem_desc(sm100::smem_u32(sSFB), 0, 128));
+            sm100::tmem_cp_32x128b_x4(sf_col + 4, sm100::smem_desc(sm100::smem_u32(sfb), 0, 128));
             const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
             for (int j = 0; j < kbn / 2; ++j) {
               const uint32_t sel = uint32_t(2 * j);
@@ -564,6 +635,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
   } else {
     // ---- epilogue (warps 4-7) ----
     const int quad = warp & 3;            // TMEM lane quadrant of this warp
+    float *sh = reinterpret_cast<float *>(smem + C::kStageHOff) + quad * 8 * 32;
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     uint32_t acc = 0;
     int cur = 0;
@@ -621,70 +693,99 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
         const int cc = min(kPairs, c_total - g0);
         const int64_t pos = pos0 + g0;
         const uint32_t col = tmem + lane_addr + buf * C::kAccCols;
-        uint32_t dg[32], du[32];
-        sm100::tmem_ld_32cols(col, dg);
-        if (NV == 2 || n_chunks > 1) sm100::tmem_ld_32cols(col + kN, du);
-        sm100::tmem_ld_wait();
-        if constexpr (NV == 1) {
-          // The MMA warps' accumulators (stages i % 3 = 0, 1, 2), added in
-          // that order; a warp that had no stage holds nothing.
-          if (n_chunks > 1) {
-#pragma unroll
-            for (int c = 0; c < kN; ++c)
-              dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
-          }
-          if (n_chunks > 2) {
-            sm100::tmem_ld_32cols(col + 2 * kN, du);
-            sm100::tmem_ld_wait();
-#pragma unroll
-            for (int c = 0; c < kN; ++c)
-              dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
-          }
-        }
-        {
-          // Every accumulator of the item is in registers: release the buffer.
-          sm100::tc_fence_before();
-          __syncwarp();
-          if (lane == 0)
-            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
-                             sm100::smem_u32(&acc_empty[buf]))
-                         : "memory");
-        }
-#pragma unroll
-        for (int j = 0; j < kPairs; ++j) {
-          if (j >= cc) break;
-          const int64_t pair = a.rows[pos + j];
-          // Column 4j + t holds term t of pair j.
-          const float gv = (__uint_as_float(dg[4 * j]) + __uint_as_float(dg[4 * j + 1])) +
-                           (__uint_as_float(dg[4 * j + 2]) + __uint_as_float(dg[4 * j + 3]));
-          float u = 0.f;
-          if constexpr (NV == 2)
-            u = (__uint_as_float(du[4 * j]) + __uint_as_float(du[4 * j + 1])) +
-                (__uint_as_float(du[4 * j + 2]) + __uint_as_float(du[4 * j + 3]));
-          if (split_mode) {
-            // This segment's partial sums; the split reduce finishes.
-            if (valid) {
-              a.part[((seg * NV) * a.a_rows + pos + j) * a.n_out + n] = gv;
-              if constexpr (NV == 2) a.part[((seg * NV + 1) * a.a_rows + pos + j) * a.n_out + n] = u;
-            }
-            continue;
-          }
+        const int n_groups = (cc + 7) / 8;   // 8-pair column groups this pass uses
+        for (int gq = 0; gq < n_groups; ++gq) {
+          // Group gq: columns 32 gq .. +31 of each accumulator (column
+          // 4j + t of the group holds term t of the group's pair j).
+          uint32_t dg[32], du[32];
+          sm100::tmem_ld_32cols(col + gq * 32, dg);
+          if (NV == 2 || n_chunks > 1) sm100::tmem_ld_32cols(col + kN + gq * 32, du);
+          sm100::tmem_ld_wait();
           if constexpr (NV == 1) {
-            if (valid) {
-              const float *br = bias_row(a.bias, 0, pair);
-              out_row(a.out, pair)[n] = br ? gv + br[n] : gv;
+            // The MMA warps' accumulators (stages i % kMma = 0, 1, 2), added
+            // in that order; a warp that had no stage holds nothing.
+            if (n_chunks > 1) {
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
             }
-          } else {
-            float gb = gv, ub = u;
-            if (valid) {
-              if (const float *br = bias_row(a.bias, 0, pair)) gb += br[n];
-              if (const float *br = bias_row(a.bias, 1, pair)) ub += br[n];
+            if (C::kMma > 2 && n_chunks > 2) {
+              sm100::tmem_ld_32cols(col + 2 * kN + gq * 32, du);
+              sm100::tmem_ld_wait();
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
             }
-            const float h = valid ? ffn_act(a.fa, gb, ub) : 0.f;
-            if (a.act && valid) a.act[pair * a.n_out + n] = h;
-            if (blk < a.o_nb)
-              warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, pos + j), 16,
-                              a.osf + a4_off(0, blk / 4, a.a_rows, pos + j) + (blk & 3), 16);
+          }
+          if (gq == n_groups - 1) {
+            // Every accumulator of the item is in registers: release the buffer.
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+              asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                               sm100::smem_u32(&acc_empty[buf]))
+                           : "memory");
+          }
+          // The group's pairs: lane j holds the j-th (one load for all).
+          const int gcc = min(8, cc - gq * 8);
+          const int64_t my_pair = lane < gcc ? a.rows[pos + gq * 8 + lane] : 0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (j >= gcc) break;   // same on every lane
+            const int jj = gq * 8 + j;
+            const int64_t pair = __shfl_sync(0xffffffffu, my_pair, j);
+            const float gv = (__uint_as_float(dg[4 * j]) + __uint_as_float(dg[4 * j + 1])) +
+                             (__uint_as_float(dg[4 * j + 2]) + __uint_as_float(dg[4 * j + 3]));
+            float u = 0.f;
+            if constexpr (NV == 2)
+              u = (__uint_as_float(du[4 * j]) + __uint_as_float(du[4 * j + 1])) +
+                  (__uint_as_float(du[4 * j + 2]) + __uint_as_float(du[4 * j + 3]));
+            if (split_mode) {
+              // This segment's partial sums; the split reduce finishes.
+              if (valid) {
+                a.part[((seg * NV) * a.a_rows + pos + jj) * a.n_out + n] = gv;
+                if constexpr (NV == 2)
+                  a.part[((seg * NV + 1) * a.a_rows + pos + jj) * a.n_out + n] = u;
+              }
+              continue;
+            }
+            if constexpr (NV == 1) {
+              if (valid) {
+                const float *br = bias_row(a.bias, 0, pair);
+                out_row(a.out, pair)[n] = br ? gv + br[n] : gv;
+              }
+            } else {
+              float gb = gv, ub = u;
+              if (valid) {
+                if (const float *br = bias_row(a.bias, 0, pair)) gb += br[n];
+                if (const float *br = bias_row(a.bias, 1, pair)) ub += br[n];
+              }
+              const float h = (valid) ? ffn_act(a.fa, gb, ub) : 0.f;
+              if (a.act && valid) a.act[pair * a.n_out + n] = h;
+              sh[j * 32 + lane] = h;
+            }
+          }
+          if constexpr (NV == 2) {
+            if (!split_mode && blk < a.o_nb) {
+              // The down projection's terms of this warp's 32-row block for
+              // the group's pairs: 4 lanes per pair (lane 4j + s holds
+              // elements 4s..4s+3 and 4s+16..4s+19 of pair j).
+              __syncwarp();
+              const int j = lane >> 2, sub = lane & 3;
+              if (j < gcc) {
+                const unsigned mask = gcc == 8 ? 0xffffffffu : (1u << (4 * gcc)) - 1u;
+                float r[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  r[e] = sh[j * 32 + 4 * sub + e];
+                  r[4 + e] = sh[j * 32 + 16 + 4 * sub + e];
+                }
+                const int64_t p_row = pos + gq * 8 + j;
+                group4_e2m1_terms(r, sub, mask, a.oq + a4_off(0, blk, a.a_rows, p_row), 16,
+                                  a.osf + a4_off(0, blk / 4, a.a_rows, p_row) + (blk & 3), 16);
+              }
+              __syncwarp();
+            }
           }
         }
         // The pass's rows of this 32-row block are stored: count them.
@@ -726,6 +827,22 @@ __global__ void __launch_bounds__(kThreads, 2) tc_kernel(const __grid_constant__
 constexpr int64_t kSplitPairs = 8;
 constexpr int kSplitMax = 4;
 
+// Wide passes: 0 = by batch size (MSB_OPT_WIDE_PASSES), 1 = never, 2 = always.
+static int g_wide_policy = 0;
+constexpr int64_t kWidePairsPerSlot = 12;
+
+static bool wide_passes_enabled(int64_t n_pairs, int64_t max_active) {
+  if (g_wide_policy == 1) return false;
+  if (g_wide_policy == 2) return true;
+  return n_pairs >= kWidePairsPerSlot * max_active;
+}
+
+int set_wide_policy(int v) {
+  if (v < 0 || v > 2) return fail(MSB_ERR_INVALID, "msb_set_option: wide passes must be 0, 1 or 2");
+  g_wide_policy = v;
+  return MSB_OK;
+}
+
 int64_t tc_split_bytes(int64_t n_out_max, int64_t n_pairs) {
   return n_pairs > 0 && n_pairs <= kSplitPairs ? 256 + 2 * kSplitMax * n_pairs * n_out_max * 4 : 0;
 }
@@ -759,10 +876,10 @@ int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb
   return MSB_OK;
 }
 
-template <int NV>
+template <int NV, bool W>
 static int launch_tc_t(const tc::Args &a, int max_active, int64_t n_pairs, cudaStream_t st) {
-  using C = tc::Cfg<NV>;
-  MSB_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<NV>,
+  using C = tc::Cfg<NV, W>;
+  MSB_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<NV, W>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
   // Persistent grid: as many CTAs as fit (shared and tensor memory), never
   // more than the work items the route can produce (each active slot has at
@@ -773,11 +890,11 @@ static int launch_tc_t(const tc::Args &a, int max_active, int64_t n_pairs, cudaS
     MSB_CUDA_TRY(cudaGetDevice(&dev));
     MSB_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
   }
-  const int64_t passes = int64_t(max_active) + n_pairs / tc::kPairs + 1;
+  const int64_t passes = int64_t(max_active) + n_pairs / C::kPairs + 1;
   int64_t grid = passes * a.tiles * (a.split_max > 0 ? a.split_max : 1);
   if (grid > int64_t(C::kCtasPerSm) * n_sm) grid = int64_t(C::kCtasPerSm) * n_sm;
   if (grid == 0) return MSB_OK;
-  MSB_CUDA_TRY(launch_pdl(tc::tc_kernel<NV>, dim3(unsigned(grid)), dim3(tc::kThreads), C::kSmem,
+  MSB_CUDA_TRY(launch_pdl(tc::tc_kernel<NV, W>, dim3(unsigned(grid)), dim3(tc::kThreads), C::kSmem,
                           st, a));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
@@ -854,25 +971,34 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
       a.slot_ids = route->slot_ids;
     }
   }
+  // Wide passes (24 pairs) for prompt-sized batches: when the pairs would
+  // fill at least kWidePairsPerSlot passes-worth per possibly active slot.
+  // Not for row targets (the expert-parallel exchange), whose rows are
+  // padded and few per expert.
+  const bool wide = a.split_max == 0 && !res_rows && wide_passes_enabled(n_pairs, max_active);
   {
     // A pair's four 16-byte term records of one block are 64 contiguous
-    // bytes (8 elements of 8 bytes); a box line is the 8 pairs of one pass
-    // and block -- 512 contiguous bytes. Boxes land as [block][pair][term]
-    // (terms) and [pair][term] (scales): B rows 4p + t.
+    // bytes (8 elements of 8 bytes); a box line is the pairs of one pass
+    // and block (512 or 1536 contiguous bytes). Boxes land as
+    // [block][pair][term] (terms) and [pair][term] (scales): B rows 4p + t.
+    const int pairs_per_pass = wide ? tc::Cfg<1, true>::kPairs : tc::Cfg<1, false>::kPairs;
     const uint64_t nc = uint64_t((pool->nb + 3) / 4);
     const uint64_t row_u64 = uint64_t(n_pairs) * tc::kTerms * 2;
     const uint64_t dq[3] = {row_u64, uint64_t(pool->nb), 1};
     const uint64_t sq[2] = {row_u64 * 8, row_u64 * 8 * uint64_t(pool->nb)};
-    const uint32_t bq[3] = {uint32_t(tc::kPairs * tc::kTerms * 2), uint32_t(tc::kChunk), 1};
+    const uint32_t bq[3] = {uint32_t(pairs_per_pass * tc::kTerms * 2), uint32_t(tc::kChunk), 1};
     const uint64_t df[3] = {row_u64, nc, 1};
     const uint64_t sf[2] = {row_u64 * 8, row_u64 * 8 * nc};
-    const uint32_t bf[3] = {uint32_t(tc::kPairs * tc::kTerms * 2), 1, 1};
+    const uint32_t bf[3] = {uint32_t(pairs_per_pass * tc::kTerms * 2), 1, 1};
     if (!encode_tmap_u64_3d(&a.tm_aq, a.aq, dq, sq, bq) ||
         !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sf, bf))
       return fail(MSB_ERR_CUDA, "tensor-core path: activation tensor maps could not be encoded");
   }
-  return nv == 2 ? launch_tc_t<2>(a, max_active, n_pairs, st)
-                 : launch_tc_t<1>(a, max_active, n_pairs, st);
+  if (wide)
+    return nv == 2 ? launch_tc_t<2, true>(a, max_active, n_pairs, st)
+                   : launch_tc_t<1, true>(a, max_active, n_pairs, st);
+  return nv == 2 ? launch_tc_t<2, false>(a, max_active, n_pairs, st)
+                 : launch_tc_t<1, false>(a, max_active, n_pairs, st);
 }
 
 }  // namespace msb

@@ -212,6 +212,12 @@ __device__ __forceinline__ void combine_arrive(const Combine &c, int64_t my_pair
   }
 }
 
+// Result row r of a RowTarget.
+__device__ __forceinline__ float *out_row(const RowTarget &t, int64_t r) {
+  const int64_t b = r / t.cap;
+  return t.blk[b] + (r - b * t.cap) * t.ld;
+}
+
 // Zeroes n words with every thread of the grid (grid-stride).
 __device__ __forceinline__ void grid_zero(uint32_t *p, int64_t n) {
   if (!p) return;

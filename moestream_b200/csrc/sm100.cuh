@@ -153,6 +153,19 @@ __device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64
       : "memory");
 }
 
+// D[128 x N] (+)= A[128 x 16] * B[N x 16]^T with f16 operands from shared
+// memory and f32 accumulation in TMEM (kind::f16).
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Each thread of a warp reads 32 consecutive columns of its lane
 // (lanes 32*(warp%4) .. +31).
 __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&v)[32]) {
@@ -187,6 +200,12 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
 __host__ __device__ constexpr uint32_t idesc_mxf4(uint32_t n, uint32_t sfa_id, uint32_t sfb_id) {
   return (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
          (sfa_id << 29) | (sfb_id << 4);
+}
+
+// Instruction descriptor of kind::f16: A and B f16 (format 0), both
+// K-major, f32 accumulator (bits 4-5 = 1), M = 128, given N (multiple of 16).
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t n) {
+  return (1u << 4) | ((n >> 3) << 17) | ((128u >> 4) << 24);
 }
 
 }  // namespace sm100

@@ -7,7 +7,7 @@ import ctypes
 
 import torch
 
-from ._lib import (OPT_MXFP4_PATH, TYPE_BF16, TYPE_F32, TYPE_IQ4_NL, TYPE_MXFP4, FfnActCfg,
+from ._lib import (OPT_MXFP4_PATH, OPT_WIDE_PASSES, TYPE_BF16, TYPE_F32, TYPE_IQ4_NL, TYPE_MXFP4, FfnActCfg,
                    FfnBiasCfg, PoolInfo, Route, c_vp, check, lib)
 
 WEIGHT_TYPES = {"iq4_nl": TYPE_IQ4_NL, "mxfp4": TYPE_MXFP4}
@@ -24,9 +24,11 @@ def _ptr(t):
 
 
 def set_mxfp4_path(path):
-    """'tc' (tensor cores where shapes allow, the default) or 'q8' (CUDA cores,
-    int8 activations)."""
-    check(lib().msb_set_option(OPT_MXFP4_PATH, {"tc": 0, "q8": 1}[path]))
+    """'tc' (tensor cores where shapes allow, passes of 8 or 24 pairs by batch
+    size: the default), 'tc_wide' (tensor cores, always 24-pair passes where
+    K is not split) or 'q8' (CUDA cores, int8 activations)."""
+    check(lib().msb_set_option(OPT_MXFP4_PATH, {"tc": 0, "tc_wide": 0, "q8": 1}[path]))
+    check(lib().msb_set_option(OPT_WIDE_PASSES, 2 if path == "tc_wide" else 0))
 
 
 def tc_eligible(wtype, K):

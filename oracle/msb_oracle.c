@@ -31,7 +31,9 @@
  *     tensor-core path for MXFP4: each 32-element block of activations is
  *     split into 4 terms, each 32 e2m1 codes with a power-of-two scale; the
  *     sum of the terms replaces the activations, and the products accumulate
- *     in f64.
+ *     in f64. A fourth, "f16", is the form of the IQ4_NL tensor-core path:
+ *     every weight d * kv and every activation rounded to fp16 (round to
+ *     nearest even), products accumulated in f64.
  *   - MoE FFN: research/spikes/s1_real_expert_stream/main.c:186-209 and
  *     research/spikes/s4_sweep_math/main.c:89-92 (SwiGLU, then down, then the
  *     router-weighted sum over k).
@@ -318,9 +320,11 @@ static void *mm_worker(void *arg) {
     const int32_t slot = j->ids[pair];
     const uint8_t *row = j->as + slot * j->slot_bytes + n * nb * bb;
     const int64_t arow = t * j->b_ne1 + (k % j->b_ne1);
-    if (j->mode == 0 || j->mode == 2) {
+    if (j->mode == 0 || j->mode == 2 || j->mode == 3) {
       orc_dequant_row(j->type, row, wrow, j->K);
-      const float *a = (j->mode == 2 ? j->bx : j->b) + arow * j->K;
+      if (j->mode == 3) /* f16 form: each weight d * kv rounded once to fp16 */
+        for (int64_t i = 0; i < j->K; ++i) wrow[i] = orc_f16_to_f32(orc_f32_to_f16(wrow[i]));
+      const float *a = (j->mode == 2 || j->mode == 3 ? j->bx : j->b) + arow * j->K;
       double s = 0.0;
       for (int64_t i = 0; i < j->K; ++i) s += (double)wrow[i] * (double)a[i];
       j->res[pair * j->N + n] = (float)s;
@@ -359,7 +363,8 @@ static void *mm_worker(void *arg) {
 }
 
 /* as: [n_slots][N][K/32 blocks] ggml bytes; b: f32 [T][b_ne1][K];
- * ids: slot ids [T][top_k]; res: f32 [T][top_k][N]. mode 0 exact, 1 q8. */
+ * ids: slot ids [T][top_k]; res: f32 [T][top_k][N]. mode 0 exact, 1 q8, 2 e2m1x4,
+ * 3 f16. */
 int orc_mul_mat_id(int type, const uint8_t *as, int64_t K, int64_t N, int64_t n_slots,
                    const float *b, int64_t b_ne1, const int32_t *ids, int top_k, int T,
                    int mode, float *res, int nthreads) {
@@ -379,6 +384,9 @@ int orc_mul_mat_id(int type, const uint8_t *as, int64_t K, int64_t N, int64_t n_
   } else if (mode == 2) {
     bx = (float *)malloc(sizeof(float) * (size_t)(rows * K));
     for (int64_t r = 0; r < rows; ++r) orc_e2m1_split(b + r * K, K, 4, bx + r * K, NULL, NULL);
+  } else if (mode == 3) {
+    bx = (float *)malloc(sizeof(float) * (size_t)(rows * K));
+    for (int64_t i = 0; i < rows * K; ++i) bx[i] = orc_f16_to_f32(orc_f32_to_f16(b[i]));
   }
   if (nthreads < 1) nthreads = 1;
   const int64_t items = (int64_t)T * top_k * N;

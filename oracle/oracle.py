@@ -239,7 +239,7 @@ def quantize_q8(x):
     return q, d
 
 
-MODES = {"exact": 0, "q8": 1, "e2m1x4": 2}
+MODES = {"exact": 0, "q8": 1, "e2m1x4": 2, "f16": 3}
 
 
 def e2m1_split(x, terms=4):

@@ -2,7 +2,9 @@
 
 Two arithmetic paths: MXFP4 with K a multiple of 64 runs on the tensor
 cores (activations as four e2m1 terms per block), everything else on the
-CUDA cores (int8 activations, ggml's q8_0 form); MXFP4 cases run both.
+CUDA cores (int8 activations, ggml's q8_0 form); MXFP4 cases run both, the
+tensor cores with passes chosen by batch size ("tc") and with 24-pair
+passes forced ("tc_wide").
 Tolerances (max |got - want| / max |want|):
   - vs the oracle in the path's own form: 1e-5 (q8; f32 block sums in
     another order) or 1e-4 (e2m1x4; f32 tensor-core accumulation);
@@ -25,7 +27,7 @@ TOL_TC = 1e-4
 TOL_EXACT = 1e-2
 
 
-@pytest.fixture(params=["tc", "q8"])
+@pytest.fixture(params=["tc", "tc_wide", "q8"])
 def path(request):
     from moestream_b200 import ops
     ops.set_mxfp4_path(request.param)
@@ -35,7 +37,7 @@ def path(request):
 
 def oracle_mode(wtype, K, path):
     from moestream_b200 import ops
-    return "e2m1x4" if path == "tc" and ops.tc_eligible(wtype, K) else "q8"
+    return "e2m1x4" if path.startswith("tc") and ops.tc_eligible(wtype, K) else "q8"
 
 
 def make_pool(wtype, K, N, n_slot, slab_bytes, slots):
