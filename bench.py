@@ -58,13 +58,14 @@ def parse():
     ap.add_argument("--eager", action="store_true",
                     help="launch every kernel from the host instead of replaying CUDA graphs")
     ap.add_argument("--workload", default="resident",
-                    choices=["resident", "streamed", "slots", "prefill"],
+                    choices=["resident", "streamed", "slots", "prefill", "single-op"],
                     help="resident: every expert in HBM (the default line); streamed: a slot "
                          "cache per layer with misses filled from pinned host memory (1 GPU); "
                          "slots: small decode batches over slot pools (1 GPU, --model); "
                          "prefill: 512-token Zipf prompt batches with ~30%% of each layer's "
                          "experts filled from pinned host memory during the grouped GEMM "
-                         "(1 GPU)")
+                         "(1 GPU); single-op: one IQ4_NL mul_mat_id over a 32-slot pool behind "
+                         "the slot streamer (1 GPU)")
     ap.add_argument("--passes", default="auto", choices=["auto", "narrow", "wide"],
                     help="tensor-core passes per weight tile: by batch size (8 or 24 pairs), "
                          "always 8, or always 24 (MSB_OPT_WIDE_PASSES)")
@@ -565,17 +566,26 @@ def slots_main(args):
     layers (MXFP4 2880 x 2880 gate, up and down, 32 slots, top-4) or a
     256-expert IQ4_NL model (hidden 2048, expert FFN 512, 64 slots, top-8).
     Weights quantized on the device from N(0, 0.02); ids are top_k distinct
-    random slots per token, new every step and layer. One CUDA graph per step;
-    the roofline counts each distinct referenced slot's bytes once per
-    layer."""
+    random slots per token, new every step and layer. A batch above the slot
+    pool's arena threshold (6 tokens for both models) runs over per-layer
+    arenas of every expert instead, routed over all of them, as the reference
+    runs it. One CUDA graph per step; the roofline counts each distinct
+    referenced slot's bytes once per layer."""
     import torch
 
     from moestream_b200 import ops
     if args.model == "gpt-oss":
-        wtype, K, n_ff, NS, top_k = "mxfp4", SHAPE["hidden"], SHAPE["n_ff"], 32, 4
+        wtype, K, n_ff, NS, top_k, E = "mxfp4", SHAPE["hidden"], SHAPE["n_ff"], 32, 4, 128
     else:
-        wtype, K, n_ff, NS, top_k = "iq4_nl", 2048, 512, 64, 8
+        wtype, K, n_ff, NS, top_k, E = "iq4_nl", 2048, 512, 64, 8, 256
     T, L = args.tokens, args.layers
+    # Batches the slot pool cannot serve (the reference's arena threshold,
+    # msb_arena_threshold) run as the reference runs them: over per-layer
+    # arenas holding every expert, routed over all of them.
+    threshold = int(ops.lib().msb_arena_threshold(E, top_k, NS))
+    arena = T > threshold
+    if arena:
+        NS = E
     t_setup = time.time()
     g = torch.Generator(device="cuda")
     g.manual_seed(77)
@@ -648,8 +658,11 @@ def slots_main(args):
                       else "iq4_nl x q8_0 -> f32 (CUDA cores) or f16 x f16 -> f32 (tensor cores, "
                            "prompt-sized batches)"),
             "data": "synthetic",
-            "config": {"workload": f"{args.model} MoE FFN decode over {NS}-slot pools, every "
-                                   "referenced expert resident",
+            "config": {"workload": (f"{args.model} MoE FFN decode over {NS}-slot pools, every "
+                                    "referenced expert resident" if not arena else
+                                    f"{args.model} MoE FFN decode of a batch above the slot "
+                                    f"pool's threshold ({threshold} tokens): per-layer arenas "
+                                    f"of all {E} experts"),
                        "n_layer": L, "slots": NS, "hidden": K, "n_ff": n_ff, "top_k": top_k,
                        "tokens": T, "distinct_per_layer": distinct / (args.steps * L),
                        "l2": "random slots every step and layer; pools far larger than L2"},
@@ -866,6 +879,109 @@ def prefill_main(args):
     return 0
 
 
+def single_op_main(args):
+    """--workload single-op: the single mul_mat_id op -- 128 IQ4_NL experts
+    [768 x 2048] quantized from N(0, 0.02), a 32-slot pool warmed with a
+    seeded subset, one f32 token per step whose top-8 of N(0, 1) router
+    logits go through the slot streamer (host remap, misses filled from
+    pinned host memory first, untimed), then the timed part: grouping and
+    mul_mat_id on the device. The roofline counts the 8 experts' bytes."""
+    import numpy as np
+    import torch
+
+    from moestream_b200 import SlotStreamer, ops
+    wtype, K, N, E, S_, top_k = "iq4_nl", 2048, 768, 128, 32, 8
+    T = args.tokens
+    t_setup = time.time()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    host = []
+    for j0 in range(0, E, 16):
+        wts = torch.randn(16 * N, K, generator=g, device="cuda") * 0.02
+        host.append(ops.quantize_rows(wtype, wts).view(16, -1).cpu())
+    host = torch.cat(host).pin_memory()
+    pool = ops.SlotPool(wtype, K, N, S_, max_fill_batch=8)
+    streamer = SlotStreamer(1, E, S_, pool.expert_bytes)
+    rng = np.random.default_rng(1)
+    subset = rng.permutation(E)[:S_].astype(np.int32)
+
+    def fill(misses):
+        if misses:
+            pool.fill([s for _, s in misses], [host[e] for e, _ in misses])
+    for c in range(S_ // top_k):
+        fill(streamer.remap(0, subset[top_k * c:top_k * (c + 1)].reshape(1, top_k))[1])
+    rng = np.random.default_rng(3)
+    route = ops.RouteBuffers(T * top_k, S_)
+    ws = ops.workspace(K, T, top_k, S_)
+    out = torch.empty(T, top_k, N, dtype=torch.float32, device="cuda")
+    b = torch.from_numpy(np.random.default_rng(2).normal(0, 1, size=(T, 1, K))
+                         .astype(np.float32)).cuda()
+    torch.cuda.synchronize()
+    t_setup = time.time() - t_setup
+    times, misses_n = [], 0
+    clocks = Clocks(torch.cuda.current_device())
+    # The op (grouping, activation quantization, mul_mat_id) 20 times in one
+    # CUDA graph over a device copy of the step's slot ids, so the timing is
+    # the device's, not the host's launch rate.
+    slots_d = torch.zeros(T, top_k, dtype=torch.int32, device="cuda")
+
+    def op():
+        r = ops.remap_group(slots_d, S_, route=route)
+        ops.mul_mat_id(pool, b, r, top_k, ws=ws, out=out)
+    op()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(20):
+            op()
+    for step in range(args.warmup + args.steps):
+        logits = rng.normal(0, 1, size=(T, E))
+        ids = np.argsort(-logits, axis=1, kind="stable")[:, :top_k].astype(np.int32)
+        slots, misses, _ = streamer.remap(0, ids)
+        fill(misses)
+        slots_d.copy_(torch.from_numpy(slots))
+        torch.cuda.synchronize()
+        if step == args.warmup:
+            clocks.start()
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        e.record()
+        torch.cuda.synchronize()
+        if step >= args.warmup:
+            times.append(a.elapsed_time(e) / 20)
+            misses_n += len(misses)
+    graph = None
+    clk = clocks.stop()
+    us = sum(times) / len(times) * 1e3
+    gbs = len(np.unique(slots)) * pool.expert_bytes / (us / 1e6) / 1e9
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    line = {"metric": "single mul_mat_id op: us per op", "impl": "msb", "value": us,
+            "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "iq4_nl x q8_0 -> f32", "data": "synthetic",
+            "config": {"workload": "single IQ4_NL mul_mat_id, 128 experts [768 x 2048], 32-slot "
+                                   "pool, top-8 through the slot streamer (misses filled before "
+                                   "the timed op)", "tokens": T,
+                       "misses_per_step": misses_n / args.steps,
+                       "timed": "grouping + activation quantization + mul_mat_id, 20 calls "
+                                "replayed from one CUDA graph per step"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                         "frac": gbs / hbm, "traffic": None,
+                         "kernel": "route + quantize + gemv (the referenced experts' bytes / "
+                                   "op time)",
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
+            "cpu_baseline": None, "e2e": None, "gpu_launches": 3 * 20 * args.steps,
+            "clocks": clk, "setup_s": round(t_setup, 1)}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "msb" and args.passes != "auto":
@@ -876,6 +992,13 @@ def main():
         from moestream_b200 import ops
         from moestream_b200._lib import OPT_IQ4NL_PATH
         ops.check(ops.lib().msb_set_option(OPT_IQ4NL_PATH, {"cuda": 1, "tc": 2}[args.iq4nl]))
+    if args.workload == "single-op":
+        if args.gpus != 1 or args.impl != "msb":
+            print(json.dumps({"workload": "single-op", "unavailable": "one GPU, --impl msb only"}))
+            return 0
+        if "--tokens" not in sys.argv:
+            args.tokens = 1
+        return single_op_main(args)
     if args.workload == "prefill":
         if args.gpus != 1 or args.impl != "msb":
             print(json.dumps({"workload": "prefill", "unavailable": "one GPU, --impl msb only"}))

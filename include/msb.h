@@ -450,7 +450,7 @@ int msb_ep_moe_ffn_peers(const msb_ep_peers_t *peers, msb_pool_t gate,
  * same either way. */
 #define MSB_OPT_WIDE_PASSES 3
 /* MSB_OPT_IQ4NL_PATH selects the arithmetic of IQ4_NL mul_mat_id: 0
- * (default) = tensor cores for batches with at least 8 pairs per slot they
+ * (default) = tensor cores for batches with at least 4 pairs per slot they
  * can reach (weights dequantized to fp16 d * kvalue in shared memory,
  * activations rounded to fp16, f32 accumulation; K a multiple of 64, rows a
  * multiple of 8, gate/up views on 128-row boundaries), the CUDA-core path

@@ -67,7 +67,7 @@ static int g_mxfp4_path = 0;
 // batches where the shapes allow, CUDA cores otherwise; 1 = CUDA cores
 // everywhere; 2 = tensor cores wherever the shapes allow.
 static int g_iq4nl_path = 0;
-constexpr int64_t kF16PairsPerSlot = 8;
+constexpr int64_t kF16PairsPerSlot = 4;
 
 static bool use_f16(int64_t pairs, int max_active) {
   if (g_iq4nl_path == 1) return false;

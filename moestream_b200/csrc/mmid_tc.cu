@@ -682,6 +682,11 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
       }
       const uint32_t a_i = acc++;
       const int buf = a_i % kBufs;
+      // The pass's pairs (lane j holds the j-th), loaded while the MMAs run.
+      const int g0 = item.pass * kPairs;
+      const int cc = min(kPairs, c_total - g0);
+      const int64_t pos = pos0 + g0;
+      const int64_t my_pair = lane < cc ? a.rows[pos + lane] : 0;
       if (!sm100::mbar_wait_bounded(&acc_full[buf], (a_i / kBufs) & 1, a.wait_ns)) {
         atomicOr(&g_status, kStatusAccFull);
         *abort_v = 1;
@@ -689,9 +694,6 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
       }
       sm100::tc_fence_after();
       {
-        const int g0 = item.pass * kPairs;
-        const int cc = min(kPairs, c_total - g0);
-        const int64_t pos = pos0 + g0;
         const uint32_t col = tmem + lane_addr + buf * C::kAccCols;
         const int n_groups = (cc + 7) / 8;   // 8-pair column groups this pass uses
         for (int gq = 0; gq < n_groups; ++gq) {
@@ -726,14 +728,12 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
                                sm100::smem_u32(&acc_empty[buf]))
                            : "memory");
           }
-          // The group's pairs: lane j holds the j-th (one load for all).
           const int gcc = min(8, cc - gq * 8);
-          const int64_t my_pair = lane < gcc ? a.rows[pos + gq * 8 + lane] : 0;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             if (j >= gcc) break;   // same on every lane
             const int jj = gq * 8 + j;
-            const int64_t pair = __shfl_sync(0xffffffffu, my_pair, j);
+            const int64_t pair = __shfl_sync(0xffffffffu, my_pair, jj);
             const float gv = (__uint_as_float(dg[4 * j]) + __uint_as_float(dg[4 * j + 1])) +
                              (__uint_as_float(dg[4 * j + 2]) + __uint_as_float(dg[4 * j + 3]));
             float u = 0.f;
@@ -790,7 +790,7 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
         }
         // The pass's rows of this 32-row block are stored: count them.
         if constexpr (NV == 1)
-          if (!split_mode) combine_arrive(a.comb, lane < cc ? a.rows[pos + lane] : 0, cc, blk, lane);
+          if (!split_mode) combine_arrive(a.comb, my_pair, cc, blk, lane);
       }
     }
   }

@@ -36,6 +36,12 @@ def tc_eligible(wtype, K):
     return WEIGHT_TYPES.get(wtype, wtype) == TYPE_MXFP4 and K % 64 == 0
 
 
+def f16_eligible(K, N):
+    """Whether an IQ4_NL projection with K inputs and N rows can run on the
+    tensor cores (fp16 dequantization)."""
+    return K % 64 == 0 and N % 8 == 0
+
+
 def device_status(clear=False):
     """Status bits of the tensor-core kernels on the current device (0 when
     every bounded wait completed). Synchronize the streams first."""

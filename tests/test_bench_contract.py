@@ -48,3 +48,8 @@ def test_reference_arm_times_every_layer_of_every_step():
 def test_prefill_workload_is_one_gpu_only():
     d = _run("--workload", "prefill", "--gpus", "2")
     assert d["workload"] == "prefill" and "unavailable" in d
+
+
+def test_single_op_workload_is_one_gpu_only():
+    d = _run("--workload", "single-op", "--gpus", "2")
+    assert d["workload"] == "single-op" and "unavailable" in d

@@ -124,7 +124,7 @@ def test_moe_ffn_on_tensor_cores(K, n_ff, n_expert, n_slot, n_tok, top_k, fused,
 
 
 def test_prompt_sized_batches_choose_the_tensor_cores():
-    """With the default policy a batch of >= 8 pairs per reachable slot runs
+    """With the default policy a batch of >= 4 pairs per reachable slot runs
     on the tensor cores (f16 form) and a decode batch on the CUDA cores
     (q8_0 form): the two forms are far enough apart to tell which ran."""
     from moestream_b200 import ops

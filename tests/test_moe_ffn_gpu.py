@@ -29,10 +29,27 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(params=["tc", "tc_wide", "q8"])
 def path(request):
+    """"tc" / "tc_wide": MXFP4 on the tensor cores (passes by batch size, or
+    always 24 pairs) and IQ4_NL on the tensor cores wherever the shapes
+    allow; "q8": both on the CUDA cores."""
     from moestream_b200 import ops
+    from moestream_b200._lib import OPT_IQ4NL_PATH
     ops.set_mxfp4_path(request.param)
+    ops.check(ops.lib().msb_set_option(OPT_IQ4NL_PATH, 1 if request.param == "q8" else 2))
     yield request.param
     ops.set_mxfp4_path("tc")
+    ops.check(ops.lib().msb_set_option(OPT_IQ4NL_PATH, 0))
+
+
+@pytest.fixture(params=["q8", "f16"])
+def iq4_form(request):
+    """IQ4_NL arithmetic for tests that do not take `path`: the CUDA-core
+    q8_0 form or the tensor-core f16 form."""
+    from moestream_b200 import ops
+    from moestream_b200._lib import OPT_IQ4NL_PATH
+    ops.check(ops.lib().msb_set_option(OPT_IQ4NL_PATH, 1 if request.param == "q8" else 2))
+    yield request.param
+    ops.check(ops.lib().msb_set_option(OPT_IQ4NL_PATH, 0))
 
 
 def build_layer(wtype, K, n_ff, n_expert, n_slot, fused, seed):
@@ -104,7 +121,10 @@ def test_moe_ffn_matches_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, 
     kw = dict(up_row0=n_ff if fused else 0)
     tc = (path.startswith("tc") and wtype == "mxfp4" and K % 64 == 0 and n_ff % 64 == 0 and
           (not fused or n_ff % 32 == 0))
-    mode = "e2m1x4" if tc else "q8"
+    f16 = (path.startswith("tc") and wtype == "iq4_nl" and K % 64 == 0 and n_ff % 64 == 0 and
+           (not fused or n_ff % 128 == 0))
+    mode = "e2m1x4" if tc else ("f16" if f16 else "q8")
+    tc = tc or f16
     y_f, h_f = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
                          mode=mode, **kw)
     y_ex, h_ex = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
@@ -139,10 +159,11 @@ def test_unweighted_top1_writes_expert_output(path):
 @pytest.mark.parametrize("wtype,K,n_ff,n_expert,n_slot,n_tok,top_k,fused", [
     ("mxfp4", 2880, 2880, 6, 4, 3, 4, False),    # tensor cores
     ("mxfp4", 512, 256, 8, 8, 40, 4, True),      # tensor cores, fused gate_up, several passes
-    ("iq4_nl", 2048, 512, 10, 8, 8, 8, False),   # CUDA cores
+    ("iq4_nl", 2048, 512, 10, 8, 8, 8, False),   # CUDA cores and tensor cores (iq4_form)
 ])
-def test_gpt_oss_activation_matches_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, fused):
-    """gpt-oss's clamped SwiGLU (alpha 1.702, limit 7) in both paths. The
+def test_gpt_oss_activation_matches_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, fused,
+                                           iq4_form):
+    """gpt-oss's clamped SwiGLU (alpha 1.702, limit 7) in every path. The
     activations are scaled by 8 so that many gate and up values pass the
     clamp; tolerances as for plain SwiGLU."""
     from moestream_b200 import ops
@@ -161,13 +182,13 @@ def test_gpt_oss_activation_matches_oracle(wtype, K, n_ff, n_expert, n_slot, n_t
                     torch.from_numpy(w).cuda(), top_k, up_row0=n_ff if fused else 0, act=act,
                     activation=("swiglu_oai", 1.702, 7.0))
     torch.cuda.synchronize()
-    tc = wtype == "mxfp4"
+    form = "e2m1x4" if wtype == "mxfp4" else iq4_form
+    tc = form != "q8"
     up = slabs["gate"] if fused else slabs["up"]
     y_f, h_f = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
-                         mode="e2m1x4" if tc else "q8", up_row0=n_ff if fused else 0,
-                         act=(1.702, 7.0))
+                         mode=form, up_row0=n_ff if fused else 0, act=(1.702, 7.0))
     _, h_silu = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
-                          mode="e2m1x4" if tc else "q8", up_row0=n_ff if fused else 0)
+                          mode=form, up_row0=n_ff if fused else 0)
     assert np.abs(h_f).max() > 0 and not np.allclose(h_f, h_silu)  # not plain SwiGLU
     assert O.max_abs_normalized(act.cpu().numpy(), h_f) < (1e-4 if tc else 1e-5)
     assert O.max_abs_normalized(y.cpu().numpy(), y_f) < (1e-3 if tc else 2e-3)
@@ -223,9 +244,10 @@ def test_up_view_off_the_tile_grid(n_ff, pad):
     ("mxfp4", 2880, 2880, 6, 4, 2, 4, True),     # 8 pairs: split over K, the reduce adds them
     ("mxfp4", 2880, 2880, 6, 4, 5, 4, True),     # fused gate_up, up view off the tile grid
     ("mxfp4", 512, 256, 8, 6, 40, 4, False),     # several passes per slot
-    ("iq4_nl", 2048, 512, 10, 8, 8, 8, False),   # CUDA cores
+    ("iq4_nl", 2048, 512, 10, 8, 8, 8, False),   # CUDA cores and tensor cores (iq4_form)
 ])
-def test_expert_biases_match_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, fused):
+def test_expert_biases_match_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, fused,
+                                    iq4_form):
     """gpt-oss expert biases, looked up by the router's expert ids (not the
     slots), added to every pair not routed to the zero slot; non-resident
     experts go to the zero slot and contribute exactly 0."""
@@ -251,15 +273,15 @@ def test_expert_biases_match_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top
                     torch.from_numpy(w).cuda(), top_k, up_row0=n_ff if fused else 0, act=act,
                     bias=(gb_t, ub_t, db_t, ids_t), activation=("swiglu_oai", 1.702, 7.0))
     torch.cuda.synchronize()
-    tc = wtype == "mxfp4"
+    form = "e2m1x4" if wtype == "mxfp4" else iq4_form
+    tc = form != "q8"
     up = slabs["gate"] if fused else slabs["up"]
     ub_o = gb[:, n_ff:] if fused else ub
     y_f, h_f = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
-                         mode="e2m1x4" if tc else "q8", up_row0=n_ff if fused else 0,
+                         mode=form, up_row0=n_ff if fused else 0,
                          act=(1.702, 7.0), bias=(gb[:, :n_ff], ub_o, db, ids_e, n_expert))
     y_0, _ = O.moe_ffn(wtype, slabs["gate"], up, slabs["down"], K, n_ff, x, slots, w,
-                       mode="e2m1x4" if tc else "q8", up_row0=n_ff if fused else 0,
-                       act=(1.702, 7.0))
+                       mode=form, up_row0=n_ff if fused else 0, act=(1.702, 7.0))
     assert O.max_abs_normalized(y_f, y_0) > 1e-2   # the biases matter
     a = act.cpu().numpy()
     assert np.all(a[slots == n_slot] == 0.0)

@@ -4,7 +4,9 @@ Two arithmetic paths: MXFP4 with K a multiple of 64 runs on the tensor
 cores (activations as four e2m1 terms per block), everything else on the
 CUDA cores (int8 activations, ggml's q8_0 form); MXFP4 cases run both, the
 tensor cores with passes chosen by batch size ("tc") and with 24-pair
-passes forced ("tc_wide").
+passes forced ("tc_wide"). With "tc", IQ4_NL with K a multiple of 64 and
+N of 8 runs on the tensor cores too (weights dequantized to fp16: the
+oracle's f16 form, within 1e-4).
 Tolerances (max |got - want| / max |want|):
   - vs the oracle in the path's own form: 1e-5 (q8; f32 block sums in
     another order) or 1e-4 (e2m1x4; f32 tensor-core accumulation);
@@ -29,15 +31,25 @@ TOL_EXACT = 1e-2
 
 @pytest.fixture(params=["tc", "tc_wide", "q8"])
 def path(request):
+    """"tc" / "tc_wide": MXFP4 on the tensor cores (passes by batch size, or
+    always 24 pairs) and IQ4_NL on the tensor cores wherever the shapes
+    allow; "q8": both on the CUDA cores."""
     from moestream_b200 import ops
+    from moestream_b200._lib import OPT_IQ4NL_PATH
     ops.set_mxfp4_path(request.param)
+    ops.check(ops.lib().msb_set_option(OPT_IQ4NL_PATH, 1 if request.param == "q8" else 2))
     yield request.param
     ops.set_mxfp4_path("tc")
+    ops.check(ops.lib().msb_set_option(OPT_IQ4NL_PATH, 0))
 
 
-def oracle_mode(wtype, K, path):
+def oracle_mode(wtype, K, path, N=None):
     from moestream_b200 import ops
-    return "e2m1x4" if path.startswith("tc") and ops.tc_eligible(wtype, K) else "q8"
+    if not path.startswith("tc"):
+        return "q8"
+    if wtype == "iq4_nl":
+        return "f16" if ops.f16_eligible(K, N) else "q8"
+    return "e2m1x4" if ops.tc_eligible(wtype, K) else "q8"
 
 
 def make_pool(wtype, K, N, n_slot, slab_bytes, slots):
@@ -95,10 +107,10 @@ def test_mul_mat_id_matches_oracle(wtype, K, N, n_expert, n_slot, n_tok, top_k, 
         b = torch.from_numpy(b).to(torch.bfloat16).float().numpy()  # oracle sees bf16 values
     got = gpu_mmid(pool, b, ids, dtype)
     slab = slab_for(ex, slot_of, n_slot)
-    mode = oracle_mode(wtype, K, path)
+    mode = oracle_mode(wtype, K, path, N)
     want_form = O.mul_mat_id(wtype, slab, K, N, b, ids, mode=mode)
     want = O.mul_mat_id(wtype, slab, K, N, b, ids, mode="exact")
-    assert O.max_abs_normalized(got, want_form) < (TOL_TC if mode == "e2m1x4" else TOL_Q8)
+    assert O.max_abs_normalized(got, want_form) < (TOL_Q8 if mode == "q8" else TOL_TC)
     assert O.max_abs_normalized(got, want) < TOL_EXACT
     # Rows routed to the zero slot are exactly zero.
     z = ids == n_slot
