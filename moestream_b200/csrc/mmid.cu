@@ -57,7 +57,8 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
                   uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st,
                   const RowTarget *res_rows = nullptr, const FfnAct *fa = nullptr,
                   uint8_t *split_ws = nullptr, int64_t split_bytes = 0,
-                  const FfnBias *bias = nullptr, const Combine *comb = nullptr);
+                  const FfnBias *bias = nullptr, const Combine *comb = nullptr,
+                  bool allow_wide = true);
 
 // MXFP4 arithmetic: 0 = tensor cores where the shapes allow, 1 = CUDA cores
 // with int8 activations (ggml's q8_0 form) everywhere.
@@ -687,8 +688,11 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
     const msb_pool_s *gu_pools[2] = {gate, up};
     const bool timed = g_gate_up_start && g_gate_up_stop;
     if (timed) MSB_CUDA_TRY(record_timing_event(g_gate_up_start, st));
+    // Expert-parallel rows (`rows`) are mostly padding: the pairs per
+    // expert stay few, so the passes stay narrow.
     if (int rc = tc_projection(gu_pools, 2, rows_gu, n_ff, route, pairs, xa, nullptr, ha, act_dev,
-                               max_active, st, nullptr, &fa, split_ws, split_bytes, &bias_gu))
+                               max_active, st, nullptr, &fa, split_ws, split_bytes, &bias_gu,
+                               nullptr, rows == nullptr))
       return rc;
     if (timed) {
       MSB_CUDA_TRY(record_timing_event(g_gate_up_stop, st));
@@ -697,7 +701,8 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
     const int64_t rows_dn[2] = {0, 0};
     const msb_pool_s *dn_pools[2] = {down, down};
     return tc_projection(dn_pools, 1, rows_dn, down->N, route, pairs, ha, rd, nullptr, nullptr,
-                         max_active, st, rows, nullptr, split_ws, split_bytes, &bias_dn, &comb);
+                         max_active, st, rows, nullptr, split_ws, split_bytes, &bias_dn, &comb,
+                         rows == nullptr);
   }
   const bool f16 = !rows && f16_supported(gate) && f16_supported(up) && f16_supported(down) &&
                    up_row0 % 128 == 0 && use_f16(pairs, max_active);

@@ -916,7 +916,8 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
                   const msb_route_t *route, int64_t n_pairs, const uint8_t *act_in, float *res,
                   uint8_t *act_out, float *act_f32, int max_active, cudaStream_t st,
                   const RowTarget *res_rows, const FfnAct *fa, uint8_t *split_ws,
-                  int64_t split_bytes, const FfnBias *bias, const Combine *comb) {
+                  int64_t split_bytes, const FfnBias *bias, const Combine *comb,
+                  bool allow_wide) {
   const msb_pool_s *pool = pools[0];
   tc::Args a{};
   if (bias) a.bias = *bias;
@@ -973,9 +974,10 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   }
   // Wide passes (24 pairs) for prompt-sized batches: when the pairs would
   // fill at least kWidePairsPerSlot passes-worth per possibly active slot.
-  // Not for row targets (the expert-parallel exchange), whose rows are
+  // Not for the expert-parallel exchange (allow_wide false), whose rows are
   // padded and few per expert.
-  const bool wide = a.split_max == 0 && !res_rows && wide_passes_enabled(n_pairs, max_active);
+  const bool wide = a.split_max == 0 && allow_wide && !res_rows &&
+                    wide_passes_enabled(n_pairs, max_active);
   {
     // A pair's four 16-byte term records of one block are 64 contiguous
     // bytes (8 elements of 8 bytes); a box line is the pairs of one pass

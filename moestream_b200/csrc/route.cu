@@ -26,7 +26,13 @@ struct RouteArgs {
   int32_t n_expert, n_slot;
   int32_t *slot_ids, *counts, *offsets, *rows, *active;
   FlagWait wait;   // ids arriving from other GPUs (expert parallelism)
+  int stash;       // pairs' slots also kept in shared memory (n_pairs <= kStashPairs)
 };
+
+// Pairs whose slots the scatter reads from shared memory instead of global
+// memory (the scatter is one warp's dependent chain: a shared-memory read
+// per step instead of a round trip to L2).
+static constexpr int kStashPairs = 12288;
 
 static constexpr int kRouteThreads = 1024;
 
@@ -78,6 +84,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   int *cursor = sm + S;      // [S]
   int *flag = sm + 2 * S;    // [S]
   int *warp_sums = sm + 3 * S;  // [33]
+  int *stash = sm + 3 * S + 33;  // [n_pairs] when a.stash
   const int tid = threadIdx.x;
   const int n_pairs = a.top_k * a.n_tok;
 
@@ -97,6 +104,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
       slot = e;  // ids already hold slot ids
     }
     a.slot_ids[i] = slot;
+    if (a.stash) stash[i] = slot;
     atomicAdd(&cnt[slot], 1);
   }
   __syncthreads();
@@ -125,7 +133,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
     for (int base = 0; base < n_pairs; base += 32) {
       const int i = base + lane;
       const bool valid = i < n_pairs;
-      const int s = valid ? a.slot_ids[i] : -1 - lane;
+      const int s = valid ? (a.stash ? stash[i] : a.slot_ids[i]) : -1 - lane;
       const unsigned same = __match_any_sync(0xffffffffu, s);
       const int leader = __ffs(same) - 1;
       int start = 0;
@@ -161,11 +169,14 @@ int msb::remap_group_wait(const int32_t *ids_dev, int64_t nb0, int64_t nb1, int3
   MSB_CHECK_ARG(nb0 % 4 == 0 && nb1 % 4 == 0, "msb_remap_group: id strides must be multiples of 4 bytes");
   MSB_CHECK_ARG(int64_t(top_k) * n_tok < (int64_t(1) << 30), "msb_remap_group: too many pairs");
   const int S = n_slot + 1;
-  const size_t smem = (size_t(3) * S + 33) * sizeof(int);
+  const int64_t n_pairs = int64_t(top_k) * n_tok;
+  size_t smem = (size_t(3) * S + 33) * sizeof(int);
   MSB_CHECK_ARG(smem <= 200 * 1024, "msb_remap_group: n_slot %d too large", n_slot);
+  const bool stash = n_pairs <= msb::kStashPairs && smem + size_t(n_pairs) * 4 <= 200 * 1024;
+  if (stash) smem += size_t(n_pairs) * sizeof(int);
   msb::RouteArgs a{reinterpret_cast<const char *>(ids_dev), nb0, nb1, top_k, n_tok,
                    table_dev, n_expert, n_slot, route->slot_ids, route->counts,
-                   route->offsets, route->rows, route->active, wait};
+                   route->offsets, route->rows, route->active, wait, stash ? 1 : 0};
   if (smem > 48 * 1024)
     MSB_CUDA_TRY(cudaFuncSetAttribute(msb::route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   MSB_CUDA_TRY(msb::launch_pdl(msb::route_kernel, dim3(1), dim3(msb::kRouteThreads), smem,
