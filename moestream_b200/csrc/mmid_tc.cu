@@ -35,7 +35,8 @@
 //                    the stages in turn, each into its own accumulator;
 //                    tcgen05.commit frees the stage / hands over a buffer;
 //   warps 4-7      : epilogue -- warp w reads TMEM lanes 32*(w%4)..+31
-//                    (rows), releases the buffer, then stores.
+//                    (rows), releases the buffer, then stores (wide passes:
+//                    warps 4-15, three sets of four, one 8-pair group each).
 // With two views (gate and up) the epilogue applies SwiGLU and writes the
 // down projection's activation terms directly.
 // Batches of up to 8 pairs leave most CTAs without an item, so there a work
@@ -63,7 +64,6 @@ namespace tc {
 
 constexpr int kTerms = 4;        // e2m1 terms per activation block
 constexpr int kChunk = 4;        // 32-element blocks per stage (two K=64 MMAs)
-constexpr int kThreads = 256;    // producer warp, 2-3 MMA warps, 4 epilogue warps
 constexpr int kMaxActive = 1024; // slots (with the zero slot) one launch can walk
 
 // Shapes of one launch with NV weight views (2: gate and up); a work item
@@ -75,6 +75,9 @@ constexpr int kMaxActive = 1024; // slots (with the zero slot) one launch can wa
 //     columns (two accumulator buffers of 2 x 96 columns plus each stage's
 //     scale factors) -- prompt-sized batches, where a tile's weights are
 //     streamed once per pass and 3x fewer passes mean 3x fewer re-reads.
+//     Three sets of 4 epilogue warps take the pass's three 8-pair groups
+//     (one each): a pass's epilogue costs about as much per group as the
+//     MMAs of the whole pass, so one set would leave the MMAs waiting.
 // (Feeding four narrow passes' accumulators from one staged tile -- one CTA
 // per SM, single-buffered tensor memory -- ran a 2048-token layer 1.4x
 // slower: the four passes' epilogue serialized with the MMAs.)
@@ -83,6 +86,11 @@ struct Cfg {
   static constexpr int kPairs = W ? 24 : 8;              // (token, k) pairs per pass
   static constexpr int kN = kTerms * kPairs;             // MMA N: the pass's terms stacked
   static constexpr int kCtasPerSm = W ? 1 : 2;
+  // Epilogue warp sets (4 warps each, one per TMEM lane quadrant); set s
+  // takes the pass's 8-pair groups s, s + kEpiSets, ...
+  static constexpr int kEpiSets = W ? 3 : 1;
+  // Warp 0 producer, warps 1-3 MMA issue, then the epilogue sets.
+  static constexpr int kThreads = 128 + 128 * kEpiSets;
   // MMA-issuing warps: one per view (gate and up), or two / three taking
   // turns over the stages of a single view. One accumulator buffer holds one
   // N = kN accumulator per MMA warp.
@@ -109,7 +117,7 @@ struct Cfg {
   // 8-pair group over its 32 rows ([pair][row] f32) to re-split it with 4
   // lanes per 32-row block.
   static constexpr int kStageHOff = kItemOff + (kMaxActive + 1) * 4;
-  static constexpr int kStageH = NV == 2 ? 4 * 8 * 32 * 4 : 0;
+  static constexpr int kStageH = NV == 2 ? 4 * kEpiSets * 8 * 32 * 4 : 0;
   static constexpr int kSmem = kStageHOff + kStageH;
   static constexpr int kAccCols = kMma * kN;
   // TMEM columns per stage: each MMA warp's scale factors (A then B).
@@ -383,7 +391,8 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant
 }
 
 template <int NV, bool W>
-__global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
+    tc_kernel(const __grid_constant__ Args a) {
   using C = Cfg<NV, W>;
   constexpr int kPairs = C::kPairs;
   constexpr int kN = C::kN;
@@ -407,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
     }
     for (int b = 0; b < 2; ++b) {
       sm100::mbar_init(&acc_full[b], C::kMma);
-      sm100::mbar_init(&acc_empty[b], 4);
+      sm100::mbar_init(&acc_empty[b], 4 * C::kEpiSets);   // every epilogue warp
     }
     sm100::mbar_init(drained, C::kMma);
     *abort_flag = 0;
@@ -433,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
   // pair's zeros).
   int *item0 = reinterpret_cast<int *>(smem + C::kItemOff);
   const int n_active = a.active[0];
-  for (int i = threadIdx.x; i < n_active; i += kThreads) {
+  for (int i = threadIdx.x; i < n_active; i += C::kThreads) {
     const int slot = a.active[1 + i];
     const int passes = slot == a.zero_slot ? 1 : (a.counts[slot] + kPairs - 1) / kPairs;
     item0[i + 1] = passes * a.tiles;
@@ -633,9 +642,10 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
       }
     }
   } else {
-    // ---- epilogue (warps 4-7) ----
+    // ---- epilogue (warps 4 .. 4 + 4 * kEpiSets - 1) ----
     const int quad = warp & 3;            // TMEM lane quadrant of this warp
-    float *sh = reinterpret_cast<float *>(smem + C::kStageHOff) + quad * 8 * 32;
+    const int set = (warp - 4) >> 2;      // epilogue warp set
+    float *sh = reinterpret_cast<float *>(smem + C::kStageHOff) + (warp - 4) * 8 * 32;
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     uint32_t acc = 0;
     int cur = 0;
@@ -650,6 +660,7 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
       const int c_total = a.counts[slot];
       const int64_t pos0 = a.offsets[slot];
       if (slot == a.zero_slot && split_mode) continue;   // the split reduce writes them
+      if (slot == a.zero_slot && set != 0) continue;     // set 0 writes them
       if (slot == a.zero_slot) {
         // Every weight of the zero slot is 0, so the exact result is 0; for
         // the down projection's input, 0 splits into four zero terms with
@@ -696,7 +707,17 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
       {
         const uint32_t col = tmem + lane_addr + buf * C::kAccCols;
         const int n_groups = (cc + 7) / 8;   // 8-pair column groups this pass uses
-        for (int gq = 0; gq < n_groups; ++gq) {
+        auto release = [&]() {
+          // This warp's accumulators are in registers: count it out of the buffer.
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0)
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                             sm100::smem_u32(&acc_empty[buf]))
+                         : "memory");
+        };
+        if (set >= n_groups) release();   // no group of this pass for this set
+        for (int gq = set; gq < n_groups; gq += C::kEpiSets) {
           // Group gq: columns 32 gq .. +31 of each accumulator (column
           // 4j + t of the group holds term t of the group's pair j).
           uint32_t dg[32], du[32];
@@ -719,15 +740,7 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
                 dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
             }
           }
-          if (gq == n_groups - 1) {
-            // Every accumulator of the item is in registers: release the buffer.
-            sm100::tc_fence_before();
-            __syncwarp();
-            if (lane == 0)
-              asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
-                               sm100::smem_u32(&acc_empty[buf]))
-                           : "memory");
-          }
+          if (gq + C::kEpiSets >= n_groups) release();   // this set's last group
           const int gcc = min(8, cc - gq * 8);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -787,10 +800,12 @@ __global__ void __launch_bounds__(kThreads, W ? 1 : 2) tc_kernel(const __grid_co
               __syncwarp();
             }
           }
+          // The group's rows of this 32-row block are stored: count them.
+          if constexpr (NV == 1)
+            if (!split_mode)
+              combine_arrive(a.comb, __shfl_sync(0xffffffffu, my_pair, (gq * 8 + lane) & 31), gcc,
+                             blk, lane);
         }
-        // The pass's rows of this 32-row block are stored: count them.
-        if constexpr (NV == 1)
-          if (!split_mode) combine_arrive(a.comb, my_pair, cc, blk, lane);
       }
     }
   }
@@ -894,7 +909,7 @@ static int launch_tc_t(const tc::Args &a, int max_active, int64_t n_pairs, cudaS
   int64_t grid = passes * a.tiles * (a.split_max > 0 ? a.split_max : 1);
   if (grid > int64_t(C::kCtasPerSm) * n_sm) grid = int64_t(C::kCtasPerSm) * n_sm;
   if (grid == 0) return MSB_OK;
-  MSB_CUDA_TRY(launch_pdl(tc::tc_kernel<NV, W>, dim3(unsigned(grid)), dim3(tc::kThreads), C::kSmem,
+  MSB_CUDA_TRY(launch_pdl(tc::tc_kernel<NV, W>, dim3(unsigned(grid)), dim3(C::kThreads), C::kSmem,
                           st, a));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
