@@ -188,7 +188,7 @@ __device__ __forceinline__ RawBlock load_block(const PoolView &v, int slot, int6
     const int64_t off = b * v.N + v.row0 + n;
     r.q = __ldg(reinterpret_cast<const uint4 *>(sb + off * 16));
     const uint8_t *sc = sb + v.nb * v.N * 16;
-    if constexpr (WT == MSB_TYPE_MXFP4) r.s = __ldg(sc + scale_offset(true, b, v.row0 + n, v.N));
+    if constexpr (WT == MSB_TYPE_MXFP4) r.s = __ldg(sc + scale_offset(true, b, v.row0 + n, v.N, v.nb));
     else r.s = __ldg(reinterpret_cast<const unsigned short *>(sc) + off);
   }
   return r;

@@ -63,7 +63,6 @@ namespace msb {
 namespace tc {
 
 constexpr int kTerms = 4;        // e2m1 terms per activation block
-constexpr int kChunk = 4;        // 32-element blocks per stage (two K=64 MMAs)
 constexpr int kMaxActive = 1024; // slots (with the zero slot) one launch can walk
 
 // Shapes of one launch with NV weight views (2: gate and up); a work item
@@ -95,21 +94,29 @@ struct Cfg {
   // turns over the stages of a single view. One accumulator buffer holds one
   // N = kN accumulator per MMA warp.
   static constexpr int kMma = NV == 2 ? 2 : (W ? 2 : 3);
-  static constexpr int kStages = W ? (NV == 2 ? 7 : 12) : (NV == 2 ? 5 : 8);
-  static constexpr int kA = NV * kChunk * 2048;          // 128 rows x 16 B per block
-  // Scale factors of a weight view: one 512-byte chunk per 128-row tile of
-  // the pool. A view whose first row is not on a tile boundary (the up half
-  // of a fused gate_up tensor, rows from N/2) spans two chunks per window;
-  // with two views there is room for both.
-  static constexpr int kSfaView = NV == 2 ? 1024 : 512;
-  static constexpr int kSFA = NV * kSfaView;
-  static constexpr int kB = kChunk * kN * 16;            // [block][pair][term] 16 B rows
-  // The activation terms' scale records of the pass, [pair][term] 16 B rows
-  // (the 4 block scales in the first word). With 8 pairs they are the MMA's
-  // 32-row scale atom as they stand; with 24 each MMA warp gathers rows
-  // 32j + l into word j of atom row l (kSfbAtom).
-  static constexpr int kSfbRec = kN * 16;
-  static constexpr int kSfbAtom = W ? 512 * kMma : 0;
+  // K blocks per stage: 4 (two K=64 MMAs per view), or 8 with wide passes.
+  // A stage costs its copy instructions more than its bytes (each tiled or
+  // bulk copy occupies the SM's copy engine for a few hundred cycles), so
+  // the prompt-sized passes move twice the bytes per instruction.
+  static constexpr int kCh = W ? 8 : 4;
+  static constexpr int kSfc = kCh / 4;                   // 4-block scale chunks per stage
+  static constexpr int kStages = W ? (NV == 2 ? 4 : 6) : (NV == 2 ? 5 : 8);
+  static constexpr int kA = NV * kCh * 2048;             // 128 rows x 16 B per block
+  // Scale factors of a weight view: one 512-byte record per 128-row tile and
+  // chunk, a tile's chunks contiguous in the pool. View 0 starts on the tile
+  // grid; view 1 of a two-view launch (the up half of a fused gate_up
+  // tensor, rows from N/2) may not, so its window also takes the next
+  // tile's records.
+  static constexpr int kSfa0 = kSfc * 512;
+  static constexpr int kSfa1 = NV == 2 ? 2 * kSfc * 512 : 0;
+  static constexpr int kSFA = kSfa0 + kSfa1;
+  static constexpr int kB = kCh * kN * 16;               // [block][pair][term] 16 B rows
+  // The activation terms' scale records of the pass, [chunk][pair][term] 16 B
+  // rows (a chunk's 4 block scales in the first word). With 8 pairs they are
+  // the MMA's 32-row scale atom as they stand; with 24 each MMA warp gathers
+  // rows 32j + l into word j of atom row l (kSfbAtom, per chunk).
+  static constexpr int kSfbRec = kSfc * kN * 16;
+  static constexpr int kSfbAtom = W ? 512 * kMma * kSfc : 0;
   static constexpr int kStage = kA + kSFA + kB + kSfbRec + kSfbAtom;
   static constexpr int kBarOff = kStages * kStage;
   static constexpr int kItemOff = kBarOff + 256;           // item prefix, kMaxActive + 1 ints
@@ -120,8 +127,9 @@ struct Cfg {
   static constexpr int kStageH = NV == 2 ? 4 * kEpiSets * 8 * 32 * 4 : 0;
   static constexpr int kSmem = kStageHOff + kStageH;
   static constexpr int kAccCols = kMma * kN;
-  // TMEM columns per stage: each MMA warp's scale factors (A then B).
-  static constexpr int kSfCols = NV == 2 ? 16 : 8;
+  // TMEM columns per stage: each MMA warp's scale factors (A then B), 8
+  // per chunk.
+  static constexpr int kSfCols = (NV == 2 ? 16 : 8) * kSfc;
   static constexpr int kTmemCols = W ? 512 : 256;
   static constexpr int kAccBufs = 2 * kAccCols + kStages * kSfCols <= kTmemCols ? 2 : 1;
   static constexpr int kSfBase = kAccBufs * kAccCols;    // after the buffers
@@ -400,7 +408,7 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
   constexpr int kBufs = C::kAccBufs;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n_chunks = (a.nb + kChunk - 1) / kChunk;
+  const int64_t n_chunks = (a.nb + C::kCh - 1) / C::kCh;   // stages per item
 
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
   uint64_t *empty = full + kStages;
@@ -501,31 +509,34 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
           }
           uint8_t *st = smem + s * C::kStage;
           uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
-          const int64_t b0 = i * kChunk;
+          const int64_t b0 = i * C::kCh;     // first block of the stage
+          const int64_t c0 = i * C::kSfc;    // its first scale chunk
+          const int64_t nc = (a.nb + 3) / 4;
+          const uint32_t sf_bytes = uint32_t(nc - c0 < C::kSfc ? nc - c0 : C::kSfc) * 512;
           // Full boxes are counted (rows or blocks outside the tensors
-          // arrive as zeros); a window off the tile grid also takes the next
-          // tile's scale chunk when the pool has one.
+          // arrive as zeros); the scale records are copied as far as they
+          // exist. A window off the tile grid (view 1 only) also takes the
+          // next tile's records when the pool has one.
           bool next_sf[NV];
           uint32_t tx = uint32_t(C::kA + C::kB + C::kSfbRec);
           for (int v = 0; v < NV; ++v) {
             const int64_t r0 = a.row0[v] + item.n0;
-            next_sf[v] = NV == 2 && (r0 & 127) != 0 && (r0 >> 7) + 1 < (a.N[v] + 127) / 128;
-            tx += next_sf[v] ? 1024u : 512u;
+            next_sf[v] = v == 1 && (r0 & 127) != 0 && (r0 >> 7) + 1 < (a.N[v] + 127) / 128;
+            tx += next_sf[v] ? 2 * sf_bytes : sf_bytes;
           }
           sm100::mbar_expect_tx(&full[s], tx);
           for (int v = 0; v < NV; ++v) {
             const int64_t r0 = a.row0[v] + item.n0;
-            sm100::tma_3d(sA + v * kChunk * 2048, &a.tm_w[v], int(r0) * 2, int(b0), slot,
+            sm100::tma_3d(sA + v * C::kCh * 2048, &a.tm_w[v], int(r0) * 2, int(b0), slot,
                           &full[s]);
             const uint8_t *slot_base = a.pool[v] + int64_t(slot) * a.slot_stride[v];
-            const uint8_t *sf_base = slot_base + a.nb * a.N[v] * 16;
-            const int64_t sf_tiles = (a.N[v] + 127) / 128;
-            const uint8_t *chunk = sf_base + (i * sf_tiles + (r0 >> 7)) * 512;
-            sm100::bulk_g2s(sSFA + v * C::kSfaView, chunk, 512, &full[s]);
-            if (next_sf[v]) sm100::bulk_g2s(sSFA + v * C::kSfaView + 512, chunk + 512, 512, &full[s]);
+            const uint8_t *sf_tile = slot_base + a.nb * a.N[v] * 16 + ((r0 >> 7) * nc + c0) * 512;
+            uint8_t *sfa_v = sSFA + (v == 0 ? 0 : C::kSfa0);
+            sm100::bulk_g2s(sfa_v, sf_tile, sf_bytes, &full[s]);
+            if (next_sf[v]) sm100::bulk_g2s(sfa_v + C::kSfc * 512, sf_tile + nc * 512, sf_bytes, &full[s]);
           }
           sm100::tma_3d(sB, &a.tm_aq, pos * 8, int(b0), 0, &full[s]);
-          sm100::tma_3d(sSFB, &a.tm_asf, pos * 8, int(i), 0, &full[s]);
+          sm100::tma_3d(sSFB, &a.tm_asf, pos * 8, int(c0), 0, &full[s]);
         }
       }
       // No copy may still be landing in shared memory when the CTA exits
@@ -583,48 +594,64 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
           }
           uint8_t *st = smem + s * C::kStage;
           uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
-          uint8_t *sfa_v = sSFA + v * C::kSfaView;
-          if (shift) {
-            // Reassemble the window's chunk in place: lane l owns 16-byte
-            // row l of both staged chunks (words = 32-row groups).
-            const uint4 c0 = *reinterpret_cast<const uint4 *>(sfa_v + lane * 16);
-            uint4 c1 = make_uint4(0u, 0u, 0u, 0u);   // rows past the pool: scale 2^-127
-            if (has_next) c1 = *reinterpret_cast<const uint4 *>(sfa_v + 512 + lane * 16);
-            const uint4 o = shift == 1   ? make_uint4(c0.y, c0.z, c0.w, c1.x)
-                            : shift == 2 ? make_uint4(c0.z, c0.w, c1.x, c1.y)
-                                         : make_uint4(c0.w, c1.x, c1.y, c1.z);
-            *reinterpret_cast<uint4 *>(sfa_v + lane * 16) = o;
-            sm100::fence_proxy_async_smem();
-          }
-          const uint8_t *sfb = sSFB;
-          if constexpr (W) {
-            // Scale atom of the pass's 96 B rows: word j of row l is the
-            // record of B row 32j + l (rows 96-127 do not exist: scale 0).
-            uint8_t *atom = sSFB + C::kSfbRec + m * 512;
-            const uint4 o = make_uint4(*reinterpret_cast<const uint32_t *>(sSFB + lane * 16),
-                                       *reinterpret_cast<const uint32_t *>(sSFB + (32 + lane) * 16),
-                                       *reinterpret_cast<const uint32_t *>(sSFB + (64 + lane) * 16),
-                                       0u);
-            *reinterpret_cast<uint4 *>(atom + lane * 16) = o;
-            sm100::fence_proxy_async_smem();
-            sfb = atom;
+          uint8_t *sfa_v = sSFA + (v == 0 ? 0 : C::kSfa0);
+          const int kbn = int(a.nb - i * C::kCh < C::kCh ? a.nb - i * C::kCh : C::kCh);
+          const int ncs = (kbn + 3) / 4;   // scale chunks with MMAs in this stage
+          for (int c = 0; c < ncs; ++c) {
+            if (shift) {
+              // Reassemble the window's record of chunk c in place: lane l
+              // owns 16-byte row l of this tile's and the next tile's
+              // records (words = 32-row groups).
+              uint8_t *rec = sfa_v + c * 512;
+              const uint4 q0 = *reinterpret_cast<const uint4 *>(rec + lane * 16);
+              uint4 q1 = make_uint4(0u, 0u, 0u, 0u);   // rows past the pool: scale 2^-127
+              if (has_next)
+                q1 = *reinterpret_cast<const uint4 *>(rec + C::kSfc * 512 + lane * 16);
+              const uint4 o = shift == 1   ? make_uint4(q0.y, q0.z, q0.w, q1.x)
+                              : shift == 2 ? make_uint4(q0.z, q0.w, q1.x, q1.y)
+                                           : make_uint4(q0.w, q1.x, q1.y, q1.z);
+              *reinterpret_cast<uint4 *>(rec + lane * 16) = o;
+              sm100::fence_proxy_async_smem();
+            }
+            if constexpr (W) {
+              // Scale atom of chunk c of the pass's 96 B rows: word j of row
+              // l is the record of B row 32j + l (rows 96-127 do not exist:
+              // scale 0).
+              const uint8_t *recs = sSFB + c * (kN * 16);
+              uint8_t *atom = sSFB + C::kSfbRec + (m * C::kSfc + c) * 512;
+              const uint4 o = make_uint4(*reinterpret_cast<const uint32_t *>(recs + lane * 16),
+                                         *reinterpret_cast<const uint32_t *>(recs + (32 + lane) * 16),
+                                         *reinterpret_cast<const uint32_t *>(recs + (64 + lane) * 16),
+                                         0u);
+              *reinterpret_cast<uint4 *>(atom + lane * 16) = o;
+              sm100::fence_proxy_async_smem();
+            }
           }
           __syncwarp();
           if (lane == 0) {
-            const uint32_t sf_col = tmem + C::kSfBase + s * C::kSfCols + (NV == 2 ? m * 8 : 0);
-            sm100::tmem_cp_32x128b_x4(sf_col, sm100::smem_desc(sm100::smem_u32(sfa_v), 0, 128));
-            sm100::tmem_cp_32x128b_x4(sf_col + 4, sm100::smem_desc(sm100::smem_u32(sfb), 0, 128));
-            const int kbn = int(a.nb - i * kChunk < kChunk ? a.nb - i * kChunk : kChunk);
-            for (int j = 0; j < kbn / 2; ++j) {
-              const uint32_t sel = uint32_t(2 * j);
-              // B: 32 stacked rows of 16 B per block; K-halves one block apart.
-              const uint64_t bdesc =
-                  sm100::smem_desc(sm100::smem_u32(sB + 2 * j * (kN * 16)), kN * 16, 128);
-              const uint64_t adesc =
-                  sm100::smem_desc(sm100::smem_u32(sA + (v * kChunk + 2 * j) * 2048), 2048, 128);
-              sm100::mma_mxf4(d0, adesc, bdesc, sm100::idesc_mxf4(kN, sel, sel),
-                              sf_col | (sel << 30), (sf_col + 4) | (sel << 30),
-                              (first && j == 0) ? 0u : 1u);
+            for (int c = 0; c < ncs; ++c) {
+              // Chunk c: its scale factors into tensor memory, then the MMAs
+              // of its two K=64 halves (blocks 4c .. 4c + 3).
+              const uint32_t sf_col =
+                  tmem + C::kSfBase + s * C::kSfCols + (NV == 2 ? m * 8 * C::kSfc : 0) + c * 8;
+              const uint8_t *sfb = W ? sSFB + C::kSfbRec + (m * C::kSfc + c) * 512
+                                     : sSFB + c * (kN * 16);
+              sm100::tmem_cp_32x128b_x4(sf_col,
+                                        sm100::smem_desc(sm100::smem_u32(sfa_v + c * 512), 0, 128));
+              sm100::tmem_cp_32x128b_x4(sf_col + 4, sm100::smem_desc(sm100::smem_u32(sfb), 0, 128));
+              const int j1 = 2 * c + 2 < kbn / 2 ? 2 * c + 2 : kbn / 2;
+              for (int j = 2 * c; j < j1; ++j) {
+                const uint32_t sel = uint32_t(2 * (j & 1));
+                // B: the pass's stacked rows of 16 B per block; K-halves one
+                // block apart.
+                const uint64_t bdesc =
+                    sm100::smem_desc(sm100::smem_u32(sB + 2 * j * (kN * 16)), kN * 16, 128);
+                const uint64_t adesc = sm100::smem_desc(
+                    sm100::smem_u32(sA + (v * C::kCh + 2 * j) * 2048), 2048, 128);
+                sm100::mma_mxf4(d0, adesc, bdesc, sm100::idesc_mxf4(kN, sel, sel),
+                                sf_col | (sel << 30), (sf_col + 4) | (sel << 30),
+                                (first && j == 0) ? 0u : 1u);
+              }
             }
             sm100::tc_commit(&empty[s]);
           }
@@ -934,13 +961,29 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
                   int64_t split_bytes, const FfnBias *bias, const Combine *comb,
                   bool allow_wide) {
   const msb_pool_s *pool = pools[0];
+  if (row0[0] % 128 != 0)
+    return fail(MSB_ERR_INVALID, "tensor-core path: the first view must start on a 128-row tile");
+  // Split over K for small batches, where the items alone leave CTAs idle:
+  // up to kSplitMax segments, as many as the caller's scratch holds.
+  int64_t split_segs = 0;
+  if (split_ws && n_pairs > 0 && n_pairs <= kSplitPairs && !(res_rows && res_rows->done)) {
+    split_segs = (split_bytes - 256) / (int64_t(nv) * n_pairs * n_out * 4);
+    if (split_segs > kSplitMax) split_segs = kSplitMax;
+    if (split_segs < 2) split_segs = 0;
+  }
+  // Wide passes (24 pairs, 8-block stages) for prompt-sized batches: when the
+  // pairs would fill at least kWidePairsPerSlot passes-worth per possibly
+  // active slot. Not with K split, nor for the expert-parallel exchange
+  // (allow_wide false), whose rows are padded and few per expert.
+  const bool wide = split_segs == 0 && allow_wide && !res_rows &&
+                    wide_passes_enabled(n_pairs, max_active);
   tc::Args a{};
   if (bias) a.bias = *bias;
   if (comb) a.comb = *comb;
   for (int v = 0; v < 2; ++v) {
     const msb_pool_s *p = pools[nv == 2 ? v : 0];
     if (!p->has_tmap) return fail(MSB_ERR_UNSUPPORTED, "tensor-core path: pool has no tensor map");
-    a.tm_w[v] = p->tmap_w;
+    a.tm_w[v] = wide ? p->tmap_w8 : p->tmap_w;
     a.pool[v] = p->data;
     a.slot_stride[v] = p->slot_stride;
     a.N[v] = p->N;
@@ -973,40 +1016,28 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   a.osf = act_out ? act_out + int64_t(tc::kTerms) * a.o_nb * n_pairs * 16 : nullptr;
   a.act = act_f32;
   a.fa = fa ? *fa : FfnAct{};
-  // Split over K for small batches, where the items alone leave CTAs idle:
-  // up to kSplitMax segments, as many as the caller's scratch holds.
-  a.split_max = 0;
-  if (split_ws && n_pairs > 0 && n_pairs <= kSplitPairs && !(res_rows && res_rows->done)) {
-    const int64_t per = int64_t(nv) * n_pairs * n_out * 4;
-    int64_t sm = (split_bytes - 256) / per;
-    if (sm > kSplitMax) sm = kSplitMax;
-    if (sm >= 2) {
-      a.split_max = int(sm);
-      a.split_word = reinterpret_cast<int *>(split_ws);
-      a.part = reinterpret_cast<float *>(split_ws + 256);
-      a.slot_ids = route->slot_ids;
-    }
+  a.split_max = int(split_segs);
+  if (split_segs) {
+    a.split_word = reinterpret_cast<int *>(split_ws);
+    a.part = reinterpret_cast<float *>(split_ws + 256);
+    a.slot_ids = route->slot_ids;
   }
-  // Wide passes (24 pairs) for prompt-sized batches: when the pairs would
-  // fill at least kWidePairsPerSlot passes-worth per possibly active slot.
-  // Not for the expert-parallel exchange (allow_wide false), whose rows are
-  // padded and few per expert.
-  const bool wide = a.split_max == 0 && allow_wide && !res_rows &&
-                    wide_passes_enabled(n_pairs, max_active);
   {
     // A pair's four 16-byte term records of one block are 64 contiguous
     // bytes (8 elements of 8 bytes); a box line is the pairs of one pass
     // and block (512 or 1536 contiguous bytes). Boxes land as
-    // [block][pair][term] (terms) and [pair][term] (scales): B rows 4p + t.
+    // [block][pair][term] (terms) and [chunk][pair][term] (scales): B rows
+    // 4p + t.
     const int pairs_per_pass = wide ? tc::Cfg<1, true>::kPairs : tc::Cfg<1, false>::kPairs;
+    const int blocks_per_stage = wide ? tc::Cfg<1, true>::kCh : tc::Cfg<1, false>::kCh;
     const uint64_t nc = uint64_t((pool->nb + 3) / 4);
     const uint64_t row_u64 = uint64_t(n_pairs) * tc::kTerms * 2;
     const uint64_t dq[3] = {row_u64, uint64_t(pool->nb), 1};
     const uint64_t sq[2] = {row_u64 * 8, row_u64 * 8 * uint64_t(pool->nb)};
-    const uint32_t bq[3] = {uint32_t(pairs_per_pass * tc::kTerms * 2), uint32_t(tc::kChunk), 1};
+    const uint32_t bq[3] = {uint32_t(pairs_per_pass * tc::kTerms * 2), uint32_t(blocks_per_stage), 1};
     const uint64_t df[3] = {row_u64, nc, 1};
     const uint64_t sf[2] = {row_u64 * 8, row_u64 * 8 * nc};
-    const uint32_t bf[3] = {uint32_t(pairs_per_pass * tc::kTerms * 2), 1, 1};
+    const uint32_t bf[3] = {uint32_t(pairs_per_pass * tc::kTerms * 2), uint32_t(blocks_per_stage / 4), 1};
     if (!encode_tmap_u64_3d(&a.tm_aq, a.aq, dq, sq, bq) ||
         !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sf, bf))
       return fail(MSB_ERR_CUDA, "tensor-core path: activation tensor maps could not be encoded");

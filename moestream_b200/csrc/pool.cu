@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(256) repack_to_ggml_kernel(
   if (i >= N * nb) return;
   const int64_t n = i / nb, b = i % nb;
   const uint8_t *qs = slot_base + (b * N + n) * 16;
-  const uint8_t *sc = slot_base + nb * N * 16 + scale_offset(scale_bytes == 1, b, n, N);
+  const uint8_t *sc = slot_base + nb * N * 16 + scale_offset(scale_bytes == 1, b, n, N, nb);
   uint8_t *o = dst + (n * nb + b) * block_bytes;
   for (int j = 0; j < scale_bytes; ++j) o[j] = sc[j];
   for (int j = 0; j < 16; ++j) o[scale_bytes + j] = qs[j];
@@ -215,8 +215,9 @@ extern "C" int msb_pool_create(int wtype, int64_t K, int64_t N, int32_t n_slot,
   if (e == cudaSuccess && wtype == MSB_TYPE_MXFP4) {
     const uint64_t dims[3] = {uint64_t(N) * 2, uint64_t(p->nb), uint64_t(n_slot) + 1};
     const uint64_t strides[2] = {uint64_t(N) * 16, uint64_t(p->slot_stride)};
-    const uint32_t box[3] = {256, 4, 1};
-    p->has_tmap = encode_tmap_u64_3d(&p->tmap_w, p->data, dims, strides, box);
+    const uint32_t box[3] = {256, 4, 1}, box8[3] = {256, 8, 1};
+    p->has_tmap = encode_tmap_u64_3d(&p->tmap_w, p->data, dims, strides, box) &&
+                  encode_tmap_u64_3d(&p->tmap_w8, p->data, dims, strides, box8);
   }
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) { msb_pool_destroy(p); return fail(MSB_ERR_CUDA, "msb_pool_create: init failed: %s", cudaGetErrorString(e)); }

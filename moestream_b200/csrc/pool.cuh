@@ -23,10 +23,12 @@ struct msb_pool_s {
   uint8_t *stage_meta = nullptr; // device copy of (slots, source pointers)
   uint8_t *host_meta = nullptr;  // pinned host block for that copy
   cudaEvent_t meta_free = nullptr;
-  // 3-D tensor map of the nibbles in 8-byte elements: (2 per row over the
+  // 3-D tensor maps of the nibbles in 8-byte elements: (2 per row over the
   // N rows of a block, blocks, slots), box (256, 4, 1) = a 128-row tile of
-  // 4 blocks, one 2 KB line per block; valid when has_tmap (MXFP4 pools).
+  // 4 blocks (tmap_w) or (256, 8, 1) = of 8 blocks (tmap_w8), one 2 KB line
+  // per block; valid when has_tmap (MXFP4 pools).
   alignas(64) CUtensorMap tmap_w;
+  alignas(64) CUtensorMap tmap_w8;
   bool has_tmap = false;
 };
 
@@ -40,7 +42,7 @@ bool encode_tmap_u64_3d(CUtensorMap *map, const void *base, const uint64_t dims[
 
 // Read-only view of one pool for the matmul kernels. Row n of block b of
 // slot s: qs at base + s*slot_stride + (b*N + row0 + n)*16, scale at
-// base + s*slot_stride + nb*N*16 + scale_offset(mx, b, row0 + n, N).
+// base + s*slot_stride + nb*N*16 + scale_offset(mx, b, row0 + n, N, nb).
 struct PoolView {
   const uint8_t *base;
   int64_t slot_stride;
@@ -95,7 +97,7 @@ __device__ __forceinline__ void repack_tile(uint8_t *tile, const uint8_t *src_ex
       uint4 v;
       memcpy(&v, q, 16);
       *reinterpret_cast<uint4 *>(dst + (b * N + n) * 16) = v;
-      uint8_t *sd = dst_scale + scale_offset(mx, b, n, N);
+      uint8_t *sd = dst_scale + scale_offset(mx, b, n, N, nb);
       for (int j = 0; j < scale_bytes; ++j) sd[j] = blk[j];
     }
   }

@@ -64,12 +64,16 @@ __device__ __forceinline__ void decode_nibbles(uint32_t q, const Codebook &cb,
 }
 
 // Byte offset of the scale of (block b, row n) within a slot's scale region
-// (N = rows stored per slot).
+// (N rows and nb blocks stored per slot). MXFP4: one 512-byte record per
+// (128-row tile, chunk of 4 blocks), tile-major, so a tile's consecutive
+// chunks are contiguous; inside a record row r of the tile is byte
+// (r % 32) * 16 + (r / 32) * 4 + (b % 4) -- the tensor core's 32x4
+// scale-factor atom.
 __host__ __device__ __forceinline__ int64_t scale_offset(bool mx, int64_t b, int64_t n,
-                                                         int64_t N) {
+                                                         int64_t N, int64_t nb) {
   if (!mx) return (b * N + n) * 2;
   const int64_t r = n & 127;
-  return ((b >> 2) * ((N + 127) >> 7) + (n >> 7)) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3);
+  return ((n >> 7) * ((nb + 3) >> 2) + (b >> 2)) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3);
 }
 
 __host__ __device__ __forceinline__ int64_t scale_region_bytes(bool mx, int64_t nb, int64_t N) {
