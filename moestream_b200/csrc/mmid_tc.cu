@@ -556,6 +556,13 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
     const int m = warp - 1;
     if (m < C::kMma) {
       uint32_t it = 0, acc = 0;
+      // Base descriptors at the shared-memory base: A (2 KB per block of
+      // 128 rows), B (the pass's kN rows per block) and the 32-row scale atoms.
+      const uint32_t smem_base = sm100::smem_u32(smem);
+      const uint64_t desc_a = sm100::smem_desc(smem_base, 2048, 128);
+      const uint64_t desc_b = sm100::smem_desc(smem_base, kN * 16, 128);
+      const uint64_t desc_sf = sm100::smem_desc(smem_base, 0, 128);
+      constexpr uint32_t kIdesc0 = sm100::idesc_mxf4(kN, 0, 0), kIdesc2 = sm100::idesc_mxf4(kN, 2, 2);
       int cur = 0;
       const int v = NV == 2 ? m : 0;
       // Scale rows of a view that starts `shift` 32-row groups into a tile:
@@ -593,7 +600,7 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
             break;
           }
           uint8_t *st = smem + s * C::kStage;
-          uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
+          uint8_t *sSFA = st + C::kA, *sSFB = sSFA + C::kSFA + C::kB;
           uint8_t *sfa_v = sSFA + (v == 0 ? 0 : C::kSfa0);
           const int kbn = int(a.nb - i * C::kCh < C::kCh ? a.nb - i * C::kCh : C::kCh);
           const int ncs = (kbn + 3) / 4;   // scale chunks with MMAs in this stage
@@ -629,28 +636,39 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
           }
           __syncwarp();
           if (lane == 0) {
-            for (int c = 0; c < ncs; ++c) {
-              // Chunk c: its scale factors into tensor memory, then the MMAs
-              // of its two K=64 halves (blocks 4c .. 4c + 3).
-              const uint32_t sf_col =
-                  tmem + C::kSfBase + s * C::kSfCols + (NV == 2 ? m * 8 * C::kSfc : 0) + c * 8;
-              const uint8_t *sfb = W ? sSFB + C::kSfbRec + (m * C::kSfc + c) * 512
-                                     : sSFB + c * (kN * 16);
-              sm100::tmem_cp_32x128b_x4(sf_col,
-                                        sm100::smem_desc(sm100::smem_u32(sfa_v + c * 512), 0, 128));
-              sm100::tmem_cp_32x128b_x4(sf_col + 4, sm100::smem_desc(sm100::smem_u32(sfb), 0, 128));
-              const int j1 = 2 * c + 2 < kbn / 2 ? 2 * c + 2 : kbn / 2;
-              for (int j = 2 * c; j < j1; ++j) {
-                const uint32_t sel = uint32_t(2 * (j & 1));
-                // B: the pass's stacked rows of 16 B per block; K-halves one
-                // block apart.
-                const uint64_t bdesc =
-                    sm100::smem_desc(sm100::smem_u32(sB + 2 * j * (kN * 16)), kN * 16, 128);
-                const uint64_t adesc = sm100::smem_desc(
-                    sm100::smem_u32(sA + (v * C::kCh + 2 * j) * 2048), 2048, 128);
-                sm100::mma_mxf4(d0, adesc, bdesc, sm100::idesc_mxf4(kN, sel, sel),
-                                sf_col | (sel << 30), (sf_col + 4) | (sel << 30),
-                                (first && j == 0) ? 0u : 1u);
+            // Byte offsets of the stage's operands from the shared-memory
+            // base, added to the base descriptors (the address field holds
+            // address / 16 in 14 bits; shared addresses stay below 2^18, so
+            // the adds never carry out of it).
+            const uint32_t st_off = uint32_t(s) * uint32_t(C::kStage);
+            const uint32_t a_off = st_off + uint32_t(v * C::kCh * 2048);
+            const uint32_t b_off = st_off + uint32_t(C::kA + C::kSFA);
+            const uint32_t sfa_off = st_off + uint32_t(C::kA + (v == 0 ? 0 : C::kSfa0));
+            const uint32_t sfb_off =
+                st_off + uint32_t(C::kA + C::kSFA + C::kB) +
+                (W ? uint32_t(C::kSfbRec + m * C::kSfc * 512) : 0u);
+            constexpr uint32_t kSfbStep = W ? 512u : uint32_t(kN * 16);
+            const uint32_t sf0 = tmem + C::kSfBase + s * C::kSfCols + (NV == 2 ? m * 8 * C::kSfc : 0);
+#pragma unroll
+            for (int c = 0; c < C::kSfc; ++c) {
+              if (c < ncs) {
+                // Chunk c: its scale factors into tensor memory, then the
+                // MMAs of its two K=64 halves (blocks 4c .. 4c + 3).
+                const uint32_t sf_col = sf0 + c * 8;
+                sm100::tmem_cp_32x128b_x4(sf_col, desc_sf + ((sfa_off + c * 512) >> 4));
+                sm100::tmem_cp_32x128b_x4(sf_col + 4, desc_sf + ((sfb_off + c * kSfbStep) >> 4));
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int j = 2 * c + h;
+                  // B: the pass's stacked rows of 16 B per block; K-halves
+                  // one block apart. A: 2 KB per block.
+                  if (j < kbn / 2)
+                    sm100::mma_mxf4(d0, desc_a + ((a_off + j * 4096) >> 4),
+                                    desc_b + ((b_off + j * (2 * kN * 16)) >> 4),
+                                    h ? kIdesc2 : kIdesc0, sf_col | (h ? 2u << 30 : 0u),
+                                    (sf_col + 4) | (h ? 2u << 30 : 0u),
+                                    (first && j == 0) ? 0u : 1u);
+                }
               }
             }
             sm100::tc_commit(&empty[s]);
