@@ -36,6 +36,7 @@ int64_t tc_act_bytes(int64_t nb, int64_t rows);
 // Scratch for the split over K of small batches (0 when the batch is not
 // small): partial sums of up to two views with n_out_max rows.
 int64_t tc_split_bytes(int64_t n_out_max, int64_t n_pairs);
+int64_t tc_split_zero_words(int64_t n_pairs);
 int tc_supported(const msb_pool_s *p);
 int set_wide_policy(int v);
 // IQ4_NL on the tensor cores (mmid_f16.cu).
@@ -545,13 +546,16 @@ extern "C" int msb_mul_mat_id(msb_pool_t pool, const void *b_dev, int b_type, in
   if (g_mxfp4_path == 0 && tc_supported(pool)) {
     // Tensor cores: activation terms per pair (grouped order), then one
     // projection writing res directly.
+    // The rest of the workspace is the split scratch; its segment counters
+    // are zeroed by the activation-terms kernel.
     uint8_t *act = ws;
+    const int64_t used = align_up(tc_act_bytes(pool->nb, pairs), 256);
     if (int rc = tc_act_terms(b_dev, b_type, b_ne1, b_nb1, b_nb2, top_k, route->rows, pairs,
-                              pool->nb, act, st))
+                              pool->nb, act, st, reinterpret_cast<uint32_t *>(ws + used),
+                              tc_split_zero_words(pairs)))
       return rc;
     const int64_t row0[2] = {0, 0};
     const msb_pool_s *pools[2] = {pool, pool};
-    const int64_t used = align_up(tc_act_bytes(pool->nb, pairs), 256);
     return tc_projection(pools, 1, row0, pool->N, route, pairs, act, res_dev, nullptr, nullptr,
                          max_active, st, nullptr, nullptr, ws + used, workspace_bytes - used);
   }
@@ -678,11 +682,14 @@ static int moe_ffn_core(msb_pool_t gate, msb_pool_t up, int64_t up_row0, msb_poo
       comb.accumulate = accumulate;
     }
     // The rest: scratch for the split over K of small batches (gate/up and
-    // down use it one after the other).
+    // down use it one after the other). The activation-terms kernel zeroes
+    // the combine's counters and the split's segment counters, which follow
+    // them.
     uint8_t *split_ws = ws + o;
     const int64_t split_bytes = workspace_bytes - o;
+    const int64_t zero_n = (split_ws - reinterpret_cast<uint8_t *>(cnt)) / 4 + tc_split_zero_words(pairs);
     if (int rc = tc_act_terms(x_dev, x_type, 1, x_nb1, x_nb1, top_k, route->rows, pairs, gate->nb,
-                              xa, st, w_dev ? cnt : nullptr, cnt_n))
+                              xa, st, zero_n ? cnt : nullptr, zero_n))
       return rc;
     const int64_t rows_gu[2] = {0, up_row0};
     const msb_pool_s *gu_pools[2] = {gate, up};

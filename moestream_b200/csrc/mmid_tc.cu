@@ -41,8 +41,9 @@
 // down projection's activation terms directly.
 // Batches of up to 8 pairs leave most CTAs without an item, so there a work
 // item is also one of up to 4 segments of the K chunks: the epilogue stores
-// f32 partial sums and split_reduce_kernel adds the segments in order and
-// runs the epilogue (every CTA derives the same split from the route).
+// f32 partial sums and counts its segment in; the warp that completes a
+// 32-row block's count adds the segments in order and runs the epilogue
+// (every CTA derives the same split from the route).
 // Every mbarrier wait is bounded (the library's wait limit, one second by
 // default); a wait that gives up sets
 // a bit of the device status word (msb_device_status) and the CTA stops
@@ -162,14 +163,14 @@ struct Args {
   FfnAct fa;                 // two views: the activation
   // Split over K for small batches (split_max > 0): a work item is also a
   // segment of the K chunks; the epilogue stores f32 partial sums
-  // part[((seg * NV + view) * a_rows + position) * n_out + row] and
-  // split_reduce_kernel finishes (sums in segment order, then the
-  // activation and terms, or the result rows). The split the launch picks
-  // is written to *split_word.
+  // part[((seg * NV + view) * a_rows + position) * n_out + row] and counts
+  // the segment in at split_cnt[item * 4 + 32-row block of the tile]
+  // (zeroed before the launch); the warp that brings a count to the split
+  // finishes those rows (sums in segment order, then the activation and
+  // terms, or the result rows and the combine).
   int split_max;
   float *part;
-  int *split_word;
-  const int32_t *slot_ids;   // slot of each pair (split reduce)
+  unsigned *split_cnt;
   long long wait_ns;         // bound of every mbarrier wait (wait_limit_ns)
   FfnBias bias;              // expert biases of each view (optional)
   Combine comb;              // one view: the fused router-weighted combine (optional)
@@ -356,46 +357,40 @@ __device__ __forceinline__ Item locate(const Args &a, const int *item0, int64_t 
   return Item{slot, int(local % passes), (local / passes) * 128};
 }
 
-// Split over K: sums the segments' partial results in order and finishes
-// the epilogue of tc_kernel<NV> -- the activation and the down projection's
-// terms (two views) or the result rows (one view); pairs routed to the zero
-// slot get exact zeros, as in the epilogue. One warp per (pair position,
-// 32-row block), lane = row.
+// Split over K: the last segment's warp of one 32-row block sums the
+// segments' partial results of each of the pass's cc pairs in segment order
+// and finishes the epilogue -- the activation and the down projection's
+// terms (two views) or the result rows and the combine (one view). Lane =
+// row n of block blk; the pairs are at grouped positions pos .. pos + cc - 1.
 template <int NV>
-__global__ void __launch_bounds__(256) split_reduce_kernel(const __grid_constant__ Args a) {
-  pdl_wait();
-  pdl_trigger();
-  const int lane = threadIdx.x & 31;
-  const int64_t nblk = (a.n_out + 31) / 32;
-  const int64_t wid = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (wid >= a.a_rows * nblk) return;   // whole warps only
-  const int64_t p = wid / nblk, blk = wid - p * nblk;
-  const int64_t n = blk * 32 + lane;
+__device__ __forceinline__ void split_finish(const Args &a, int split, int64_t pos, int cc,
+                                             int64_t blk, int64_t n, int lane) {
   const bool valid = n < a.n_out;
-  const int64_t pair = a.rows[p];
-  const bool zero = a.slot_ids[pair] == a.zero_slot;
-  const int split = *a.split_word;
-  if (split <= 1) return;   // tc_kernel finished the epilogue itself
-  float g = 0.f, u = 0.f;
-  if (!zero && valid) {
-    for (int sg = 0; sg < split; ++sg) {
-      g += a.part[((int64_t(sg) * NV) * a.a_rows + p) * a.n_out + n];
-      if constexpr (NV == 2) u += a.part[((int64_t(sg) * NV + 1) * a.a_rows + p) * a.n_out + n];
+  for (int j = 0; j < cc; ++j) {
+    const int64_t p = pos + j;
+    const int64_t pair = a.rows[p];
+    float g = 0.f, u = 0.f;
+    if (valid) {
+      for (int sg = 0; sg < split; ++sg) {
+        g += __ldcg(a.part + ((int64_t(sg) * NV) * a.a_rows + p) * a.n_out + n);
+        if constexpr (NV == 2)
+          u += __ldcg(a.part + ((int64_t(sg) * NV + 1) * a.a_rows + p) * a.n_out + n);
+      }
+      if (const float *br = bias_row(a.bias, 0, pair)) g += br[n];
+      if constexpr (NV == 2)
+        if (const float *br = bias_row(a.bias, 1, pair)) u += br[n];
     }
-    if (const float *br = bias_row(a.bias, 0, pair)) g += br[n];
-    if constexpr (NV == 2)
-      if (const float *br = bias_row(a.bias, 1, pair)) u += br[n];
+    if constexpr (NV == 1) {
+      if (valid) out_row(a.out, pair)[n] = g;
+    } else {
+      const float h = valid ? ffn_act(a.fa, g, u) : 0.f;
+      if (a.act && valid) a.act[pair * a.n_out + n] = h;
+      if (blk < a.o_nb)
+        warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, p), 16,
+                        a.osf + a4_off(0, blk / 4, a.a_rows, p) + (blk & 3), 16);
+    }
   }
-  if constexpr (NV == 1) {
-    if (valid && !(zero && a.out.skip_zero)) out_row(a.out, pair)[n] = g;
-    combine_arrive(a.comb, pair, 1, blk, lane);
-  } else {
-    const float h = (!zero && valid) ? ffn_act(a.fa, g, u) : 0.f;
-    if (a.act && valid) a.act[pair * a.n_out + n] = h;
-    if (blk < a.o_nb)
-      warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, p), 16,
-                      a.osf + a4_off(0, blk / 4, a.a_rows, p) + (blk & 3), 16);
-  }
+  if constexpr (NV == 1) combine_arrive(a.comb, lane < cc ? a.rows[pos + lane] : 0, cc, blk, lane);
 }
 
 template <int NV, bool W>
@@ -482,9 +477,7 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
     if (sp > a.split_max) sp = a.split_max;
     if (sp > by_chunks) sp = by_chunks;
     split = sp < 1 ? 1 : int(sp);
-    if (blockIdx.x == 0 && threadIdx.x == 0) *a.split_word = split;
   }
-  // With one segment the epilogue finishes as usual and the reduce exits.
   const bool split_mode = split > 1;
   const int64_t n_work = n_items * split;
 
@@ -704,8 +697,7 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
       const int64_t blk = (n0 >> 5) + quad;   // SwiGLU output block of this warp
       const int c_total = a.counts[slot];
       const int64_t pos0 = a.offsets[slot];
-      if (slot == a.zero_slot && split_mode) continue;   // the split reduce writes them
-      if (slot == a.zero_slot && set != 0) continue;     // set 0 writes them
+      if (slot == a.zero_slot && (seg != 0 || set != 0)) continue;   // written once
       if (slot == a.zero_slot) {
         // Every weight of the zero slot is 0, so the exact result is 0; for
         // the down projection's input, 0 splits into four zero terms with
@@ -851,6 +843,21 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
               combine_arrive(a.comb, __shfl_sync(0xffffffffu, my_pair, (gq * 8 + lane) & 31), gcc,
                              blk, lane);
         }
+        if (split_mode) {
+          // This segment's partial sums of the 32-row block are stored:
+          // count the segment in (the stores are fenced before the count);
+          // the warp that completes the count finishes the block's rows.
+          __threadfence();
+          __syncwarp();
+          unsigned old = 0;
+          if (lane == 0) {
+            old = atomicAdd(a.split_cnt + wi * 4 + quad, 1u);
+            __threadfence();
+          }
+          old = __shfl_sync(0xffffffffu, old, 0);
+          __syncwarp();
+          if (old == unsigned(split - 1)) split_finish<NV>(a, split, pos, cc, blk, n, lane);
+        }
       }
     }
   }
@@ -903,8 +910,23 @@ int set_wide_policy(int v) {
   return MSB_OK;
 }
 
+// Split scratch: the segment counters of a two-view and of a one-view
+// launch (kSplitCntWords each: up to 9 active slots -- 8 pairs and the zero
+// slot -- x kSplitMaxTiles tiles x 4 row blocks), then the partial sums.
+// The counters must be zero when a launch starts: the activation-terms
+// kernel that precedes every launch chain zeroes them
+// (tc_split_zero_words).
+constexpr int64_t kSplitMaxTiles = 128;
+constexpr int64_t kSplitCntWords = (kSplitPairs + 1) * kSplitMaxTiles * 4;
+
 int64_t tc_split_bytes(int64_t n_out_max, int64_t n_pairs) {
-  return n_pairs > 0 && n_pairs <= kSplitPairs ? 256 + 2 * kSplitMax * n_pairs * n_out_max * 4 : 0;
+  return n_pairs > 0 && n_pairs <= kSplitPairs
+             ? 2 * kSplitCntWords * 4 + 2 * kSplitMax * n_pairs * n_out_max * 4
+             : 0;
+}
+
+int64_t tc_split_zero_words(int64_t n_pairs) {
+  return n_pairs > 0 && n_pairs <= kSplitPairs ? 2 * kSplitCntWords : 0;
 }
 
 int64_t tc_act_bytes(int64_t nb, int64_t rows) {
@@ -958,13 +980,6 @@ static int launch_tc_t(const tc::Args &a, int max_active, int64_t n_pairs, cudaS
                           st, a));
   count_launch();
   MSB_CUDA_TRY(cudaGetLastError());
-  if (a.split_max > 0) {
-    const int64_t warps = n_pairs * ((a.n_out + 31) / 32);
-    MSB_CUDA_TRY(launch_pdl(tc::split_reduce_kernel<NV>, dim3(unsigned((warps + 7) / 8)),
-                            dim3(256), 0, st, a));
-    count_launch();
-    MSB_CUDA_TRY(cudaGetLastError());
-  }
   return MSB_OK;
 }
 
@@ -984,8 +999,9 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   // Split over K for small batches, where the items alone leave CTAs idle:
   // up to kSplitMax segments, as many as the caller's scratch holds.
   int64_t split_segs = 0;
-  if (split_ws && n_pairs > 0 && n_pairs <= kSplitPairs && !(res_rows && res_rows->done)) {
-    split_segs = (split_bytes - 256) / (int64_t(nv) * n_pairs * n_out * 4);
+  if (split_ws && n_pairs > 0 && n_pairs <= kSplitPairs && !(res_rows && res_rows->done) &&
+      (n_out + 127) / 128 <= kSplitMaxTiles) {
+    split_segs = (split_bytes - 2 * kSplitCntWords * 4) / (int64_t(nv) * n_pairs * n_out * 4);
     if (split_segs > kSplitMax) split_segs = kSplitMax;
     if (split_segs < 2) split_segs = 0;
   }
@@ -1036,9 +1052,8 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   a.fa = fa ? *fa : FfnAct{};
   a.split_max = int(split_segs);
   if (split_segs) {
-    a.split_word = reinterpret_cast<int *>(split_ws);
-    a.part = reinterpret_cast<float *>(split_ws + 256);
-    a.slot_ids = route->slot_ids;
+    a.split_cnt = reinterpret_cast<unsigned *>(split_ws) + (nv == 2 ? 0 : kSplitCntWords);
+    a.part = reinterpret_cast<float *>(split_ws + 2 * kSplitCntWords * 4);
   }
   {
     // A pair's four 16-byte term records of one block are 64 contiguous
