@@ -111,11 +111,13 @@ struct Cfg {
   static constexpr int kSfa0 = kSfc * 512;
   static constexpr int kSfa1 = NV == 2 ? 2 * kSfc * 512 : 0;
   static constexpr int kSFA = kSfa0 + kSfa1;
-  static constexpr int kB = kCh * kN * 16;               // [block][pair][term] 16 B rows
-  // The activation terms' scale records of the pass, [chunk][pair][term] 16 B
-  // rows (a chunk's 4 block scales in the first word). With 8 pairs they are
-  // the MMA's 32-row scale atom as they stand; with 24 each MMA warp gathers
-  // rows 32j + l into word j of atom row l (kSfbAtom, per chunk).
+  // The pass's activation lines of the stage, [chunk][4 blocks, then the
+  // scale records][pair][term] 16 B rows: kB bytes of terms and kSfbRec of
+  // scale records (a chunk's 4 block scales in the first word). With 8
+  // pairs a chunk's records are the MMA's 32-row scale atom as they stand;
+  // with 24 each MMA warp gathers rows 32j + l into word j of atom row l
+  // (kSfbAtom, per chunk, after the lines).
+  static constexpr int kB = kCh * kN * 16;
   static constexpr int kSfbRec = kSfc * kN * 16;
   static constexpr int kSfbAtom = W ? 512 * kMma * kSfc : 0;
   static constexpr int kStage = kA + kSFA + kB + kSfbRec + kSfbAtom;
@@ -143,8 +145,7 @@ struct Cfg {
 
 struct Args {
   CUtensorMap tm_w[2];       // each view's pool: (8 B x 2 x rows, blocks, slots)
-  CUtensorMap tm_aq;         // activation terms: (8 B x 8 x pairs, blocks, 1)
-  CUtensorMap tm_asf;        // their scales: (8 B x 8 x pairs, chunks, 1)
+  CUtensorMap tm_aq;         // activation terms and scales: (8 B x 8 x pairs, 5 lines, chunks)
   const uint8_t *pool[2];    // slot 0 of each view's pool
   int64_t slot_stride[2], N[2];
   int64_t nb;                // blocks per row (K / 32), same for both views
@@ -154,10 +155,10 @@ struct Args {
   int tiles;                 // ceil(n_out / 128)
   const int32_t *counts, *offsets, *rows, *active;
   int32_t zero_slot;
-  const uint8_t *aq, *asf;   // activation terms (grouped pair order)
+  const uint8_t *aq;         // activation terms and scales (grouped pair order)
   int64_t a_rows;            // rows of the activation buffers (= pairs)
   RowTarget out;              // one view: result row of each pair
-  uint8_t *oq, *osf;         // two views: terms of silu(gate) * up
+  uint8_t *oq;               // two views: terms and scales of silu(gate) * up
   int64_t o_nb;              // n_out / 32
   float *act;                // two views, optional: f32 silu(gate) * up
   FfnAct fa;                 // two views: the activation
@@ -182,13 +183,23 @@ __device__ int g_status;
 constexpr int kStatusProducer = 1, kStatusAccEmpty = 2, kStatusFull = 4, kStatusAccFull = 8,
               kStatusDrain = 16;
 
-// Byte offset of the 16-byte record of (term t, block or chunk b, row r) in
-// an activation-term buffer of `rows` rows: [b][r][t][16 B]. The records of
-// one pass (8 consecutive rows, all terms) of one block are 512 contiguous
-// bytes -- the stacked B operand of one MMA K-half (row 4p + t), or its 32
-// scale rows -- so the pass moves as one 512-byte line per block.
-__device__ __forceinline__ int64_t a4_off(int t, int64_t b, int64_t rows, int64_t r) {
-  return ((b * rows + r) * kTerms + t) * 16;
+// Activation-term buffers of `rows` rows (grouped pair positions) are lines
+// of [r][t][16 B] records, five per chunk of 4 blocks: the chunk's four
+// blocks' packed terms, then the chunk's scale records (the 4 block scales in
+// the first word). The records of one pass (8 or 24 consecutive rows, all
+// terms) of one line are contiguous -- the stacked B operand of one MMA
+// K-half (row 4p + t) or its scale rows -- so one tiled copy moves a pass's
+// blocks and scales of a stage together. Byte offset of the record of
+// (term t, line, row r):
+__device__ __forceinline__ int64_t act_line_off(int t, int64_t line, int64_t rows, int64_t r) {
+  return ((line * rows + r) * kTerms + t) * 16;
+}
+// ... of block b's packed terms, and of chunk c's scale records.
+__device__ __forceinline__ int64_t act_q_off(int t, int64_t b, int64_t rows, int64_t r) {
+  return act_line_off(t, (b >> 2) * 5 + (b & 3), rows, r);
+}
+__device__ __forceinline__ int64_t act_sf_off(int t, int64_t c, int64_t rows, int64_t r) {
+  return act_line_off(t, c * 5 + 4, rows, r);
 }
 
 // Splits the block held by the warp (lane j = element j) into kTerms e2m1
@@ -339,8 +350,8 @@ __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t n
     if constexpr (sizeof(T) == 4) r[e] = live ? float(x[el[e]]) : 0.f;
     else r[e] = live ? __bfloat162float(x[el[e]]) : 0.f;
   }
-  group_e2m1_terms(r, l, live, q + a4_off(0, blk, n_pairs, pos), 16,
-                   sf + a4_off(0, blk / 4, n_pairs, pos) + (blk & 3), 16);
+  group_e2m1_terms(r, l, live, q + act_q_off(0, blk, n_pairs, pos), 16,
+                   q + act_sf_off(0, blk / 4, n_pairs, pos) + (blk & 3), 16);
 }
 
 // Item w of the launch: its active-slot index (cursor, advanced
@@ -386,8 +397,8 @@ __device__ __forceinline__ void split_finish(const Args &a, int split, int64_t p
       const float h = valid ? ffn_act(a.fa, g, u) : 0.f;
       if (a.act && valid) a.act[pair * a.n_out + n] = h;
       if (blk < a.o_nb)
-        warp_e2m1_terms(h, lane, a.oq + a4_off(0, blk, a.a_rows, p), 16,
-                        a.osf + a4_off(0, blk / 4, a.a_rows, p) + (blk & 3), 16);
+        warp_e2m1_terms(h, lane, a.oq + act_q_off(0, blk, a.a_rows, p), 16,
+                        a.oq + act_sf_off(0, blk / 4, a.a_rows, p) + (blk & 3), 16);
     }
   }
   if constexpr (NV == 1) combine_arrive(a.comb, lane < cc ? a.rows[pos + lane] : 0, cc, blk, lane);
@@ -501,7 +512,7 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
             break;
           }
           uint8_t *st = smem + s * C::kStage;
-          uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA, *sSFB = sB + C::kB;
+          uint8_t *sA = st, *sSFA = st + C::kA, *sB = sSFA + C::kSFA;
           const int64_t b0 = i * C::kCh;     // first block of the stage
           const int64_t c0 = i * C::kSfc;    // its first scale chunk
           const int64_t nc = (a.nb + 3) / 4;
@@ -528,8 +539,8 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
             sm100::bulk_g2s(sfa_v, sf_tile, sf_bytes, &full[s]);
             if (next_sf[v]) sm100::bulk_g2s(sfa_v + C::kSfc * 512, sf_tile + nc * 512, sf_bytes, &full[s]);
           }
-          sm100::tma_3d(sB, &a.tm_aq, pos * 8, int(b0), 0, &full[s]);
-          sm100::tma_3d(sSFB, &a.tm_asf, pos * 8, int(c0), 0, &full[s]);
+          // The pass's activation terms and scales of the stage's chunks.
+          sm100::tma_3d(sB, &a.tm_aq, pos * 8, 0, int(c0), &full[s]);
         }
       }
       // No copy may still be landing in shared memory when the CTA exits
@@ -593,7 +604,7 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
             break;
           }
           uint8_t *st = smem + s * C::kStage;
-          uint8_t *sSFA = st + C::kA, *sSFB = sSFA + C::kSFA + C::kB;
+          uint8_t *sSFA = st + C::kA, *sB = sSFA + C::kSFA;
           uint8_t *sfa_v = sSFA + (v == 0 ? 0 : C::kSfa0);
           const int kbn = int(a.nb - i * C::kCh < C::kCh ? a.nb - i * C::kCh : C::kCh);
           const int ncs = (kbn + 3) / 4;   // scale chunks with MMAs in this stage
@@ -617,8 +628,8 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
               // Scale atom of chunk c of the pass's 96 B rows: word j of row
               // l is the record of B row 32j + l (rows 96-127 do not exist:
               // scale 0).
-              const uint8_t *recs = sSFB + c * (kN * 16);
-              uint8_t *atom = sSFB + C::kSfbRec + (m * C::kSfc + c) * 512;
+              const uint8_t *recs = sB + (c * 5 + 4) * (kN * 16);
+              uint8_t *atom = sB + C::kB + C::kSfbRec + (m * C::kSfc + c) * 512;
               const uint4 o = make_uint4(*reinterpret_cast<const uint32_t *>(recs + lane * 16),
                                          *reinterpret_cast<const uint32_t *>(recs + (32 + lane) * 16),
                                          *reinterpret_cast<const uint32_t *>(recs + (64 + lane) * 16),
@@ -635,12 +646,13 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
             // the adds never carry out of it).
             const uint32_t st_off = uint32_t(s) * uint32_t(C::kStage);
             const uint32_t a_off = st_off + uint32_t(v * C::kCh * 2048);
+            // B lines per chunk: 4 blocks, then the scale records.
+            constexpr uint32_t kLine = uint32_t(kN * 16);
             const uint32_t b_off = st_off + uint32_t(C::kA + C::kSFA);
             const uint32_t sfa_off = st_off + uint32_t(C::kA + (v == 0 ? 0 : C::kSfa0));
-            const uint32_t sfb_off =
-                st_off + uint32_t(C::kA + C::kSFA + C::kB) +
-                (W ? uint32_t(C::kSfbRec + m * C::kSfc * 512) : 0u);
-            constexpr uint32_t kSfbStep = W ? 512u : uint32_t(kN * 16);
+            const uint32_t sfb_off = W ? b_off + uint32_t(C::kB + C::kSfbRec + m * C::kSfc * 512)
+                                       : b_off + 4 * kLine;
+            constexpr uint32_t kSfbStep = W ? 512u : 5 * kLine;
             const uint32_t sf0 = tmem + C::kSfBase + s * C::kSfCols + (NV == 2 ? m * 8 * C::kSfc : 0);
 #pragma unroll
             for (int c = 0; c < C::kSfc; ++c) {
@@ -657,7 +669,7 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
                   // one block apart. A: 2 KB per block.
                   if (j < kbn / 2)
                     sm100::mma_mxf4(d0, desc_a + ((a_off + j * 4096) >> 4),
-                                    desc_b + ((b_off + j * (2 * kN * 16)) >> 4),
+                                    desc_b + ((b_off + (c * 5 + 2 * h) * kLine) >> 4),
                                     h ? kIdesc2 : kIdesc0, sf_col | (h ? 2u << 30 : 0u),
                                     (sf_col + 4) | (h ? 2u << 30 : 0u),
                                     (first && j == 0) ? 0u : 1u);
@@ -720,9 +732,9 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
           if (blk < a.o_nb) {
             const int t = lane & 3;
             for (int j = lane >> 2; j < c_total; j += 8) {
-              *reinterpret_cast<uint4 *>(a.oq + a4_off(t, blk, a.a_rows, pos0 + j)) =
+              *reinterpret_cast<uint4 *>(a.oq + act_q_off(t, blk, a.a_rows, pos0 + j)) =
                   make_uint4(0u, 0u, 0u, 0u);
-              a.osf[a4_off(t, blk / 4, a.a_rows, pos0 + j) + (blk & 3)] = 0;
+              a.oq[act_sf_off(t, blk / 4, a.a_rows, pos0 + j) + (blk & 3)] = 0;
             }
           }
         }
@@ -831,8 +843,8 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
                   r[4 + e] = sh[j * 32 + 16 + 4 * sub + e];
                 }
                 const int64_t p_row = pos + gq * 8 + j;
-                group4_e2m1_terms(r, sub, mask, a.oq + a4_off(0, blk, a.a_rows, p_row), 16,
-                                  a.osf + a4_off(0, blk / 4, a.a_rows, p_row) + (blk & 3), 16);
+                group4_e2m1_terms(r, sub, mask, a.oq + act_q_off(0, blk, a.a_rows, p_row), 16,
+                                  a.oq + act_sf_off(0, blk / 4, a.a_rows, p_row) + (blk & 3), 16);
               }
               __syncwarp();
             }
@@ -930,7 +942,7 @@ int64_t tc_split_zero_words(int64_t n_pairs) {
 }
 
 int64_t tc_act_bytes(int64_t nb, int64_t rows) {
-  return int64_t(tc::kTerms) * (nb + (nb + 3) / 4) * rows * 16;
+  return int64_t(tc::kTerms) * 5 * ((nb + 3) / 4) * rows * 16;   // 5 lines per chunk
 }
 
 int tc_supported(const msb_pool_s *p) {
@@ -941,7 +953,7 @@ int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb
                  const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st,
                  uint32_t *zero, int64_t zero_n) {
   if (n_pairs == 0) return MSB_OK;
-  uint8_t *q = ws, *sf = ws + int64_t(tc::kTerms) * nb * n_pairs * 16;
+  uint8_t *q = ws, *sf = ws;   // one buffer: act_q_off / act_sf_off
   const int64_t grid = (n_pairs * ((nb + 3) / 4) + 7) / 8;
   const char *p = static_cast<const char *>(b);
   if (b_type == MSB_TYPE_F32)
@@ -1036,7 +1048,6 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
     return fail(MSB_ERR_UNSUPPORTED, "tensor-core path: %d slots exceed %d", pool->n_slot,
                 tc::kMaxActive - 1);
   a.aq = act_in;
-  a.asf = act_in + int64_t(tc::kTerms) * pool->nb * n_pairs * 16;
   a.a_rows = n_pairs;
   if (res_rows) {
     a.out = *res_rows;
@@ -1047,7 +1058,6 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   }
   a.oq = act_out;
   a.o_nb = n_out / 32;
-  a.osf = act_out ? act_out + int64_t(tc::kTerms) * a.o_nb * n_pairs * 16 : nullptr;
   a.act = act_f32;
   a.fa = fa ? *fa : FfnAct{};
   a.split_max = int(split_segs);
@@ -1056,24 +1066,19 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
     a.part = reinterpret_cast<float *>(split_ws + 2 * kSplitCntWords * 4);
   }
   {
-    // A pair's four 16-byte term records of one block are 64 contiguous
-    // bytes (8 elements of 8 bytes); a box line is the pairs of one pass
-    // and block (512 or 1536 contiguous bytes). Boxes land as
-    // [block][pair][term] (terms) and [chunk][pair][term] (scales): B rows
-    // 4p + t.
+    // A pair's four 16-byte term records of one line are 64 contiguous
+    // bytes (8 elements of 8 bytes); a box row is the pairs of one pass and
+    // line (512 or 1536 contiguous bytes), five lines per chunk. Boxes land
+    // as [chunk][4 blocks, scales][pair][term]: B rows 4p + t.
     const int pairs_per_pass = wide ? tc::Cfg<1, true>::kPairs : tc::Cfg<1, false>::kPairs;
-    const int blocks_per_stage = wide ? tc::Cfg<1, true>::kCh : tc::Cfg<1, false>::kCh;
+    const int chunks_per_stage = wide ? tc::Cfg<1, true>::kSfc : tc::Cfg<1, false>::kSfc;
     const uint64_t nc = uint64_t((pool->nb + 3) / 4);
     const uint64_t row_u64 = uint64_t(n_pairs) * tc::kTerms * 2;
-    const uint64_t dq[3] = {row_u64, uint64_t(pool->nb), 1};
-    const uint64_t sq[2] = {row_u64 * 8, row_u64 * 8 * uint64_t(pool->nb)};
-    const uint32_t bq[3] = {uint32_t(pairs_per_pass * tc::kTerms * 2), uint32_t(blocks_per_stage), 1};
-    const uint64_t df[3] = {row_u64, nc, 1};
-    const uint64_t sf[2] = {row_u64 * 8, row_u64 * 8 * nc};
-    const uint32_t bf[3] = {uint32_t(pairs_per_pass * tc::kTerms * 2), uint32_t(blocks_per_stage / 4), 1};
-    if (!encode_tmap_u64_3d(&a.tm_aq, a.aq, dq, sq, bq) ||
-        !encode_tmap_u64_3d(&a.tm_asf, a.asf, df, sf, bf))
-      return fail(MSB_ERR_CUDA, "tensor-core path: activation tensor maps could not be encoded");
+    const uint64_t dq[3] = {row_u64, 5, nc};
+    const uint64_t sq[2] = {row_u64 * 8, row_u64 * 8 * 5};
+    const uint32_t bq[3] = {uint32_t(pairs_per_pass * tc::kTerms * 2), 5, uint32_t(chunks_per_stage)};
+    if (!encode_tmap_u64_3d(&a.tm_aq, a.aq, dq, sq, bq))
+      return fail(MSB_ERR_CUDA, "tensor-core path: activation tensor map could not be encoded");
   }
   if (wide)
     return nv == 2 ? launch_tc_t<2, true>(a, max_active, n_pairs, st)
