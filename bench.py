@@ -564,13 +564,17 @@ def slots_main(args):
     MoE layers whose routed experts are all resident in slot pools (the
     reference's decode configurations of a slot cache that hits): gpt-oss
     layers (MXFP4 2880 x 2880 gate, up and down, 32 slots, top-4) or a
-    256-expert IQ4_NL model (hidden 2048, expert FFN 512, 64 slots, top-8).
+    256-expert IQ4_NL model (hidden 2048, expert FFN 512, 64 slots, top-8 plus
+    one shared expert).
     Weights quantized on the device from N(0, 0.02); ids are top_k distinct
-    random slots per token, new every step and layer. A batch above the slot
-    pool's arena threshold (6 tokens for both models) runs over per-layer
-    arenas of every expert instead, routed over all of them, as the reference
-    runs it. One CUDA graph per step; the roofline counts each distinct
-    referenced slot's bytes once per layer."""
+    random slots per token, new every step and layer. The 256-expert model's
+    shared expert is always resident in one more slot of each layer's pools:
+    every token's ids end with it, at weight 1 next to the routed experts'
+    weights, so it runs in the same grouped matmuls and combine. A batch
+    above the slot pool's arena threshold (6 tokens for both models) runs
+    over per-layer arenas of every expert instead, routed over all of them,
+    as the reference runs it. One CUDA graph per step; the roofline counts
+    each distinct referenced slot's bytes once per layer."""
     import torch
 
     from moestream_b200 import ops
@@ -586,35 +590,43 @@ def slots_main(args):
     arena = T > threshold
     if arena:
         NS = E
+    # The 256-expert model's shared expert: slot NS of every pool.
+    shared = 1 if args.model != "gpt-oss" else 0
+    NSP, top_k_all = NS + shared, top_k + shared
     t_setup = time.time()
     g = torch.Generator(device="cuda")
     g.manual_seed(77)
 
     def qpool(kk, nn):
-        pool = ops.SlotPool(wtype, kk, nn, NS, max_fill_batch=8)
-        for j0 in range(0, NS, 8):
-            wts = torch.randn(8 * nn, kk, generator=g, device="cuda") * 0.02
-            q = ops.quantize_rows(wtype, wts).view(8, -1)
-            pool.fill(list(range(j0, j0 + 8)), [q[i] for i in range(8)])
+        pool = ops.SlotPool(wtype, kk, nn, NSP, max_fill_batch=8)
+        for j0 in range(0, NSP, 8):
+            j1 = min(NSP, j0 + 8)
+            wts = torch.randn((j1 - j0) * nn, kk, generator=g, device="cuda") * 0.02
+            q = ops.quantize_rows(wtype, wts).view(j1 - j0, -1)
+            pool.fill(list(range(j0, j1)), [q[i] for i in range(j1 - j0)])
         return pool
     layers = [(qpool(K, n_ff), qpool(K, n_ff), qpool(n_ff, K)) for _ in range(L)]
     S = args.warmup + args.steps
     ids_all = torch.rand(S, L, T, NS, generator=g, device="cuda").argsort(dim=-1)[..., :top_k]
+    if shared:
+        ids_all = torch.cat([ids_all, torch.full((S, L, T, 1), NS, device="cuda")], dim=-1)
     ids_all = ids_all.to(torch.int32).contiguous()
-    w = torch.full((T, top_k), 1.0 / top_k, device="cuda")
+    w = torch.full((T, top_k_all), 1.0 / top_k, device="cuda")
+    if shared:
+        w[:, top_k] = 1.0
     x = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
     y = torch.empty(L, T, K, dtype=torch.float32, device="cuda")
-    route = ops.RouteBuffers(T * top_k, NS)
-    ws = ops.workspace(max(K, n_ff), T, top_k, NS)
-    ids_d = torch.empty(L, T, top_k, dtype=torch.int32, device="cuda")
+    route = ops.RouteBuffers(T * top_k_all, NSP)
+    ws = ops.workspace(max(K, n_ff), T, top_k_all, NSP)
+    ids_d = torch.empty(L, T, top_k_all, dtype=torch.int32, device="cuda")
     eb = sum(p.expert_bytes for p in layers[0])
     lib = ops.lib()
 
     def step():
         for il in range(L):
-            r = ops.remap_group(ids_d[il], NS, route=route)
+            r = ops.remap_group(ids_d[il], NSP, route=route)
             ga, up, dn = layers[il]
-            ops.moe_ffn(ga, up, dn, x, r, w, top_k, ws=ws, out=y[il])
+            ops.moe_ffn(ga, up, dn, x, r, w, top_k_all, ws=ws, out=y[il])
     for s_ in range(args.warmup):
         ids_d.copy_(ids_all[s_])
         step()
@@ -640,7 +652,7 @@ def slots_main(args):
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1)
-    timed = ids_all[args.warmup:].view(args.steps * L, T * top_k).cpu()
+    timed = ids_all[args.warmup:].view(args.steps * L, T * top_k_all).cpu()
     distinct = sum(len(torch.unique(row)) for row in timed)
     gbs = distinct * eb / (ms / 1e3) / 1e9
     peaks = {}
@@ -664,6 +676,7 @@ def slots_main(args):
                                     f"pool's threshold ({threshold} tokens): per-layer arenas "
                                     f"of all {E} experts"),
                        "n_layer": L, "slots": NS, "hidden": K, "n_ff": n_ff, "top_k": top_k,
+                       "shared_experts": shared,
                        "tokens": T, "distinct_per_layer": distinct / (args.steps * L),
                        "l2": "random slots every step and layer; pools far larger than L2"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",

@@ -137,6 +137,45 @@ def test_moe_ffn_matches_oracle(wtype, K, n_ff, n_expert, n_slot, n_tok, top_k, 
     assert O.max_abs_normalized(y, y_ex) < max(1e-2, form_err + 5e-4)
 
 
+@pytest.mark.parametrize("n_tok", [1, 8])
+def test_shared_expert_runs_with_the_routed_ones(n_tok, path):
+    """The 256-expert model's layer shape (IQ4_NL, hidden 2048, expert FFN
+    512) with an always-on shared expert: every token's ids are its top-k
+    routed experts plus the shared expert (its own slot, weight 1.0), so the
+    shared expert runs in the same grouped matmuls and combine. y matches
+    the oracle, which sums the shared expert's output into every token."""
+    from moestream_b200 import ops
+    n_routed, top_k, K, n_ff = 8, 4, 2048, 512
+    n_expert = n_routed + 1                      # expert n_routed is the shared one
+    pools, slabs, slot_of = build_layer("iq4_nl", K, n_ff, n_expert, n_expert, False, seed=31)
+    rng = np.random.default_rng(40 + n_tok)
+    x = rng.normal(0, 1, size=(n_tok, K)).astype(np.float32)
+    ids_r, w_r = topk_ids(rng, n_tok, n_routed, top_k)
+    ids_e = np.concatenate([ids_r, np.full((n_tok, 1), n_routed, np.int32)], axis=1)
+    w = np.concatenate([w_r, np.ones((n_tok, 1), np.float32)], axis=1)
+    table = np.full(n_expert, -1, dtype=np.int32)
+    for e, sl in slot_of.items():
+        table[e] = sl
+    slots = O.remap_table(ids_e, table, n_expert)
+    r = ops.remap_group(torch.from_numpy(ids_e).cuda(), n_expert,
+                        table=torch.from_numpy(table).cuda(), n_expert=n_expert)
+    y = ops.moe_ffn(pools["gate"], pools["up"], pools["down"], torch.from_numpy(x).cuda(), r,
+                    torch.from_numpy(w).cuda(), top_k + 1)
+    torch.cuda.synchronize()
+    y = y.cpu().numpy()
+    f16 = path.startswith("tc")
+    y_f, _ = O.moe_ffn("iq4_nl", slabs["gate"], slabs["up"], slabs["down"], K, n_ff, x, slots, w,
+                       mode="f16" if f16 else "q8")
+    y_ex, _ = O.moe_ffn("iq4_nl", slabs["gate"], slabs["up"], slabs["down"], K, n_ff, x, slots, w,
+                        mode="exact")
+    assert O.max_abs_normalized(y, y_f) < (1e-3 if f16 else 2e-3)
+    assert O.max_abs_normalized(y, y_ex) < max(1e-2, O.max_abs_normalized(y_f, y_ex) + 5e-4)
+    # The shared expert contributes to every token: without it y differs.
+    y_routed, _ = O.moe_ffn("iq4_nl", slabs["gate"], slabs["up"], slabs["down"], K, n_ff, x,
+                            slots[:, :top_k], w[:, :top_k], mode="exact")
+    assert O.max_abs_normalized(y_routed, y_ex) > 1e-2
+
+
 def test_unweighted_top1_writes_expert_output(path):
     """w omitted with top_k 1: y is the expert output itself, identical to
     weighting by 1.0."""
