@@ -16,22 +16,23 @@
 // shared memory once for all four terms; the epilogue adds the four f32
 // partial sums of a pair.
 //
-// Persistent CTAs (two per SM, 256 threads) walk the work items (active
-// slot x 128-row tile) with a stride of the grid; each item runs in passes of
-// 8 of the slot's (token, k) pairs. The pipeline never drains between
-// items: the producer streams the next item's tiles while the accumulators
-// of the previous one are read out. Roles:
-//   warp 0, lane 0 : producer -- per stage, one tiled TMA copy per weight
-//                    view (128 rows x 4 blocks, 8 KB), one 512-byte bulk
-//                    copy of each view's scale-factor chunk, one tiled TMA
-//                    copy of the pass's activation terms (4 blocks x 8
-//                    pairs x 4 terms: four 512-byte lines) and one of their
-//                    scales (one 512-byte line),
+// Persistent CTAs walk the work items (active slot x 128-row tile x pass)
+// with a stride of the grid; a pass is 8 of the slot's (token, k) pairs
+// (narrow: two CTAs per SM, 256 threads) or 24 (wide, prompt-sized batches:
+// one CTA per SM, 512 threads). The pipeline never drains between items:
+// the producer streams the next item's tiles while the accumulators of the
+// previous one are read out. Roles:
+//   warp 0, lane 0 : producer -- per stage (4 or 8 blocks of K), one tiled
+//                    TMA copy per weight view (128 rows x the stage's
+//                    blocks), one bulk copy per view of the stage's scale
+//                    records (a tile's chunks are contiguous in the pool),
+//                    and one tiled TMA copy of the pass's activation lines
+//                    (per chunk: 4 blocks of terms, then the scale records),
 //                    into a shared-memory ring;
-//   warps 1-3, lane 0 : copy the stage's scale factors into tensor memory
+//   warps 1-3, lane 0 : copy each chunk's scale factors into tensor memory
 //                    (tcgen05.cp) and issue the MMAs (one per K=64 step)
 //                    into one of two accumulator buffers -- with two views
-//                    warps 1-2 take one each, with one view warps 1-3 take
+//                    warps 1-2 take one each, with one view the MMA warps take
 //                    the stages in turn, each into its own accumulator;
 //                    tcgen05.commit frees the stage / hands over a buffer;
 //   warps 4-7      : epilogue -- warp w reads TMEM lanes 32*(w%4)..+31
@@ -322,14 +323,15 @@ __device__ __forceinline__ void group4_e2m1_terms(float (&r)[8], int sub, unsign
   }
 }
 
-// Activations of every pair in grouped order into the term layout:
-// q [nb][kTerms][rows][16 B], sf [ceil(nb/4)][kTerms][rows][16 B] (byte b%4).
-// One warp per (pair position, chunk of 4 blocks); 8 lanes per block.
+// Activations of every pair in grouped order into the line layout of
+// act_line_off (per chunk of 4 blocks: the blocks' term records, then the
+// chunk's scale records, block b's scale in byte b%4). One warp per (pair
+// position, chunk); 8 lanes per block.
 template <typename T>
 __global__ void __launch_bounds__(256) act_terms_kernel(const char *b, int64_t nb1, int64_t nb2,
                                                         int32_t ne1, int32_t top_k,
                                                         const int32_t *rows, int64_t n_pairs,
-                                                        int64_t nb, uint8_t *q, uint8_t *sf,
+                                                        int64_t nb, uint8_t *q,
                                                         uint32_t *zero, int64_t zero_n) {
   pdl_wait();
   pdl_trigger();
@@ -953,15 +955,15 @@ int tc_act_terms(const void *b, int b_type, int64_t ne1, int64_t nb1, int64_t nb
                  const int32_t *rows, int64_t n_pairs, int64_t nb, uint8_t *ws, cudaStream_t st,
                  uint32_t *zero, int64_t zero_n) {
   if (n_pairs == 0) return MSB_OK;
-  uint8_t *q = ws, *sf = ws;   // one buffer: act_q_off / act_sf_off
+  uint8_t *q = ws;   // terms and scales, act_q_off / act_sf_off
   const int64_t grid = (n_pairs * ((nb + 3) / 4) + 7) / 8;
   const char *p = static_cast<const char *>(b);
   if (b_type == MSB_TYPE_F32)
     MSB_CUDA_TRY(launch_pdl(tc::act_terms_kernel<float>, dim3(unsigned(grid)), dim3(256), 0, st, p,
-                            nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, sf, zero, zero_n));
+                            nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, zero, zero_n));
   else if (b_type == MSB_TYPE_BF16)
     MSB_CUDA_TRY(launch_pdl(tc::act_terms_kernel<__nv_bfloat16>, dim3(unsigned(grid)), dim3(256), 0,
-                            st, p, nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, sf, zero,
+                            st, p, nb1, nb2, int32_t(ne1), top_k, rows, n_pairs, nb, q, zero,
                             zero_n));
   else
     return fail(MSB_ERR_INVALID, "activation type %d is not F32 or BF16", b_type);
