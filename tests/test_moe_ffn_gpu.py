@@ -86,6 +86,9 @@ CASES = [
     ("mxfp4", 2880, 2880, 6, 4, 2, 4, True),     # gpt-oss widths, fused gate_up (up half off
                                                  # the 128-row tile grid)
     ("mxfp4", 2880, 2880, 6, 4, 3, 4, False),    # gpt-oss widths, separate gate and up
+    ("mxfp4", 2880, 2880, 6, 4, 16, 4, True),    # the same fused layout with 64 pairs: wide
+                                                 # passes (8-block stages, the up half's scale
+                                                 # records from two tiles)
     ("iq4_nl", 2048, 512, 10, 8, 8, 8, False),   # 256-expert model widths
     ("mxfp4", 512, 256, 8, 8, 40, 4, True),      # several passes per slot
     ("iq4_nl", 256, 128, 6, 3, 5, 2, False),
