@@ -1106,6 +1106,8 @@ def main():
         for g_i in graphs:
             g_i.replay()
     torch.cuda.synchronize()
+    from moestream_b200 import ops as _ops
+    setup_status = _ops.device_status(clear=True)   # warm-up and graph uploads
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.05)
@@ -1126,6 +1128,12 @@ def main():
     if args.eager:
         launches = int(lib.msb_kernel_launches()) - launches0
     clk = clocks.stop()
+    # Status bits of the timed steps' kernels: 0 unless a bounded wait gave
+    # up (then that launch stalled for the wait limit, one second).
+    timed_status = _ops.device_status(clear=True)
+    if timed_status:
+        print(f"bench: a bounded wait gave up in the timed steps (status {timed_status:#x})",
+              file=sys.stderr, flush=True)
     ms = t0.elapsed_time(t1)
     ms = max_over_ranks(ms, world)
     ms_step = ms / args.steps
@@ -1239,6 +1247,7 @@ def main():
                              "kernel": "tc_kernel<2> (fused gate/up mul_mat_id, tcgen05 mxf4)",
                              "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
+                "device_status": {"timed": timed_status, "before": setup_status},
                 "setup_s": round(t_setup, 1)}
         print(json.dumps(line), flush=True)
     if world > 1:
