@@ -146,15 +146,13 @@ __device__ __forceinline__ void flag_wait_block(const FlagWait &w) {
   if (int(threadIdx.x) < w.n) {
     const uint32_t seq = *reinterpret_cast<const volatile uint32_t *>(w.seq) * w.mult;
     const uint32_t *f = w.flags + threadIdx.x;
-    uint64_t t0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    // Bounded in SM cycles, 2 per ns of the limit (as sm100::wait_cycles).
+    const long long c0 = clock64(), lim = 2 * w.limit_ns;
     for (;;) {
       uint32_t v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
       if (int32_t(v - seq) >= 0) break;
-      uint64_t t;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-      if (t - t0 > uint64_t(w.limit_ns)) { ok = false; break; }
+      if (clock64() - c0 > lim) { ok = false; break; }
     }
   }
   if (!ok) atomicOr(w.status, w.bit);

@@ -49,13 +49,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Nanoseconds of the GPU's global timer (wall time, independent of the SM
-// clock).
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
+// The bound of every wait, in SM cycles (clock64: monotonic on the SM the
+// thread runs on) for a limit given in nanoseconds: 2 cycles per ns, at
+// least the limit at SM clocks up to 2 GHz (B200 peaks at 1.965 GHz). The
+// global timer is not used: read with an unsigned difference, a timer that
+// steps back once ends a wait at once, and a wait must only give up once
+// the limit has really passed.
+__device__ __forceinline__ long long wait_cycles(long long limit_ns) { return 2 * limit_ns; }
 
 // Waits for the phase of `parity` for at most `limit_ns` nanoseconds (the
 // library's wait limit, one second unless msb_set_option changed it); false
@@ -64,9 +64,9 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
                                                   long long limit_ns) {
   if (mbar_test_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long c0 = clock64(), lim = wait_cycles(limit_ns);
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > uint64_t(limit_ns)) return false;
+    if (clock64() - c0 > lim) return false;
   }
   return true;
 }
