@@ -1172,9 +1172,9 @@ def main():
         pass
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     # DRAM bytes (read + write) of one gate/up launch of this workload: the
-    # mean of the two launches of the committed ncu capture of the same layer
-    # shape (profiles/tc_kernel_moe_ffn_decode_64tok.md, last section); other
-    # shapes: unmeasured.
+    # mean of two launches of a 1-pass ncu capture of the same layer shape
+    # (dram__bytes_read.sum + dram__bytes_write.sum; the decode summary under
+    # profiles/); other shapes: unmeasured.
     traffic = 0.969e9 if (world == 1 and T == SHAPE["tokens"]) else None
     # Graphs holding NCCL calls must be gone before the process group is
     # destroyed.
