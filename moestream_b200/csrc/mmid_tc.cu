@@ -29,11 +29,12 @@
 //                    and one tiled TMA copy of the pass's activation lines
 //                    (per chunk: 4 blocks of terms, then the scale records),
 //                    into a shared-memory ring;
-//   warps 1-3, lane 0 : copy each chunk's scale factors into tensor memory
+//   warps 1-2, lane 0 : copy each chunk's scale factors into tensor memory
 //                    (tcgen05.cp) and issue the MMAs (one per K=64 step)
 //                    into one of two accumulator buffers -- with two views
-//                    warps 1-2 take one each, with one view the MMA warps take
-//                    the stages in turn, each into its own accumulator;
+//                    each takes one view, with one view they take the chunks
+//                    in turn (each warp its own stage ring), each into its
+//                    own accumulator;
 //                    tcgen05.commit frees the stage / hands over a buffer;
 //   warps 4-7      : epilogue -- warp w reads TMEM lanes 32*(w%4)..+31
 //                    (rows), releases the buffer, then stores (wide passes:
@@ -90,19 +91,30 @@ struct Cfg {
   // Epilogue warp sets (4 warps each, one per TMEM lane quadrant); set s
   // takes the pass's 8-pair groups s, s + kEpiSets, ...
   static constexpr int kEpiSets = W ? 3 : 1;
-  // Warp 0 producer, warps 1-3 MMA issue, then the epilogue sets.
+  // Warp 0 producer, warps 1-2 MMA issue (warp 3 idle), then the epilogue sets.
   static constexpr int kThreads = 128 + 128 * kEpiSets;
-  // MMA-issuing warps: one per view (gate and up), or two / three taking
-  // turns over the stages of a single view. One accumulator buffer holds one
+  // MMA-issuing warps: one per view (gate and up), or two taking turns
+  // over the chunks of a single view. One accumulator buffer holds one
   // N = kN accumulator per MMA warp.
-  static constexpr int kMma = NV == 2 ? 2 : (W ? 2 : 3);
-  // K blocks per stage: 4 (two K=64 MMAs per view), or 8 with wide passes.
-  // A stage costs its copy instructions more than its bytes (each tiled or
-  // bulk copy occupies the SM's copy engine for a few hundred cycles), so
-  // the prompt-sized passes move twice the bytes per instruction.
-  static constexpr int kCh = W ? 8 : 4;
+  static constexpr int kMma = 2;
+  // Stage rings. With two views every MMA warp consumes every stage: one
+  // ring. With one view each MMA warp owns a ring of kStages / kMma stages
+  // (stages m * kRing ..), filled with its chunks in order, so that each
+  // warp waits on every phase of the stages it reads. (A parity wait on a
+  // barrier two phases behind -- a stage whose previous copy, for another
+  // warp, has not landed -- would report the older phase as complete.)
+  static constexpr int kRings = NV == 2 ? 1 : kMma;
+  // K blocks per stage: 4 (two K=64 MMAs per view) for narrow two-view
+  // passes, else 8. A stage costs its copy instructions more than its bytes
+  // (each tiled or bulk copy occupies the SM's copy engine for a few hundred
+  // cycles), so wide passes and one-view launches move twice the bytes per
+  // instruction. (A narrow two-view stage of 8 blocks would take ~40 KB:
+  // two stages per CTA at two CTAs per SM.)
+  static constexpr int kCh = (W || NV == 1) ? 8 : 4;
   static constexpr int kSfc = kCh / 4;                   // 4-block scale chunks per stage
-  static constexpr int kStages = W ? (NV == 2 ? 4 : 6) : (NV == 2 ? 5 : 8);
+  static constexpr int kStages = W ? (NV == 2 ? 4 : 6) : (NV == 2 ? 5 : 4);
+  static constexpr int kRing = kStages / kRings;
+  static_assert(kStages % kRings == 0, "whole rings per MMA warp");
   static constexpr int kA = NV * kCh * 2048;             // 128 rows x 16 B per block
   // Scale factors of a weight view: one 512-byte record per 128-row tile and
   // chunk, a tile's chunks contiguous in the pool. View 0 starts on the tile
@@ -497,7 +509,7 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
   if (warp == 0) {
     // ---- producer ----
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t fills[C::kRings] = {};   // copies issued into each ring
       int cur = 0;
       for (int64_t w = blockIdx.x; w < n_work && !*abort_v; w += gridDim.x) {
         const int64_t wi = w / split, seg = w - wi * split;
@@ -506,9 +518,15 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
         if (slot == a.zero_slot) continue;
         const int pos = int(a.offsets[slot] + int64_t(item.pass) * kPairs);
         const int64_t lo = seg * n_chunks / split, hi = (seg + 1) * n_chunks / split;
-        for (int64_t i = lo; i < hi; ++i, ++it) {
-          const int s = it % kStages;
-          if (!sm100::mbar_wait_bounded(&empty[s], ((it / kStages) & 1) ^ 1, a.wait_ns)) {
+        for (int64_t i = lo; i < hi; ++i) {
+          // Chunk i goes to the ring of the MMA warp that reads it.
+          const int ring = C::kRings == 1 ? 0 : int(i % C::kRings);
+          uint32_t k = 0;   // (selects keep the counters in registers)
+#pragma unroll
+          for (int r = 0; r < C::kRings; ++r)
+            if (r == ring) k = fills[r];
+          const int s = ring * C::kRing + int(k % C::kRing);
+          if (!sm100::mbar_wait_bounded(&empty[s], ((k / C::kRing) & 1) ^ 1, a.wait_ns)) {
             atomicOr(&g_status, kStatusProducer);
             *abort_v = 1;
             break;
@@ -543,20 +561,29 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
           }
           // The pass's activation terms and scales of the stage's chunks.
           sm100::tma_3d(sB, &a.tm_aq, pos * 8, 0, int(c0), &full[s]);
+#pragma unroll
+          for (int r = 0; r < C::kRings; ++r)
+            if (r == ring) fills[r] = k + 1;
         }
       }
       // No copy may still be landing in shared memory when the CTA exits
-      // (only possible after an abort): wait for the last stages issued.
-      for (uint32_t k = it > uint32_t(kStages) ? it - kStages : 0; k < it; ++k)
-        if (!sm100::mbar_wait_bounded(&full[k % kStages], (k / kStages) & 1, a.wait_ns))
-          atomicOr(&g_status, kStatusDrain);
+      // (only possible after an abort): wait for each ring's last fills.
+#pragma unroll
+      for (int ring = 0; ring < C::kRings; ++ring) {
+        const uint32_t n = fills[ring];
+        for (uint32_t k = n > uint32_t(C::kRing) ? n - C::kRing : 0; k < n; ++k)
+          if (!sm100::mbar_wait_bounded(&full[ring * C::kRing + k % C::kRing], (k / C::kRing) & 1,
+                                        a.wait_ns))
+            atomicOr(&g_status, kStatusDrain);
+      }
     }
   } else if (warp <= 3) {
-    // ---- scale-factor copies and MMA issue (warps 1-3) ----
+    // ---- scale-factor copies and MMA issue (warps 1-2; warp 3 idles) ----
     // One thread issuing every tcgen05 copy and MMA caps a CTA at ~26 GB/s
     // (about 0.4 us per stage), so several warps issue: with two views each
-    // of warps 1-2 takes one (gate, up); with one view warps 1-3 take the
-    // stages in turn, each into its own accumulator, added by the epilogue.
+    // of warps 1-2 takes one (gate, up); with one view they take the chunks
+    // in turn (chunk i to warp i % kMma, staged in that warp's ring),
+    // each into its own accumulator, added by the epilogue.
     // The whole warp runs the loop (every lane waits on the barriers, so all
     // see the staged bytes); lane 0 issues the tensor-core instructions.
     const int m = warp - 1;
@@ -595,10 +622,13 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
         const int64_t r0 = a.row0[v] + item.n0;
         const bool has_next = (r0 >> 7) + 1 < (a.N[v] + 127) / 128;
         bool first = true;
-        for (int64_t i = lo; i < hi; ++i, ++it) {
-          if (NV == 1 && i % C::kMma != m) continue;   // another warp's stage
-          const int s = it % kStages;
-          if (!__all_sync(0xffffffffu, sm100::mbar_wait_bounded(&full[s], (it / kStages) & 1, a.wait_ns))) {
+        for (int64_t i = lo; i < hi; ++i) {
+          if (NV == 1 && i % C::kMma != m) continue;   // another warp's chunk
+          // This warp's ring (one view) or the shared ring (two views), in
+          // the order the producer fills it.
+          const uint32_t k = it++;
+          const int s = (NV == 1 ? m * C::kRing : 0) + int(k % C::kRing);
+          if (!__all_sync(0xffffffffu, sm100::mbar_wait_bounded(&full[s], (k / C::kRing) & 1, a.wait_ns))) {
             if (lane == 0) {
               atomicOr(&g_status, kStatusFull);
               *abort_v = 1;
@@ -776,16 +806,10 @@ __global__ void __launch_bounds__(Cfg<NV, W>::kThreads, W ? 1 : 2)
           if (NV == 2 || n_chunks > 1) sm100::tmem_ld_32cols(col + kN + gq * 32, du);
           sm100::tmem_ld_wait();
           if constexpr (NV == 1) {
-            // The MMA warps' accumulators (stages i % kMma = 0, 1, 2), added
-            // in that order; a warp that had no stage holds nothing.
+            // The MMA warps' accumulators (chunks i % kMma = 0, 1), added
+            // in that order; a warp that had no chunk holds nothing.
+            static_assert(C::kMma == 2, "one view: two accumulators");
             if (n_chunks > 1) {
-#pragma unroll
-              for (int c = 0; c < 32; ++c)
-                dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
-            }
-            if (C::kMma > 2 && n_chunks > 2) {
-              sm100::tmem_ld_32cols(col + 2 * kN + gq * 32, du);
-              sm100::tmem_ld_wait();
 #pragma unroll
               for (int c = 0; c < 32; ++c)
                 dg[c] = __float_as_uint(__uint_as_float(dg[c]) + __uint_as_float(du[c]));
@@ -1031,7 +1055,7 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
   for (int v = 0; v < 2; ++v) {
     const msb_pool_s *p = pools[nv == 2 ? v : 0];
     if (!p->has_tmap) return fail(MSB_ERR_UNSUPPORTED, "tensor-core path: pool has no tensor map");
-    a.tm_w[v] = wide ? p->tmap_w8 : p->tmap_w;
+    a.tm_w[v] = (wide || nv == 1) ? p->tmap_w8 : p->tmap_w;   // the config's kCh blocks
     a.pool[v] = p->data;
     a.slot_stride[v] = p->slot_stride;
     a.N[v] = p->N;
@@ -1073,7 +1097,8 @@ int tc_projection(const msb_pool_s *const *pools, int nv, const int64_t *row0, i
     // line (512 or 1536 contiguous bytes), five lines per chunk. Boxes land
     // as [chunk][4 blocks, scales][pair][term]: B rows 4p + t.
     const int pairs_per_pass = wide ? tc::Cfg<1, true>::kPairs : tc::Cfg<1, false>::kPairs;
-    const int chunks_per_stage = wide ? tc::Cfg<1, true>::kSfc : tc::Cfg<1, false>::kSfc;
+    const int chunks_per_stage = nv == 2 ? (wide ? tc::Cfg<2, true>::kSfc : tc::Cfg<2, false>::kSfc)
+                                         : (wide ? tc::Cfg<1, true>::kSfc : tc::Cfg<1, false>::kSfc);
     const uint64_t nc = uint64_t((pool->nb + 3) / 4);
     const uint64_t row_u64 = uint64_t(n_pairs) * tc::kTerms * 2;
     const uint64_t dq[3] = {row_u64, 5, nc};
